@@ -1,0 +1,392 @@
+"""Benchmark of the DWA retrieval hot path on B200.
+
+Workload (the op-at-scale configuration): queries [8192, 1024] bf16 ~N(0,1);
+pool keys [1,048,576, 1024] bf16 ~N(0, 1/1024) and values ~N(0,1) (2 GiB
+each, resident in HBM); top-k = 64, fp32 accumulate, softmax over the k
+scores (no gate), weighted sum of the gathered value rows -> [8192, 1024] f32.
+One step = one retrieval of all 8192 queries.  Inputs are synthetic (seeded
+counter-based generator on the device).
+
+Multi-GPU (torchrun, one process per GPU, NCCL): the same pool is row-sharded
+over the N ranks (strong scaling): each rank runs the fused score + top-k on
+its shard, the per-rank candidates are all-gathered over NVLink and merged on
+the device, each rank sums the value rows it owns and one all-reduce combines
+them.  Time = max over ranks of the CUDA-event step time.
+
+Reported: queries/s (value, device-resident inputs), e2e queries/s through the
+public API with pinned host buffers (H2D of queries + D2H of out/alpha/idx
+inside the timed region), the fused kernel's roofline fraction, the CPU
+baseline (NumPy restatement on the host cores, bounded sample), clocks.
+
+``--impl reference`` times the reference's CPU path restated in NumPy
+(oracle/dwa_oracle.py) on the host cores on a bounded sample of the same
+workload and prints the same JSON line with "impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    # name: (M queries, N pool rows, d, k, use_sigmoid)
+    "op_at_scale": dict(M=8192, N=1 << 20, d=1024, k=64, use_sigmoid=False,
+                        desc="queries [8192,1024] bf16 ~N(0,1); pool 1,048,576x1024 bf16 keys "
+                             "~N(0,1/1024), values ~N(0,1); top-k 64; softmax-weighted value sum"),
+    "c1_op": dict(M=2048, N=16384, d=128, k=16, use_sigmoid=False,
+                  desc="queries [2048,128]; pool [16384,128]; top-k 16; softmax-weighted sum"),
+}
+METRIC = "fused score+top-k retrieval queries/s"
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p["bf16_tflops"], p["bf16_tflops_sustained"], p["hbm_gbs"], "measured"
+    except Exception:
+        return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.out = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                self.out = ""
+        return False
+
+    def summary(self):
+        if not self.out:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- CPU legs
+def cpu_sample(keys_rows_fn, n_total, d, k, q_host, use_sigmoid, chunk_rows=131072):
+    """NumPy restatement of the reference path for the sampled queries against
+    the whole pool, streamed in chunks: scores, fused score, running top-k,
+    normalisation, gather + weighted sum.  Returns seconds spent on CPU work."""
+    import numpy as np
+
+    from oracle import dwa_oracle as O
+
+    t_cpu = 0.0
+    best_v = best_i = None
+    for r0 in range(0, n_total, chunk_rows):
+        kf = keys_rows_fn(r0, min(n_total, r0 + chunk_rows))  # float32 [rows, d], untimed fetch
+        t0 = time.perf_counter()
+        s = q_host @ kf.T
+        v = O.fused_score(s, 1.0, 0.0, 1.0, use_sigmoid)
+        tv, ti = O.top_k(v, k)
+        ti = ti + r0
+        if best_v is None:
+            best_v, best_i = tv, ti
+        else:
+            best_v, sel = O.top_k(np.concatenate([best_v, tv], 1), k)
+            best_i = np.take_along_axis(np.concatenate([best_i, ti], 1), sel, 1)
+        t_cpu += time.perf_counter() - t0
+    t0 = time.perf_counter()
+    alpha = O.normalise(best_v)
+    t_cpu += time.perf_counter() - t0
+    return t_cpu, alpha, best_i
+
+
+def run_reference(args, wl):
+    """--impl reference: NumPy restatement of the reference's CPU path, host cores."""
+    import numpy as np
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = len(os.sched_getaffinity(0))
+    M, N, d, k = wl["M"], wl["N"], wl["d"], wl["k"]
+    mq = args.cpu_queries
+    rng = np.random.default_rng(0)
+    t0 = time.perf_counter()
+    # pool generated once on the host (bf16-rounded float32), untimed
+    from oracle import dwa_oracle as O
+
+    chunk = 131072
+    keys = np.empty((N, d), dtype=np.float32)
+    values = np.empty((N, d), dtype=np.float32)
+    for r0 in range(0, N, chunk):
+        r1 = min(N, r0 + chunk)
+        keys[r0:r1] = O.bf16_round(rng.standard_normal((r1 - r0, d), dtype=np.float32)
+                                   / np.float32(np.sqrt(d)))
+        values[r0:r1] = O.bf16_round(rng.standard_normal((r1 - r0, d), dtype=np.float32))
+    gen_s = time.perf_counter() - t0
+    step_times = []
+    for step in range(args.warmup + args.steps):
+        q = O.bf16_round(rng.standard_normal((mq, d), dtype=np.float32))
+        t_cpu, alpha, idx = cpu_sample(lambda a, b: keys[a:b], N, d, k, q, wl["use_sigmoid"])
+        t0 = time.perf_counter()
+        O.weighted_sum(alpha, idx, values, accum=np.float32)
+        t_cpu += time.perf_counter() - t0
+        if step >= args.warmup:
+            step_times.append(t_cpu)
+    per_step = sum(step_times) / len(step_times)
+    qps = mq / per_step
+    line = {
+        "impl": "reference", "metric": METRIC, "value": qps, "unit": "queries/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32 (bf16-valued inputs)", "data": "synthetic",
+        "config": {"workload": args.workload, "M": M, "N": N, "d": d, "k": k,
+                   "desc": wl["desc"], "sample_queries_per_step": mq},
+        "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": threads, "kind": "port",
+                         "sample": f"{mq} queries per step against the full {N}-row pool "
+                                   f"(NumPy restatement of tiled_topk_fallback + normalise + "
+                                   f"gather-sum; pool generation {gen_s:.1f}s untimed)"},
+        "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def run_ours(args, wl):
+    import torch
+    import torch.distributed as dist
+
+    import computd_b200 as cb
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpus != world:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    group = None
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    cb.load_library()
+
+    M, N, d, k = wl["M"], wl["N"], wl["d"], wl["k"]
+    spec = cb.ShardSpec(N, rank, world)
+    keys = cb.new_normal(spec.n_local, d, seed=2, stddev=d ** -0.5, row_offset=spec.row_begin,
+                         device=dev)
+    values = cb.new_normal(spec.n_local, d, seed=3, stddev=1.0, row_offset=spec.row_begin,
+                           device=dev)
+    queries = [cb.new_normal(M, d, seed=100 + i, stddev=1.0, device=dev) for i in range(2)]
+    r = cb.Retriever(keys, values, M, k, use_sigmoid=wl["use_sigmoid"], group=group)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+
+    # ------------------------------------------------ device-resident timing
+    for i in range(args.warmup):
+        r(queries[i % 2])
+    barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local_rank) as clocks:
+        barrier()
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record()
+        for i in range(args.steps):
+            e0, e1, e2 = ev[i]
+            e0.record()
+            r.topk_local(queries[i % 2])     # fused kernel + split merge on this rank
+            e1.record()
+            r.finish()                       # exchange + merge + gather + reduce
+            e2.record()
+        t_end.record()
+        barrier()
+    status = r.status()
+    total_ms = t_start.elapsed_time(t_end)
+    topk_ms = [a.elapsed_time(b) for a, b, _ in ev]
+    t = torch.tensor([total_ms, sum(topk_ms) / len(topk_ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, topk_avg_ms = float(t[0]), float(t[1])
+    ms_per_step = total_ms / args.steps
+
+    # ------------------------------------------------ end to end (host buffers)
+    q_host = [queries[i].cpu().pin_memory() for i in range(2)]
+    out_host = torch.empty((M, d), dtype=torch.float32).pin_memory()
+    alpha_host = torch.empty((M, k), dtype=torch.float32).pin_memory()
+    idx_host = torch.empty((M, k), dtype=torch.int32).pin_memory()
+    q_dev = torch.empty_like(queries[0])
+
+    def e2e_step(i):
+        q_dev.copy_(q_host[i % 2], non_blocking=True)
+        out, alpha, tv, ti = r(q_dev)
+        out_host.copy_(out, non_blocking=True)
+        alpha_host.copy_(alpha, non_blocking=True)
+        idx_host.copy_(ti, non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    barrier()
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_end = torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for i in range(args.steps):
+        e2e_step(i)
+    e_end.record()
+    barrier()
+    te = torch.tensor([e_start.elapsed_time(e_end)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te[0]) / args.steps
+    h2d = q_host[0].numel() * q_host[0].element_size()
+    d2h = (out_host.numel() * 4 + alpha_host.numel() * 4 + idx_host.numel() * 4)
+
+    # ------------------------------------------------ roofline of the fused kernel
+    burst, sustained, hbm, peak_src = _peaks()
+    n_local = spec.n_local
+    flops = 2.0 * M * n_local * d
+    achieved_tflops = flops / (topk_avg_ms * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "achieved": achieved_tflops, "peak": burst,
+                "unit": "TFLOP/s", "frac": achieved_tflops / burst,
+                "frac_of_sustained": achieved_tflops / sustained,
+                "peak_source": f"{peak_src} bf16 dense burst (MEASURED_PEAKS.json)",
+                "kernel": "score_topk_kernel + split merge (dwa_score_topk)",
+                "flops_per_launch": flops, "ms_per_launch": topk_avg_ms,
+                "traffic": _ncu_traffic(args.workload, world)}
+
+    line = {
+        "metric": METRIC, "value": M / (ms_per_step * 1e-3), "unit": "queries/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16 in, f32 accumulate", "data": "synthetic",
+        "config": {"workload": args.workload, "M": M, "N": N, "d": d, "k": k,
+                   "n_local": n_local, "desc": wl["desc"],
+                   "parallelism": f"pool rows sharded x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (2 GiB keys + 2 GiB values)"},
+        "e2e": {"value": M / (e2e_ms * 1e-3), "unit": "queries/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+        "roofline": roofline,
+        "gpu_launches": r.kernels_per_call * args.steps,
+        "clocks": clocks.summary(),
+        "device_status": status,
+    }
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = _cpu_baseline(args, wl, keys, values, queries[0])
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def _ncu_traffic(workload, world):
+    """DRAM bytes per launch of the fused kernel from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", f"score_topk_{workload}.md")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch_full_size:") and world == 1:
+                    return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+def _cpu_baseline(args, wl, keys_dev, values_dev, q_dev):
+    import numpy as np
+    import torch
+
+    from oracle import dwa_oracle as O
+
+    threads = len(os.sched_getaffinity(0))
+    N, d, k = wl["N"], wl["d"], wl["k"]
+    mq = args.cpu_queries
+    q = q_dev[:mq].float().cpu().numpy()
+    cache = {}
+
+    def rows(a, b):
+        return keys_dev[a:b].float().cpu().numpy()
+
+    t_cpu, alpha, idx = cpu_sample(rows, N, d, k, q, wl["use_sigmoid"])
+    vals = values_dev[torch.from_numpy(idx.reshape(-1).astype(np.int64)).to(values_dev.device)]
+    vals = vals.float().cpu().numpy().reshape(mq, k, d)
+    t0 = time.perf_counter()
+    np.einsum("mk,mkd->md", alpha, vals)
+    t_cpu += time.perf_counter() - t0
+    return {"value": mq / t_cpu, "unit": "queries/s", "cores": threads, "kind": "port",
+            "sample": f"{mq} queries against the full {N}-row pool, NumPy restatement of the "
+                      f"reference jnp path (matmul, gate/exp, top_k, normalise, gather-sum), "
+                      f"{t_cpu:.2f}s of CPU work"}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="op_at_scale")
+    ap.add_argument("--cpu-queries", type=int, default=64,
+                    help="queries per CPU sample (CPU baseline / reference arm)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        return run_reference(args, wl)
+    return run_ours(args, wl)
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,203 @@
+// capi.cu — the exported C ABI (include/dwa_retrieval.h).
+//
+// Every entry point validates its arguments on the host before enqueueing
+// anything; a rejected call launches nothing and leaves a message in
+// dwa_last_error().  The reference raises Python exceptions at trace time for
+// the same conditions (e.g. lax.top_k with k > N); here they are status codes.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/dwa_retrieval.h"
+#include "dwa_internal.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+dwa_status fail(dwa_status s, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+dwa_status fail(dwa_status s, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return s;
+}
+
+dwa_status cuda_fail(cudaError_t e, const char* where, const char* detail = nullptr) {
+  return fail(DWA_ERR_CUDA, "%s: %s%s%s", where, cudaGetErrorString(e), detail ? " — " : "",
+              detail ? detail : "");
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+dwa_status ok() {
+  g_last_error.clear();
+  return DWA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t dwa_abi_version(void) { return DWA_ABI_VERSION; }
+
+const char* dwa_status_string(dwa_status s) {
+  switch (s) {
+    case DWA_OK: return "DWA_OK";
+    case DWA_ERR_INVALID_ARG: return "DWA_ERR_INVALID_ARG";
+    case DWA_ERR_UNSUPPORTED_SHAPE: return "DWA_ERR_UNSUPPORTED_SHAPE";
+    case DWA_ERR_CUDA: return "DWA_ERR_CUDA";
+    case DWA_ERR_TIMEOUT: return "DWA_ERR_TIMEOUT";
+    case DWA_ERR_DEVICE_CHECK: return "DWA_ERR_DEVICE_CHECK";
+    case DWA_ERR_WORKSPACE: return "DWA_ERR_WORKSPACE";
+    default: return "DWA_ERR_UNKNOWN";
+  }
+}
+
+const char* dwa_last_error(void) { return g_last_error.c_str(); }
+
+size_t dwa_score_topk_workspace(int64_t M, int64_t N_local, int32_t d, int32_t k) {
+  if (M <= 0 || N_local <= 0 || d <= 0 || k <= 0 || k > DWA_MAX_K) return 0;
+  dwa::ScoreTopkPlan plan;
+  if (!dwa::plan_score_topk(M, N_local, d, k, dwa::device_sm_count(), &plan)) return 0;
+  return plan.ws_bytes;
+}
+
+dwa_status dwa_score_topk(const void* q, int64_t M, int64_t ldq, const void* keys,
+                          int64_t N_local, int64_t ldk, int32_t d, int32_t k, float lambda_sharp,
+                          float tau, float T, int32_t use_sigmoid, int64_t idx_offset,
+                          float* out_vals, int32_t* out_idx, void* ws, size_t ws_bytes,
+                          dwa_stream_t stream) {
+  if (M < 0 || N_local < 0) return fail(DWA_ERR_INVALID_ARG, "negative size (M=%lld, N=%lld)",
+                                        (long long)M, (long long)N_local);
+  if (M == 0) return ok();
+  if (!q || !keys || !out_vals || !out_idx)
+    return fail(DWA_ERR_INVALID_ARG, "null queries/keys/output pointer");
+  if (N_local == 0) return fail(DWA_ERR_INVALID_ARG, "empty key shard (N_local = 0)");
+  if (k < 1 || k > N_local)
+    return fail(DWA_ERR_INVALID_ARG, "k=%d must satisfy 1 <= k <= N_local=%lld", k,
+                (long long)N_local);
+  if (k > DWA_MAX_K)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "k=%d exceeds DWA_MAX_K=%d", k, DWA_MAX_K);
+  if (d < 8 || d % 8 != 0)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "d=%d must be a positive multiple of 8", d);
+  if (ldq < d || ldk < d)
+    return fail(DWA_ERR_INVALID_ARG, "row stride below d (ldq=%lld, ldk=%lld, d=%d)",
+                (long long)ldq, (long long)ldk, d);
+  if (ldq % 8 != 0 || ldk % 8 != 0)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "row strides must be multiples of 8 elements");
+  if (!aligned(q, 16) || !aligned(keys, 16))
+    return fail(DWA_ERR_INVALID_ARG, "queries and keys must be 16-byte aligned");
+  if (M > INT32_MAX || N_local > INT32_MAX)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "M and N_local must be < 2^31");
+  if (idx_offset < 0 || N_local + idx_offset > INT32_MAX)
+    return fail(DWA_ERR_INVALID_ARG, "idx_offset=%lld out of the int32 index range",
+                (long long)idx_offset);
+  if (!(T > 0.f) || !std::isfinite(T))
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "temperature T must be finite and > 0");
+  if (use_sigmoid && (!(lambda_sharp >= 0.f) || !std::isfinite(lambda_sharp) ||
+                      !std::isfinite(tau)))
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE,
+                "the gate needs finite lambda_sharp >= 0 and finite tau (selection on raw "
+                "scores requires a monotone gate)");
+  dwa::ScoreTopkPlan plan;
+  if (!dwa::plan_score_topk(M, N_local, d, k, dwa::device_sm_count(), &plan))
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "no launch plan for this shape");
+  if (!ws || !aligned(ws, 256))
+    return fail(DWA_ERR_WORKSPACE, "workspace must be non-null and 256-byte aligned");
+  if (ws_bytes < plan.ws_bytes)
+    return fail(DWA_ERR_WORKSPACE, "workspace too small: %zu < %zu bytes", ws_bytes,
+                plan.ws_bytes);
+  const char* detail = nullptr;
+  cudaError_t e = dwa::launch_score_topk(plan, q, ldq, keys, ldk, lambda_sharp, tau, T,
+                                         use_sigmoid ? 1 : 0, idx_offset, out_vals, out_idx, ws,
+                                         static_cast<cudaStream_t>(stream), &detail);
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_score_topk launch", detail);
+  return ok();
+}
+
+dwa_status dwa_merge_topk(const float* cand_vals, const int32_t* cand_idx, int32_t P, int64_t M,
+                          int32_t k, float* out_vals, int32_t* out_idx, dwa_stream_t stream) {
+  if (M < 0) return fail(DWA_ERR_INVALID_ARG, "negative M");
+  if (M == 0) return ok();
+  if (!cand_vals || !cand_idx || !out_vals || !out_idx)
+    return fail(DWA_ERR_INVALID_ARG, "null pointer");
+  if (P < 1) return fail(DWA_ERR_INVALID_ARG, "P=%d must be >= 1", P);
+  if (k < 1) return fail(DWA_ERR_INVALID_ARG, "k=%d must be >= 1", k);
+  if (k > DWA_MAX_K)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "k=%d exceeds DWA_MAX_K=%d", k, DWA_MAX_K);
+  if (static_cast<const void*>(out_vals) == static_cast<const void*>(cand_vals) ||
+      static_cast<const void*>(out_idx) == static_cast<const void*>(cand_idx))
+    return fail(DWA_ERR_INVALID_ARG, "outputs must not alias the candidate lists");
+  cudaError_t e = dwa::launch_merge_topk(
+      cand_vals, cand_idx, P, k, M * static_cast<int64_t>(k), 1, k, M, k, /*transform=*/0, 0.f,
+      0.f, 1.f, 0, /*idx_offset=*/0, out_vals, out_idx, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_merge_topk launch");
+  return ok();
+}
+
+dwa_status dwa_weighted_gather(const float* vals, const int32_t* gidx, int64_t M, int32_t k,
+                               const void* values, int64_t row_begin, int64_t row_end,
+                               int64_t ldv, int32_t d, float* out, float* alpha_out,
+                               dwa_stream_t stream) {
+  if (M < 0) return fail(DWA_ERR_INVALID_ARG, "negative M");
+  if (M == 0) return ok();
+  if (!vals || !gidx || !out) return fail(DWA_ERR_INVALID_ARG, "null vals/gidx/out pointer");
+  if (k < 1) return fail(DWA_ERR_INVALID_ARG, "k=%d must be >= 1", k);
+  if (k > DWA_MAX_K)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "k=%d exceeds DWA_MAX_K=%d", k, DWA_MAX_K);
+  if (d < 8 || d % 8 != 0)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "d=%d must be a positive multiple of 8", d);
+  if (row_begin < 0 || row_end < row_begin || row_end > INT32_MAX)
+    return fail(DWA_ERR_INVALID_ARG, "bad owned row range [%lld, %lld)", (long long)row_begin,
+                (long long)row_end);
+  if (row_end > row_begin) {
+    if (!values) return fail(DWA_ERR_INVALID_ARG, "null values with a non-empty row range");
+    if (ldv < d) return fail(DWA_ERR_INVALID_ARG, "ldv=%lld below d=%d", (long long)ldv, d);
+    if (ldv % 8 != 0)
+      return fail(DWA_ERR_UNSUPPORTED_SHAPE, "ldv must be a multiple of 8 elements");
+    if (!aligned(values, 16))
+      return fail(DWA_ERR_INVALID_ARG, "values must be 16-byte aligned");
+  }
+  if (!aligned(out, 16)) return fail(DWA_ERR_INVALID_ARG, "out must be 16-byte aligned");
+  cudaError_t e = dwa::launch_weighted_gather(vals, gidx, M, k, values, row_begin, row_end, ldv, d,
+                                              out, alpha_out, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_weighted_gather launch");
+  return ok();
+}
+
+dwa_status dwa_pool_init_normal(void* out, int64_t rows, int64_t cols, int64_t ld,
+                                int64_t row_offset, uint64_t seed, float stddev,
+                                dwa_stream_t stream) {
+  if (rows < 0 || cols < 0 || row_offset < 0)
+    return fail(DWA_ERR_INVALID_ARG, "negative rows/cols/row_offset");
+  if (rows == 0 || cols == 0) return ok();
+  if (!out) return fail(DWA_ERR_INVALID_ARG, "null output");
+  if (ld < cols) return fail(DWA_ERR_INVALID_ARG, "ld below cols");
+  if (!aligned(out, 2)) return fail(DWA_ERR_INVALID_ARG, "output must be 2-byte aligned");
+  if (!std::isfinite(stddev)) return fail(DWA_ERR_INVALID_ARG, "stddev must be finite");
+  cudaError_t e = dwa::launch_pool_init_normal(out, rows, cols, ld, row_offset, seed, stddev,
+                                               static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_pool_init_normal launch");
+  return ok();
+}
+
+dwa_status dwa_workspace_status(const void* ws, dwa_stream_t stream, int32_t* out_status) {
+  if (!ws || !out_status) return fail(DWA_ERR_INVALID_ARG, "null workspace or output");
+  int32_t v = 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(&v, ws, sizeof(v), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_workspace_status");
+  *out_status = v;
+  return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,66 @@
+// dwa_internal.h — launch plans and launchers shared by the kernel files and
+// the C ABI (capi.cu).  Nothing here is exported from the shared library.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace dwa {
+
+// Tile shape of the fused score + top-k kernel (one CTA, cta_group::1).
+constexpr int kTileM = 128;   // query rows per tile  (UMMA M, TMEM lanes)
+constexpr int kTileN = 256;   // pool keys per tile   (UMMA N, TMEM columns)
+constexpr int kTileK = 64;    // bf16 elements per 128-byte swizzled row
+constexpr size_t kStatusBytes = 256;  // status word block at the head of the workspace
+
+// How one dwa_score_topk call is cut into work units.
+// A unit is (query tile, contiguous range of key tiles); each unit leaves one
+// partial top-k list per query row in the workspace, merged afterwards.
+struct ScoreTopkPlan {
+  int64_t M = 0, N = 0;
+  int d = 0, k = 0;
+  int n_qt = 0;        // query tiles  = ceil(M / 128)
+  int64_t n_kt = 0;    // key tiles    = ceil(N / 256)
+  int n_split = 0;     // key-range splits per query tile
+  int num_kb = 0;      // k-blocks of 64 along d
+  int kcap = 0;        // heap capacity variant (16, 32, 64, 128)
+  int64_t m_pad = 0;   // n_qt * 128
+  size_t ws_bytes = 0; // status block + partial lists
+};
+
+// Returns false when the shape is outside what the kernel supports.
+bool plan_score_topk(int64_t M, int64_t N, int d, int k, int num_sms, ScoreTopkPlan* plan);
+
+// Number of SMs of the current device (cached per device).
+int device_sm_count();
+
+// Launches the fused kernel + split merge.  Arguments were validated by the caller.
+cudaError_t launch_score_topk(const ScoreTopkPlan& plan, const void* q, int64_t ldq,
+                              const void* keys, int64_t ldk, float lambda_sharp, float tau,
+                              float T, int use_sigmoid, int64_t idx_offset, float* out_vals,
+                              int32_t* out_idx, void* ws, cudaStream_t stream,
+                              const char** err_detail);
+
+// Generic candidate merge.  Candidate (list l, position p, row r) lives at
+// offset l*stride_list + p*stride_pos + r*stride_row.  When `transform` is
+// set, candidate scores are raw dot products s and the output holds
+// v(s) = [sigmoid(lambda (s - tau))] * exp(s / T); otherwise the scores are
+// copied.  Indices get `idx_offset` added.
+cudaError_t launch_merge_topk(const float* cand_vals, const int32_t* cand_idx, int n_lists,
+                              int k_in, int64_t stride_list, int64_t stride_pos,
+                              int64_t stride_row, int64_t M, int k, int transform,
+                              float lambda_sharp, float tau, float T, int use_sigmoid,
+                              int64_t idx_offset, float* out_vals, int32_t* out_idx,
+                              cudaStream_t stream);
+
+cudaError_t launch_weighted_gather(const float* vals, const int32_t* gidx, int64_t M, int k,
+                                   const void* values, int64_t row_begin, int64_t row_end,
+                                   int64_t ldv, int d, float* out, float* alpha_out,
+                                   cudaStream_t stream);
+
+cudaError_t launch_pool_init_normal(void* out, int64_t rows, int64_t cols, int64_t ld,
+                                    int64_t row_offset, uint64_t seed, float stddev,
+                                    cudaStream_t stream);
+
+}  // namespace dwa

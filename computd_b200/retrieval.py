@@ -1,0 +1,198 @@
+"""Pool-parallel retrieval: local fused top-k, all-gather, merge, owner-computes value sum.
+
+Mirrors the reference's multi-chip retrieval, ``MultiAspectRetrieval.pallas_hybrid_forward``
+(src/model/retrieval.py:204-343) and its ``shard_map`` body ``_chip_topk``
+(retrieval.py:285-303):
+
+    tv, li     = tiled_topk_fallback(q, keys_local, k, lambda, tau, T, use_sigmoid)
+    gidx       = li + axis_index * N_local                        (292-293)
+    cand_v/i   = all_gather(tv / gidx)  -> [P, BT, k]             (295-296)
+    fv, fi     = top_k over the P*k candidates per row            (299-302)
+    alpha      = fv / (sum(fv) + 1e-8)                            (326)
+
+On B200 the ``shard_map`` becomes one process per GPU (torch.distributed over
+NCCL): queries are replicated, rank r holds pool rows [r*N/P, (r+1)*N/P) in
+HBM, the candidate exchange is one NCCL all-gather per array over NVLink, and
+the merge runs on the device.  The value side (assembly.py:104-128) sums only
+owned rows per rank and adds the partial sums with one all-reduce.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .assembly import _check_values, weighted_gather_into
+from .pool import ShardSpec
+from .tiled_topk import (_as_bf16_rows, _stream_handle, merge_topk, score_topk_into,
+                         tiled_topk_fused, workspace_bytes)
+
+
+def _group_rank_world(group) -> tuple[int, int]:
+    if group is None and not (dist.is_available() and dist.is_initialized()):
+        return 0, 1
+    return dist.get_rank(group), dist.get_world_size(group)
+
+
+def exchange_candidates(local_vals: torch.Tensor, local_idx: torch.Tensor, group=None,
+                        out_vals: torch.Tensor | None = None, out_idx: torch.Tensor | None = None
+                        ) -> tuple[torch.Tensor, torch.Tensor]:
+    """All-gather each rank's [M, k] candidates into [P, M, k] (reference retrieval.py:295-296).
+
+    Same collective order on every rank.  NCCL gathers straight into the
+    stacked buffer; other backends (gloo, used by the CPU tests) use list
+    all_gather.
+    """
+    _, world = _group_rank_world(group)
+    M, k = local_vals.shape
+    if out_vals is None:
+        out_vals = torch.empty((world, M, k), dtype=local_vals.dtype, device=local_vals.device)
+    if out_idx is None:
+        out_idx = torch.empty((world, M, k), dtype=local_idx.dtype, device=local_idx.device)
+    if world == 1:
+        out_vals[0].copy_(local_vals)
+        out_idx[0].copy_(local_idx)
+        return out_vals, out_idx
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out_vals, local_vals.contiguous(), group=group)
+        dist.all_gather_into_tensor(out_idx, local_idx.contiguous(), group=group)
+    else:
+        dist.all_gather(list(out_vals.unbind(0)), local_vals.contiguous(), group=group)
+        dist.all_gather(list(out_idx.unbind(0)), local_idx.contiguous(), group=group)
+    return out_vals, out_idx
+
+
+def reduce_partials(out: torch.Tensor, group=None) -> torch.Tensor:
+    """Sum the owner-computes partial value sums over ranks (in place)."""
+    _, world = _group_rank_world(group)
+    if world > 1:
+        dist.all_reduce(out, op=dist.ReduceOp.SUM, group=group)
+    return out
+
+
+def chip_topk(queries_flat: torch.Tensor, keys_local: torch.Tensor, k_max: int, lambda_sharp, tau,
+              T, use_sigmoid: bool, group=None) -> tuple[torch.Tensor, torch.Tensor]:
+    """The per-rank body of the reference's shard_map (retrieval.py:285-303).
+
+    Returns the global top-k (fused scores f32, global indices i32), identical
+    on every rank of ``group``.
+    """
+    rank, world = _group_rank_world(group)
+    n_local = keys_local.shape[0]
+    tv, gi = tiled_topk_fused(queries_flat, keys_local, k_max, lambda_sharp, tau, T, use_sigmoid,
+                              idx_offset=rank * n_local)
+    if world == 1:
+        return tv, gi
+    cand_v, cand_i = exchange_candidates(tv, gi, group)
+    return merge_topk(cand_v, cand_i)
+
+
+class Retriever:
+    """Pre-planned retrieval over a resident (possibly row-sharded) pool.
+
+    Owns its outputs and workspace so that repeated calls allocate nothing and
+    enqueue only kernels and collectives.  One call computes, for queries
+    [M, d_k]:
+
+        top_vals, top_idx = global top-k of v(q . key) (fused scores, global rows)
+        alpha             = top_vals / (sum + 1e-8)
+        out               = sum_j alpha[:, j] * values[top_idx[:, j]]   (f32 [M, d_v])
+
+    ``keys_local`` / ``values_local`` are this rank's rows [row_begin, row_end)
+    of the pool (the whole pool when ``group`` is None or has one rank).
+    """
+
+    def __init__(self, keys_local: torch.Tensor, values_local: torch.Tensor, M: int, k: int, *,
+                 lambda_sharp: float = 1.0, tau: float = 0.0, T: float = 1.0,
+                 use_sigmoid: bool = False, group=None):
+        self.keys = _as_bf16_rows(keys_local, "keys_local")
+        self.values = _check_values(values_local)
+        if self.values.shape[0] != self.keys.shape[0]:
+            raise ValueError("keys_local and values_local must hold the same pool rows")
+        self.group = group
+        self.rank, self.world = _group_rank_world(group)
+        self.n_local = self.keys.shape[0]
+        self.shard = ShardSpec(self.n_local * self.world, self.rank, self.world)
+        self.M, self.k = int(M), int(k)
+        self.d_k = self.keys.shape[1]
+        self.d_v = self.values.shape[1]
+        self.lambda_sharp, self.tau, self.T = float(lambda_sharp), float(tau), float(T)
+        self.use_sigmoid = bool(use_sigmoid)
+        dev = self.keys.device
+        self.device = dev
+        f32, i32 = torch.float32, torch.int32
+        self.local_vals = torch.empty((self.M, self.k), dtype=f32, device=dev)
+        self.local_idx = torch.empty((self.M, self.k), dtype=i32, device=dev)
+        if self.world > 1:
+            self.cand_vals = torch.empty((self.world, self.M, self.k), dtype=f32, device=dev)
+            self.cand_idx = torch.empty((self.world, self.M, self.k), dtype=i32, device=dev)
+            self.top_vals = torch.empty((self.M, self.k), dtype=f32, device=dev)
+            self.top_idx = torch.empty((self.M, self.k), dtype=i32, device=dev)
+        else:
+            self.top_vals, self.top_idx = self.local_vals, self.local_idx
+        self.alpha = torch.empty((self.M, self.k), dtype=f32, device=dev)
+        self.out = torch.empty((self.M, self.d_v), dtype=f32, device=dev)
+        nbytes = workspace_bytes(self.M, self.n_local, self.d_k, self.k, dev)
+        if nbytes == 0:
+            raise _lib.DWAArgumentError(_lib.DWA_ERR_UNSUPPORTED_SHAPE, "Retriever",
+                                        "no workspace plan for this shape")
+        self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+
+    @property
+    def kernels_per_call(self) -> int:
+        """Kernels of this library one full call launches (NCCL kernels not counted):
+        fused score + top-k, split merge, [cross-shard merge,] weighted gather."""
+        return 3 if self.world == 1 else 4
+
+    def topk_local(self, queries: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """This rank's shard only: fused score + top-k and the split merge
+        (global indices), into ``local_vals`` / ``local_idx``."""
+        if tuple(queries.shape) != (self.M, self.d_k):
+            raise ValueError(f"queries must be [{self.M}, {self.d_k}], got {tuple(queries.shape)}")
+        score_topk_into(queries, self.keys, self.k, self.lambda_sharp, self.tau, self.T,
+                        self.use_sigmoid, self.local_vals, self.local_idx, self.workspace,
+                        idx_offset=self.shard.row_begin)
+        return self.local_vals, self.local_idx
+
+    def _merge_shards(self) -> None:
+        if self.world == 1:
+            return
+        exchange_candidates(self.local_vals, self.local_idx, self.group, self.cand_vals,
+                            self.cand_idx)
+        lib = _lib.load()
+        with torch.cuda.device(self.device):
+            st = lib.dwa_merge_topk(self.cand_vals.data_ptr(), self.cand_idx.data_ptr(),
+                                    self.world, self.M, self.k, self.top_vals.data_ptr(),
+                                    self.top_idx.data_ptr(), _stream_handle(self.device))
+        _lib.check(st, "dwa_merge_topk")
+
+    def topk(self, queries: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """Global top-k only (fused scores f32, global indices i32), same on every rank."""
+        self.topk_local(queries)
+        self._merge_shards()
+        return self.top_vals, self.top_idx
+
+    def finish(self):
+        """After ``topk_local``: cross-shard merge, alpha, owner-computes weighted
+        sum and the all-reduce of the partial sums."""
+        self._merge_shards()
+        weighted_gather_into(self.top_vals, self.top_idx, self.values, self.out, self.alpha,
+                             self.shard.row_begin, self.shard.row_end)
+        reduce_partials(self.out, self.group)
+        return self.out, self.alpha, self.top_vals, self.top_idx
+
+    def __call__(self, queries: torch.Tensor):
+        """Returns (out f32 [M, d_v], alpha f32 [M, k], top_vals f32 [M, k], top_idx i32 [M, k])."""
+        self.topk_local(queries)
+        return self.finish()
+
+    def status(self) -> int:
+        """Device status word the fused kernel left in the workspace (syncs the stream)."""
+        import ctypes
+        lib = _lib.load()
+        v = ctypes.c_int32(0)
+        with torch.cuda.device(self.device):
+            st = lib.dwa_workspace_status(self.workspace.data_ptr(), _stream_handle(self.device),
+                                          ctypes.byref(v))
+        _lib.check(st, "dwa_workspace_status")
+        return int(v.value)

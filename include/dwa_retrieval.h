@@ -1,0 +1,156 @@
+/*
+ * dwa_retrieval.h — C ABI of the B200 (sm_100a) DWA retrieval hot path.
+ *
+ * The reference (computd, JAX) runs this path as:
+ *   src/kernels/tiled_topk.py:160-176  tiled_topk_fallback: s = q.k^T, gate/exp, lax.top_k
+ *   src/kernels/tiled_topk.py:86-153   tiled_topk_fused (same contract, Pallas/TPU, uncalled)
+ *   src/model/retrieval.py:285-303     _chip_topk: global index offset, all_gather, merge top_k
+ *   src/model/retrieval.py:324-326     alpha = v / (sum(v) + 1e-8)
+ *   src/model/assembly.py:104,123-128  vectors[idx] gather and the alpha-weighted sum
+ *
+ * Every entry point is stream-ordered and asynchronous: it validates its
+ * arguments on the host, returns a non-zero status WITHOUT launching anything
+ * when they are invalid, and otherwise enqueues kernels on `stream`.
+ * The library never allocates device memory: buffers and workspace belong to
+ * the caller.  All device pointers are plain CUDA device addresses.
+ *
+ * Element types: "bf16" buffers hold IEEE bfloat16 (uint16 bit patterns);
+ * scores and outputs are fp32; indices are int32.
+ */
+#ifndef DWA_RETRIEVAL_H_
+#define DWA_RETRIEVAL_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define DWA_API __attribute__((visibility("default")))
+#else
+#define DWA_API
+#endif
+
+/* Opaque CUDA stream handle (cudaStream_t / CUstream). NULL = legacy default stream. */
+typedef void* dwa_stream_t;
+
+typedef int32_t dwa_status;
+enum {
+  DWA_OK = 0,
+  DWA_ERR_INVALID_ARG = 1,       /* null pointer, negative size, k > N, misaligned buffer   */
+  DWA_ERR_UNSUPPORTED_SHAPE = 2, /* k > DWA_MAX_K, d % 8 != 0, lambda < 0, T <= 0, ...       */
+  DWA_ERR_CUDA = 3,              /* a CUDA runtime/driver call failed (message has details) */
+  DWA_ERR_TIMEOUT = 4,           /* a bounded device-side wait gave up (kernel returned)    */
+  DWA_ERR_DEVICE_CHECK = 5,      /* a device-side argument check failed                     */
+  DWA_ERR_WORKSPACE = 6          /* workspace pointer null/misaligned or too small          */
+};
+
+/* Largest top-k the fused score kernel keeps per query (its per-row heap
+ * lives in shared memory: 128 rows x k x 8 bytes). */
+#define DWA_MAX_K 128
+#define DWA_ABI_VERSION 1
+
+DWA_API int32_t dwa_abi_version(void);
+
+/* Human-readable name of a status code (static storage). */
+DWA_API const char* dwa_status_string(dwa_status s);
+
+/* Detail of the last failing call on this host thread (thread-local storage). */
+DWA_API const char* dwa_last_error(void);
+
+/* Bytes of device workspace dwa_score_topk needs for this shape on the current
+ * device (0 when the shape is invalid). */
+DWA_API size_t dwa_score_topk_workspace(int64_t M, int64_t N_local, int32_t d, int32_t k);
+
+/*
+ * Fused score GEMM + streaming top-k over one pool shard.
+ * Replaces tiled_topk_fallback / tiled_topk_fused (src/kernels/tiled_topk.py:160-176,
+ * :86-153) plus the per-chip global offset of _chip_topk (src/model/retrieval.py:292-293).
+ *
+ *   s[m, n]  = sum_d q[m, d] * keys[n, d]        (bf16 x bf16, fp32 accumulate, tcgen05)
+ *   v(s)     = sigmoid(lambda_sharp * (s - tau)) * exp(s / T)   if use_sigmoid
+ *            = exp(s / T)                                       otherwise
+ *   out_vals[m, j], out_idx[m, j] = top-k of v over n, sorted by v descending,
+ *            equal v ordered by lower index first (the lax.top_k contract);
+ *            out_idx = n + idx_offset (int32 global pool row).
+ *
+ * v is strictly increasing in s for lambda_sharp >= 0 and T > 0, so selection
+ * runs on s and v is evaluated for the k survivors only; other parameters
+ * return DWA_ERR_UNSUPPORTED_SHAPE.  The [M, N_local] score matrix never
+ * reaches device memory.
+ *
+ * q: bf16 [M, ldq] (row stride ldq elements), keys: bf16 [N_local, ldk].
+ * Requirements: d % 8 == 0, ldq % 8 == 0, ldk % 8 == 0, 16-byte aligned bases,
+ * 1 <= k <= min(DWA_MAX_K, N_local), N_local + idx_offset <= INT32_MAX.
+ * out_vals f32 [M, k], out_idx i32 [M, k] (dense row-major).
+ * ws: >= dwa_score_topk_workspace(M, N_local, d, k) bytes, 256-byte aligned.
+ */
+DWA_API dwa_status dwa_score_topk(const void* q, int64_t M, int64_t ldq,
+                          const void* keys, int64_t N_local, int64_t ldk,
+                          int32_t d, int32_t k,
+                          float lambda_sharp, float tau, float T, int32_t use_sigmoid,
+                          int64_t idx_offset,
+                          float* out_vals, int32_t* out_idx,
+                          void* ws, size_t ws_bytes, dwa_stream_t stream);
+
+/*
+ * Merge P per-shard candidate lists into the global top-k.
+ * Replaces the all_gather transpose/reshape + second top_k + take of
+ * _chip_topk (src/model/retrieval.py:295-302).
+ *
+ * cand_vals f32 / cand_idx i32: [P, M, k] (the all-gather output, list p from
+ * shard p).  Output: the k best of the P*k candidates per row, by v descending
+ * and lower global index first among equal v.  out_* are [M, k]; they must not
+ * alias the inputs.
+ */
+DWA_API dwa_status dwa_merge_topk(const float* cand_vals, const int32_t* cand_idx,
+                          int32_t P, int64_t M, int32_t k,
+                          float* out_vals, int32_t* out_idx, dwa_stream_t stream);
+
+/*
+ * Alpha normalisation + gathered-value weighted sum (owner-computes form).
+ * Replaces retrieval.py:326 (alpha = v / (sum v + 1e-8)) and the gather +
+ * alpha-weighted sum of WeightAssembler (src/model/assembly.py:104,127):
+ *
+ *   alpha[m, j] = vals[m, j] / (sum_j vals[m, j] + 1e-8)
+ *   out[m, :]   = sum_{j : row_begin <= gidx[m,j] < row_end} alpha[m, j] * values[gidx[m,j] - row_begin, :]
+ *
+ * values: bf16 rows [row_end - row_begin, ldv] holding global pool rows
+ * [row_begin, row_end) (the caller's shard; the whole pool on one GPU).
+ * out f32 [M, d] is overwritten (rows owned elsewhere contribute zero, so the
+ * partial sums of all shards add up to the full result).  alpha_out f32 [M, k]
+ * may be NULL.  Requirements: d % 8 == 0, ldv % 8 == 0, 16-byte aligned values.
+ */
+DWA_API dwa_status dwa_weighted_gather(const float* vals, const int32_t* gidx,
+                               int64_t M, int32_t k,
+                               const void* values, int64_t row_begin, int64_t row_end,
+                               int64_t ldv, int32_t d,
+                               float* out, float* alpha_out, dwa_stream_t stream);
+
+/*
+ * Deterministic pool / query initialisation: element (r, c) of a logical
+ * [rows_total, cols] matrix is  stddev * N(0,1)  drawn from Philox4x32-10
+ * keyed by (seed, row_offset + r, c), rounded to bf16.  A shard
+ * [row_offset, row_offset + rows) is therefore identical whichever rank or
+ * shard count produces it.  Counterpart of VectorPool's per-shard init
+ * (src/model/pool.py:19-40; jax.random.normal per shard with fold_in).
+ * out: bf16 [rows, ld], ld % 8 == 0.
+ */
+DWA_API dwa_status dwa_pool_init_normal(void* out, int64_t rows, int64_t cols, int64_t ld,
+                                int64_t row_offset, uint64_t seed, float stddev,
+                                dwa_stream_t stream);
+
+/*
+ * Device-side status word of a workspace: DWA_OK, or the first error a
+ * kernel recorded there (DWA_ERR_TIMEOUT from a bounded wait).  Copies 4
+ * bytes device->host on `stream` and synchronises that stream.
+ */
+DWA_API dwa_status dwa_workspace_status(const void* ws, dwa_stream_t stream, int32_t* out_status);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* DWA_RETRIEVAL_H_ */

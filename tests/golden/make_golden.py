@@ -1,0 +1,156 @@
+"""Generate tests/golden/dwa_golden.npz by executing the reference's own code.
+
+The reference (computd) is JAX; JAX is not installable here, so its modules
+are imported over ``jax_standin`` (NumPy restatements of jnp.dot, lax.top_k,
+all_gather, shard_map, ...).  What runs is the reference's own source:
+
+* ``src/kernels/tiled_topk.py``  ``tiled_topk_fallback``            (lines 160-176)
+* ``src/model/retrieval.py``     ``MultiAspectRetrieval.pallas_hybrid_forward``
+                                  with a 4-device ``shard_map``         (lines 204-343)
+* ``src/model/assembly.py``      ``WeightAssembler.assemble``        (lines 47-73)
+
+Inputs are float32 arrays holding bf16-representable values (the B200 kernel
+takes bf16, so both sides see identical inputs).  Run from the repository
+root:  ``python tests/golden/make_golden.py [--reference PATH]``.
+The reference tree is read only; nothing from it is copied into the fixture
+except the computed outputs.
+"""
+from __future__ import annotations
+
+import argparse
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE))
+sys.path.insert(0, str(HERE.parents[1]))
+
+import jax_standin  # noqa: E402
+from oracle.dwa_oracle import bf16_bits, bf16_round  # noqa: E402
+
+
+def _bits(x):
+    return bf16_bits(x)
+
+
+def case_tiled_topk(ref_tk, name, rng, M, N, d, k, lam, tau, T, use_sigmoid, out, q_scale=1.0,
+                    k_scale=None):
+    """tiled_topk_fallback on C1-distributed inputs (q ~ N(0,1), keys ~ N(0,1/d))."""
+    k_scale = (1.0 / np.sqrt(d)) if k_scale is None else k_scale
+    q = bf16_round(rng.standard_normal((M, d), dtype=np.float32) * q_scale)
+    keys = bf16_round(rng.standard_normal((N, d), dtype=np.float32) * np.float32(k_scale))
+    vals, idx = ref_tk.tiled_topk_fallback(q, keys, k, np.float32(lam), np.float32(tau),
+                                           np.float32(T), use_sigmoid)
+    out[f"{name}/q"] = _bits(q)
+    out[f"{name}/keys"] = _bits(keys)
+    out[f"{name}/params"] = np.array([k, lam, tau, T, float(use_sigmoid)], dtype=np.float64)
+    out[f"{name}/vals"] = np.asarray(vals, np.float32)
+    out[f"{name}/idx"] = np.asarray(idx, np.int32)
+
+
+def case_ties(ref_tk, rng, out):
+    """Exact score ties: small-integer inputs make every dot product exact in fp32,
+    and duplicated key rows tie; lax.top_k must put the lower index first."""
+    M, N, d, k = 64, 600, 64, 12
+    q = rng.integers(-2, 3, size=(M, d)).astype(np.float32) * np.float32(0.25)
+    base = rng.integers(-2, 3, size=(N // 4, d)).astype(np.float32) * np.float32(0.25)
+    keys = np.concatenate([base, base[::-1], base, base[::2], base[1::2]], axis=0)[:N]
+    perm = rng.permutation(N)
+    keys = np.ascontiguousarray(keys[perm])
+    vals, idx = ref_tk.tiled_topk_fallback(q, keys, k, np.float32(1.0), np.float32(0.0),
+                                           np.float32(8.0), False)
+    out["ties/q"] = _bits(q)
+    out["ties/keys"] = _bits(keys)
+    out["ties/params"] = np.array([k, 1.0, 0.0, 8.0, 0.0], dtype=np.float64)
+    out["ties/vals"] = np.asarray(vals, np.float32)
+    out["ties/idx"] = np.asarray(idx, np.int32)
+
+
+def case_sharded(ref_tk, ref_ret, ref_asm, rng, out, n_chips=4):
+    """pallas_hybrid_forward over a 4-device mesh + WeightAssembler.assemble."""
+    B, seq, d_A, S, d_k, k = 2, 48, 32, 2, 32, 8
+    d_B, r = 8, 2
+    N = n_chips * 250
+    D = d_B * r + r * d_A + d_B  # 88: U, V and b blocks of each pool vector
+    lam, T, use_sigmoid = 5.0, 0.8, True
+
+    recorded = {"q": None, "keys": [None] * n_chips, "local": [None] * n_chips}
+    orig = ref_tk.tiled_topk_fallback
+
+    def recording_fallback(queries, keys, k_max, lambda_sharp, tau, T_, use_sig):
+        # bf16 inputs, as the B200 kernel receives them
+        qb = bf16_round(np.asarray(queries, np.float32))
+        kb = bf16_round(np.asarray(keys, np.float32))
+        chip = int(jax_standin._ctx.index)
+        recorded["q"] = qb
+        recorded["keys"][chip] = kb
+        recorded["tau"] = float(tau)
+        res = orig(qb, kb, k_max, lambda_sharp, tau, T_, use_sig)
+        recorded["local"][chip] = res
+        return res
+
+    ref_tk.tiled_topk_fallback = recording_fallback
+    try:
+        self = types.SimpleNamespace()
+        self.S, self.d_k, self.N = S, d_k, N
+        self.W_Q = types.SimpleNamespace(value=(rng.standard_normal((S, d_k, d_A)) * d_A ** -0.5).astype(np.float32))
+        self.W_K = types.SimpleNamespace(value=(rng.standard_normal((S, d_k, D)) * D ** -0.5).astype(np.float32))
+        self.aspect_logits = types.SimpleNamespace(value=rng.standard_normal(S).astype(np.float32))
+        self.tau = types.SimpleNamespace(value=(0.1 * rng.standard_normal(S)).astype(np.float32))
+        z = rng.standard_normal((B, seq, d_A)).astype(np.float32)
+        vectors = bf16_round(rng.standard_normal((N, D)).astype(np.float32) * np.float32(0.02 * 50))
+        mesh = jax_standin.Mesh(np.arange(n_chips), ("tp",))
+        alpha, top_idx, sims_seq, alpha_raw_seq = ref_ret.MultiAspectRetrieval.pallas_hybrid_forward(
+            self, z, vectors, k, T, lam, use_sigmoid, tp_axis="tp", mesh=mesh)
+    finally:
+        ref_tk.tiled_topk_fallback = orig
+
+    asm = types.SimpleNamespace(d_A=d_A, d_B=d_B, r=r, _off_V=d_B * r, _off_b=d_B * r + r * d_A,
+                                _end_b=d_B * r + r * d_A + d_B)
+    asm.W_base = types.SimpleNamespace(value=np.zeros((d_B, d_A), np.float32))
+    asm.b_base = types.SimpleNamespace(value=np.zeros(d_B, np.float32))
+    W, b = ref_asm.WeightAssembler.assemble(asm, alpha, top_idx, vectors)
+
+    out["sharded/q"] = _bits(recorded["q"])
+    out["sharded/keys"] = _bits(np.concatenate(recorded["keys"], axis=0))
+    out["sharded/params"] = np.array([k, lam, recorded["tau"], T, float(use_sigmoid)], dtype=np.float64)
+    out["sharded/n_chips"] = np.array(n_chips)
+    out["sharded/alpha"] = np.asarray(alpha, np.float32).reshape(B * seq, k)
+    out["sharded/idx"] = np.asarray(top_idx, np.int32).reshape(B * seq, k)
+    out["sharded/local_vals"] = np.stack([np.asarray(v, np.float32) for v, _ in recorded["local"]])
+    out["sharded/local_idx"] = np.stack([np.asarray(i, np.int32) for _, i in recorded["local"]])
+    out["sharded/vectors"] = _bits(vectors)
+    out["sharded/b_slice"] = np.array([asm._off_b, asm._end_b])
+    out["sharded/b_delta"] = np.asarray(b, np.float32).reshape(B * seq, d_B)
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--reference", default="/root/reference",
+                    help="path of the reference checkout (read only)")
+    ap.add_argument("--out", default=str(HERE / "dwa_golden.npz"))
+    args = ap.parse_args(argv)
+
+    jax_standin.install()
+    sys.path.insert(0, args.reference)
+    from src.kernels import tiled_topk as ref_tk  # noqa: E402  (reference code)
+    from src.model import assembly as ref_asm  # noqa: E402
+    from src.model import retrieval as ref_ret  # noqa: E402
+
+    rng = np.random.default_rng(20261201)
+    out: dict[str, np.ndarray] = {}
+    case_tiled_topk(ref_tk, "c1_exp", rng, 128, 2000, 128, 16, 1.0, 0.0, 1.0, False, out)
+    case_tiled_topk(ref_tk, "c1_gate", rng, 96, 1500, 128, 16, 5.0, 0.5, 0.7, True, out)
+    case_tiled_topk(ref_tk, "odd", rng, 33, 777, 40, 5, 2.0, -0.25, 1.3, True, out)
+    case_ties(ref_tk, rng, out)
+    case_sharded(ref_tk, ref_ret, ref_asm, rng, out)
+    np.savez_compressed(args.out, **out)
+    print(f"wrote {args.out}: {len(out)} arrays")
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

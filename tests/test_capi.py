@@ -1,0 +1,124 @@
+"""CPU tests of the C ABI: the library loads, exports exactly what
+include/dwa_retrieval.h declares, and rejects invalid arguments on the host
+without launching anything (no GPU is touched by these calls)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from computd_b200 import _lib
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "dwa_retrieval.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"DWA_API\s+[\w\s\*]+?\b(dwa_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_bound_symbols():
+    assert declared_symbols() == sorted(_lib.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    assert lib.dwa_abi_version() == 1
+
+
+def test_only_dwa_symbols_are_exported():
+    import subprocess
+
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    text_syms = [l.split()[-1] for l in out.splitlines() if " T " in l]
+    assert sorted(text_syms) == declared_symbols()
+
+
+def test_status_strings():
+    lib = _lib.load()
+    names = {s: lib.dwa_status_string(s).decode() for s in range(7)}
+    assert names[0] == "DWA_OK" and names[4] == "DWA_ERR_TIMEOUT"
+    assert lib.dwa_status_string(99).decode() == "DWA_ERR_UNKNOWN"
+
+
+FAKE = 0x10000  # 16-byte aligned, never dereferenced: validation fails before any launch
+
+
+def score_topk(**kw):
+    lib = _lib.load()
+    a = dict(q=FAKE, M=128, ldq=128, keys=FAKE, N=1000, ldk=128, d=128, k=16, lam=1.0, tau=0.0,
+             T=1.0, sig=0, off=0, ov=FAKE, oi=FAKE, ws=FAKE, ws_bytes=0, stream=None)
+    a.update(kw)
+    st = lib.dwa_score_topk(a["q"], a["M"], a["ldq"], a["keys"], a["N"], a["ldk"], a["d"], a["k"],
+                            a["lam"], a["tau"], a["T"], a["sig"], a["off"], a["ov"], a["oi"],
+                            a["ws"], a["ws_bytes"], a["stream"])
+    return st, lib.dwa_last_error().decode()
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(q=None), _lib.DWA_ERR_INVALID_ARG),
+    (dict(ov=None), _lib.DWA_ERR_INVALID_ARG),
+    (dict(M=-1), _lib.DWA_ERR_INVALID_ARG),
+    (dict(N=0), _lib.DWA_ERR_INVALID_ARG),
+    (dict(k=0), _lib.DWA_ERR_INVALID_ARG),
+    (dict(k=1001), _lib.DWA_ERR_INVALID_ARG),          # k > N (lax.top_k raises too)
+    (dict(k=129, N=5000), _lib.DWA_ERR_UNSUPPORTED_SHAPE),
+    (dict(d=100, ldq=128, ldk=128), _lib.DWA_ERR_UNSUPPORTED_SHAPE),
+    (dict(d=4, ldq=8, ldk=8), _lib.DWA_ERR_UNSUPPORTED_SHAPE),
+    (dict(ldq=64), _lib.DWA_ERR_INVALID_ARG),
+    (dict(ldk=132), _lib.DWA_ERR_UNSUPPORTED_SHAPE),
+    (dict(q=FAKE + 8), _lib.DWA_ERR_INVALID_ARG),      # misaligned
+    (dict(off=-1), _lib.DWA_ERR_INVALID_ARG),
+    (dict(off=2**31 - 10), _lib.DWA_ERR_INVALID_ARG),  # global index overflows int32
+    (dict(T=0.0), _lib.DWA_ERR_UNSUPPORTED_SHAPE),
+    (dict(T=float("nan")), _lib.DWA_ERR_UNSUPPORTED_SHAPE),
+    (dict(sig=1, lam=-1.0), _lib.DWA_ERR_UNSUPPORTED_SHAPE),  # non-monotone gate
+    (dict(ws=None), _lib.DWA_ERR_WORKSPACE),
+    (dict(ws=FAKE + 16), _lib.DWA_ERR_WORKSPACE),      # not 256-aligned
+    (dict(ws_bytes=1024), _lib.DWA_ERR_WORKSPACE),     # too small
+])
+def test_score_topk_rejects_before_launch(kw, status):
+    st, msg = score_topk(**kw)
+    assert st == status, msg
+    assert msg
+
+
+def test_score_topk_empty_batch_is_a_noop():
+    st, msg = score_topk(M=0, q=None)
+    assert st == _lib.DWA_OK and msg == ""
+
+
+def test_workspace_plan():
+    lib = _lib.load()
+    # 8192 queries x 1M keys (the op-at-scale shape): 64 query tiles, 4096 key tiles
+    nbytes = lib.dwa_score_topk_workspace(8192, 1 << 20, 1024, 64)
+    assert nbytes > 0 and (nbytes - 256) % (64 * 8192 * 8) == 0
+    assert lib.dwa_score_topk_workspace(8192, 1 << 20, 1024, 129) == 0
+    assert lib.dwa_score_topk_workspace(0, 10, 8, 1) == 0
+
+
+def test_merge_and_gather_validation():
+    lib = _lib.load()
+    assert lib.dwa_merge_topk(FAKE, FAKE, 0, 8, 4, FAKE + 256, FAKE + 512, None) == 1
+    assert lib.dwa_merge_topk(FAKE, FAKE, 2, 8, 4, FAKE, FAKE + 512, None) == 1  # aliasing
+    assert lib.dwa_merge_topk(FAKE, FAKE, 2, 8, 200, FAKE + 256, FAKE + 512, None) == 2
+    assert lib.dwa_weighted_gather(FAKE, FAKE, 8, 4, FAKE, 0, 10, 64, 60, FAKE, None, None) == 2
+    assert lib.dwa_weighted_gather(FAKE, FAKE, 8, 4, FAKE, 5, 2, 64, 64, FAKE, None, None) == 1
+    assert lib.dwa_weighted_gather(FAKE, FAKE, 8, 4, FAKE + 8, 0, 10, 64, 64, FAKE, None, None) == 1
+    assert lib.dwa_weighted_gather(FAKE, FAKE, 8, 4, FAKE, 0, 10, 60, 64, FAKE, None, None) == 1
+    assert lib.dwa_pool_init_normal(FAKE, 4, 8, 4, 0, 1, 1.0, None) == 1
+    assert lib.dwa_workspace_status(None, None, ctypes.byref(ctypes.c_int32())) == 1
+
+
+def test_python_api_refuses_cpu_tensors():
+    import torch
+
+    from computd_b200 import tiled_topk_fused
+
+    q = torch.zeros(4, 16, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        tiled_topk_fused(q, q, 2, 1.0, 0.0, 1.0, False)

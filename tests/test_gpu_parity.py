@@ -1,0 +1,259 @@
+"""GPU parity: the sm_100a kernels (through the C ABI) against the oracle and
+against fixtures computed by the reference's own code.
+
+Tolerance (the parity contract): bf16 inputs, fp32 accumulation; scores and
+outputs within rel 1e-2; top-k index sets identical except at near-ties of
+the k-th value (oracle.compare_topk).  Exact ties must come back lower index
+first, like jax.lax.top_k.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import dwa_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-2
+
+
+def _dev():
+    return torch.device("cuda", 0)
+
+
+def to_dev_bf16(bits: np.ndarray) -> torch.Tensor:
+    t = torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).to(_dev())
+    return t.view(torch.bfloat16)
+
+
+def from_f32(x: np.ndarray) -> torch.Tensor:
+    return to_dev_bf16(O.bf16_bits(x))
+
+
+def _status_ok():
+    torch.cuda.synchronize()
+
+
+@pytest.fixture(scope="module")
+def lib():
+    import computd_b200
+
+    computd_b200.load_library()
+    return computd_b200
+
+
+def _case(golden, name):
+    k, lam, tau, T, sig = golden[f"{name}/params"]
+    return (O.bits_to_f32(golden[f"{name}/q"]), O.bits_to_f32(golden[f"{name}/keys"]), int(k),
+            float(lam), float(tau), float(T), bool(sig))
+
+
+@pytest.mark.parametrize("name", ["c1_exp", "c1_gate", "odd", "ties"])
+def test_golden_tiled_topk(lib, golden, name):
+    q, keys, k, lam, tau, T, sig = _case(golden, name)
+    v, i = lib.tiled_topk_fused(to_dev_bf16(golden[f"{name}/q"]),
+                                to_dev_bf16(golden[f"{name}/keys"]), k, lam, tau, T, sig)
+    v, i = v.cpu().numpy(), i.cpu().numpy()
+    errs = O.compare_topk(v, i, golden[f"{name}/vals"], golden[f"{name}/idx"], q, keys, lam, tau,
+                          T, sig, rtol=RTOL)
+    assert errs == [], errs
+    if name == "ties":
+        # integer-valued inputs: every score is exact, so ties must resolve exactly
+        np.testing.assert_array_equal(i, golden["ties/idx"])
+        np.testing.assert_array_equal(v, golden["ties/vals"])
+
+
+def test_golden_sharded_merge_and_assembly(lib, golden):
+    q, keys, k, lam, tau, T, sig = _case(golden, "sharded")
+    P = int(golden["sharded/n_chips"])
+    n_local = keys.shape[0] // P
+    qd = to_dev_bf16(golden["sharded/q"])
+    kd = to_dev_bf16(golden["sharded/keys"])
+    loc_v, loc_i = [], []
+    for p in range(P):
+        v, i = lib.tiled_topk_fused(qd, kd[p * n_local:(p + 1) * n_local], k, lam, tau, T, sig,
+                                    idx_offset=p * n_local)
+        loc_v.append(v)
+        loc_i.append(i)
+        errs = O.compare_topk(v.cpu().numpy(), i.cpu().numpy() - p * n_local,
+                              golden["sharded/local_vals"][p], golden["sharded/local_idx"][p], q,
+                              keys[p * n_local:(p + 1) * n_local], lam, tau, T, sig, rtol=RTOL)
+        assert errs == [], (p, errs)
+    fv, fi = lib.merge_topk(torch.stack(loc_v), torch.stack(loc_i))
+    fv, fi = fv.cpu().numpy(), fi.cpu().numpy()
+    errs = O.compare_topk(fv, fi, O.chip_merge(golden["sharded/local_vals"],
+                                               (golden["sharded/local_idx"] + (np.arange(P) * n_local)[:, None, None]).astype(np.int32))[0],
+                          golden["sharded/idx"], q, keys, lam, tau, T, sig, rtol=RTOL)
+    assert errs == [], errs
+    np.testing.assert_allclose(O.normalise(fv), golden["sharded/alpha"], rtol=RTOL)
+    # value side through the reference's own assembly output (b_delta block)
+    vectors = to_dev_bf16(golden["sharded/vectors"])
+    b0, b1 = (int(x) for x in golden["sharded/b_slice"])
+    out, alpha = lib.weighted_value_sum(torch.from_numpy(golden["sharded/alpha"]).to(_dev()),
+                                        torch.from_numpy(golden["sharded/idx"]).to(_dev()),
+                                        vectors[:, b0:b1])
+    assert O.compare_rows(out.cpu().numpy(), golden["sharded/b_delta"], rtol=RTOL) == []
+
+
+SHAPES = [
+    # M, N, d, k, use_sigmoid
+    (1, 300, 64, 1, False),
+    (1, 256, 8, 8, True),
+    (5, 17, 16, 17, False),          # k == N
+    (127, 1000, 128, 16, False),
+    (129, 4097, 200, 32, True),      # ragged M, N and d (d not a multiple of 64)
+    (300, 20000, 384, 32, False),
+    (256, 9000, 1024, 64, True),
+    (200, 6000, 512, 128, False),    # largest supported k
+    (64, 3000, 40, 100, True),
+]
+
+
+@pytest.mark.parametrize("M,N,d,k,sig", SHAPES)
+def test_random_shapes_vs_oracle(lib, M, N, d, k, sig):
+    rng = np.random.default_rng(M * 7919 + N * 31 + d + k)
+    q = O.bf16_round(rng.standard_normal((M, d), dtype=np.float32))
+    keys = O.bf16_round(rng.standard_normal((N, d), dtype=np.float32) / np.float32(np.sqrt(d)))
+    lam, tau, T = 3.0, 0.2, 0.9
+    v, i = lib.tiled_topk_fused(from_f32(q), from_f32(keys), k, lam, tau, T, sig)
+    rv, ri = O.tiled_topk(q, keys, k, lam, tau, T, sig)
+    errs = O.compare_topk(v.cpu().numpy(), i.cpu().numpy(), rv, ri, q, keys, lam, tau, T, sig,
+                          rtol=RTOL)
+    assert errs == [], errs
+
+
+def test_strided_inputs_and_offset(lib):
+    rng = np.random.default_rng(5)
+    M, N, d, k = 70, 3000, 96, 10
+    qb = from_f32(rng.standard_normal((M, 128), dtype=np.float32))
+    kb = from_f32(rng.standard_normal((N, 160), dtype=np.float32) / 10)
+    q, keys = qb[:, :d], kb[:, :d]   # row strides 128 and 160 elements
+    v, i = lib.tiled_topk_fused(q, keys, k, 1.0, 0.0, 1.0, False, idx_offset=12345)
+    qn = q.float().cpu().numpy()
+    kn = keys.float().cpu().numpy()
+    rv, ri = O.tiled_topk(qn, kn, k)
+    errs = O.compare_topk(v.cpu().numpy(), i.cpu().numpy() - 12345, rv, ri, qn, kn, rtol=RTOL)
+    assert errs == [], errs
+
+
+def test_merge_matches_oracle(lib):
+    rng = np.random.default_rng(11)
+    P, M, k = 8, 333, 64
+    vals = -np.sort(-rng.standard_normal((P, M, k)).astype(np.float32), axis=2)
+    vals[:, :, 10:14] = vals[:, :, 10:11]   # ties inside and across lists
+    vals = -np.sort(-vals, axis=2)
+    idx = (np.arange(P)[:, None, None] * 1000 + rng.integers(0, 1000, (P, M, k))).astype(np.int32)
+    for p in range(P):  # sorted lists, lower index first on ties (as dwa_score_topk emits)
+        for m in range(M):
+            o = np.lexsort((idx[p, m], -vals[p, m]))
+            idx[p, m], vals[p, m] = idx[p, m][o], vals[p, m][o]
+    fv, fi = lib.merge_topk(torch.from_numpy(vals).to(_dev()), torch.from_numpy(idx).to(_dev()))
+    rv, ri = O.chip_merge(vals, idx)
+    np.testing.assert_array_equal(fi.cpu().numpy(), ri)
+    np.testing.assert_array_equal(fv.cpu().numpy(), rv)
+
+
+@pytest.mark.parametrize("M,N,d,k", [(1, 10, 8, 1), (77, 500, 128, 16), (64, 4096, 1024, 64),
+                                     (33, 700, 264, 128)])
+def test_weighted_gather_vs_oracle(lib, M, N, d, k):
+    rng = np.random.default_rng(M + N + d + k)
+    vals = np.abs(rng.standard_normal((M, k))).astype(np.float32) + 0.1
+    idx = rng.integers(0, N, (M, k)).astype(np.int32)
+    values = O.bf16_round(rng.standard_normal((N, d), dtype=np.float32))
+    out, alpha = lib.weighted_value_sum(torch.from_numpy(vals).to(_dev()),
+                                        torch.from_numpy(idx).to(_dev()), from_f32(values))
+    ra = O.normalise(vals)
+    np.testing.assert_allclose(alpha.cpu().numpy(), ra, rtol=1e-5)
+    assert O.compare_rows(out.cpu().numpy(), O.weighted_sum(ra, idx, values), rtol=RTOL) == []
+
+
+def test_owner_computes_partials_add_up(lib):
+    rng = np.random.default_rng(3)
+    M, N, d, k, P = 50, 800, 64, 16, 4
+    vals = np.abs(rng.standard_normal((M, k))).astype(np.float32)
+    idx = rng.integers(0, N, (M, k)).astype(np.int32)
+    values = from_f32(rng.standard_normal((N, d), dtype=np.float32))
+    vd, idd = torch.from_numpy(vals).to(_dev()), torch.from_numpy(idx).to(_dev())
+    full, _ = lib.weighted_value_sum(vd, idd, values)
+    n = N // P
+    parts = sum(lib.weighted_value_sum(vd, idd, values[p * n:(p + 1) * n], row_begin=p * n)[0]
+                for p in range(P))
+    torch.testing.assert_close(parts, full, rtol=1e-5, atol=1e-5)
+
+
+def test_pool_init_matches_oracle_generator(lib):
+    rows, cols, seed = 300, 72, 123456789
+    dev = lib.new_normal(rows, cols, seed, stddev=0.5, row_offset=1000)
+    got = dev.float().cpu().numpy()
+    want = O.bf16_round(O.pool_init_normal(rows, cols, seed, 0.5, row_offset=1000))
+    ulp = np.abs(got.view(np.int32) - want.view(np.int32)) >> 16
+    assert ulp.max() <= 1
+    assert (ulp == 0).mean() > 0.99
+    # shard invariance on the device
+    a = lib.new_normal(64, 72, seed, 0.5, row_offset=1000)
+    torch.testing.assert_close(a, dev[:64], rtol=0, atol=0)
+
+
+def test_c1_config_full(lib):
+    """C1: queries [2048,128] ~N(0,1), keys [16384,128] ~N(0,1/128), values ~N(0,1),
+    k=16, softmax over the 16 scores, weighted sum (seed 0; bf16-rounded on the GPU)."""
+    rng = np.random.default_rng(0)
+    q = rng.standard_normal((2048, 128), dtype=np.float32)
+    keys = rng.standard_normal((16384, 128), dtype=np.float32) / np.float32(np.sqrt(128))
+    values = rng.standard_normal((16384, 128), dtype=np.float32)
+    qb, kb, vb = O.bf16_round(q), O.bf16_round(keys), O.bf16_round(values)
+    r = lib.Retriever(from_f32(kb), from_f32(vb), 2048, 16)
+    out, alpha, tv, ti = r(from_f32(qb))
+    torch.cuda.synchronize()
+    assert r.status() == 0
+    ro, ra, rv, ri = O.retrieve(qb, kb, vb, 16)
+    errs = O.compare_topk(tv.cpu().numpy(), ti.cpu().numpy(), rv, ri, qb, kb, rtol=RTOL)
+    assert errs == [], errs
+    # value side checked on the GPU's own selection (a near-tie swap changes rows legitimately)
+    ti_n = ti.cpu().numpy()
+    want = O.weighted_sum(O.normalise(tv.cpu().numpy()), ti_n, vb)
+    assert O.compare_rows(out.cpu().numpy(), want, rtol=RTOL) == []
+    assert O.compare_rows(out.cpu().numpy(), ro, rtol=RTOL) == [] or \
+        (ti_n != ri).any()
+
+
+def test_op_at_scale_properties(lib):
+    """C3 shape (8192 x 1,048,576 x 1024, k=64): sampled rows against an exact
+    recomputation, plus size-independent properties on every row."""
+    dev = _dev()
+    M, N, d, k = 8192, 1 << 20, 1024, 64
+    q = lib.new_normal(M, d, seed=1, stddev=1.0)
+    keys = lib.new_normal(N, d, seed=2, stddev=d ** -0.5)
+    values = lib.new_normal(N, d, seed=3, stddev=1.0)
+    r = lib.Retriever(keys, values, M, k)
+    out, alpha, tv, ti = r(q)
+    torch.cuda.synchronize()
+    assert r.status() == 0
+    # every row: sorted, in range, no duplicates, alpha sums to 1
+    assert bool((tv[:, 1:] <= tv[:, :-1]).all())
+    assert int(ti.min()) >= 0 and int(ti.max()) < N
+    s_idx, _ = torch.sort(ti, dim=1)
+    assert not bool((s_idx[:, 1:] == s_idx[:, :-1]).any())
+    torch.testing.assert_close(alpha.sum(1), torch.ones(M, device=dev), rtol=1e-5, atol=1e-5)
+    # returned scores equal the recomputed dot products of the returned indices
+    s_true = torch.einsum("md,mkd->mk", q.float(), keys[ti.long()].float())
+    torch.testing.assert_close(tv, torch.exp(s_true), rtol=1e-4, atol=0)
+    # sampled rows: exact top-k over the whole pool (fp32 scores on the GPU, oracle top_k)
+    rows = torch.arange(0, M, M // 24, device=dev)
+    s = (q[rows].float() @ keys.float().T).double().cpu().numpy()
+    rv, ri = O.top_k(np.exp(s), k)
+    got_v, got_i = tv[rows].cpu().numpy(), ti[rows].cpu().numpy()
+    qn, kn = q[rows].float().cpu().numpy(), None
+    bad = 0
+    for j in range(len(rows)):
+        gs, rs_ = set(got_i[j].tolist()), set(ri[j].tolist())
+        if gs != rs_:
+            extra = np.array(sorted(gs - rs_))
+            vext = np.exp(s[j, extra])
+            if (vext < rv[j, -1] * (1 - RTOL)).any():
+                bad += 1
+    assert bad == 0
+    np.testing.assert_allclose(got_v, rv, rtol=RTOL)
+    # value side on the sampled rows
+    want = torch.einsum("mk,mkd->md", alpha[rows].double(), values[ti[rows].long()].double())
+    assert O.compare_rows(out[rows].cpu().numpy(), want.cpu().numpy(), rtol=RTOL) == []
