@@ -41,6 +41,9 @@ WORKLOADS = {
     "op_at_scale": dict(M=8192, N=1 << 20, d=1024, k=64, use_sigmoid=False,
                         desc="queries [8192,1024] bf16 ~N(0,1); pool 1,048,576x1024 bf16 keys "
                              "~N(0,1/1024), values ~N(0,1); top-k 64; softmax-weighted value sum"),
+    "profile_small": dict(M=8192, N=131072, d=1024, k=64, use_sigmoid=False,
+                          desc="profiling case: queries [8192,1024]; pool 131,072x1024 (256 MiB "
+                               "keys, larger than L2); top-k 64"),
     "c1_op": dict(M=2048, N=16384, d=128, k=16, use_sigmoid=False,
                   desc="queries [2048,128]; pool [16384,128]; top-k 16; softmax-weighted sum"),
 }

@@ -130,6 +130,8 @@ dwa_status dwa_merge_topk(const float* cand_vals, const int32_t* cand_idx, int32
   if (!cand_vals || !cand_idx || !out_vals || !out_idx)
     return fail(DWA_ERR_INVALID_ARG, "null pointer");
   if (P < 1) return fail(DWA_ERR_INVALID_ARG, "P=%d must be >= 1", P);
+  if (P > dwa::kMaxSplits)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "P=%d exceeds %d lists", P, dwa::kMaxSplits);
   if (k < 1) return fail(DWA_ERR_INVALID_ARG, "k=%d must be >= 1", k);
   if (k > DWA_MAX_K)
     return fail(DWA_ERR_UNSUPPORTED_SHAPE, "k=%d exceeds DWA_MAX_K=%d", k, DWA_MAX_K);

@@ -8,11 +8,14 @@
 
 namespace dwa {
 
-// Tile shape of the fused score + top-k kernel (one CTA, cta_group::1).
-constexpr int kTileM = 128;   // query rows per tile  (UMMA M, TMEM lanes)
+// Tile shape of the fused score + top-k kernel: a CTA pair (cta_group::2)
+// computes 2 x kTileM query rows against kTileN keys per MMA.
+constexpr int kTileM = 128;   // query rows per CTA   (TMEM lanes)
 constexpr int kTileN = 256;   // pool keys per tile   (UMMA N, TMEM columns)
 constexpr int kTileK = 64;    // bf16 elements per 128-byte swizzled row
 constexpr size_t kStatusBytes = 256;  // status word block at the head of the workspace
+constexpr int kMaxSplits = 128;       // most lists one merge handles (key splits or shards)
+#define DWA_MERGE_MAX_K 128           // most entries a merged list keeps
 
 // How one dwa_score_topk call is cut into work units.
 // A unit is (query tile, contiguous range of key tiles); each unit leaves one
@@ -20,13 +23,13 @@ constexpr size_t kStatusBytes = 256;  // status word block at the head of the wo
 struct ScoreTopkPlan {
   int64_t M = 0, N = 0;
   int d = 0, k = 0;
-  int n_qt = 0;        // query tiles  = ceil(M / 128)
+  int n_qt = 0;        // pair query tiles = ceil(M / 256)
   int64_t n_kt = 0;    // key tiles    = ceil(N / 256)
   int n_split = 0;     // key-range splits per query tile
   int num_kb = 0;      // k-blocks of 64 along d
   int kcap = 0;        // heap capacity variant (16, 32, 64, 128)
-  int64_t m_pad = 0;   // n_qt * 128
-  size_t ws_bytes = 0; // status block + partial lists
+  int64_t m_pad = 0;   // n_qt * 256
+  size_t ws_bytes = 0; // status block + per-row bounds + partial lists
 };
 
 // Returns false when the shape is outside what the kernel supports.

@@ -1,17 +1,22 @@
-// merge_topk.cu — k-way merge of per-split / per-shard top-k candidate lists.
+// merge_topk.cu — k-way merge of sorted per-split / per-shard top-k lists.
 //
 // Two callers:
 //  * dwa_score_topk: merges the key-range splits of the fused kernel (raw
-//    scores s), sorts, evaluates v(s) = [sigmoid(lambda (s - tau))] * exp(s / T)
-//    on the k survivors (tiled_topk.py:172-175) and adds the shard's global
-//    index offset (retrieval.py:292-293).
+//    scores s, each list sorted best first), evaluates
+//    v(s) = [sigmoid(lambda (s - tau))] * exp(s / T) on the k survivors
+//    (tiled_topk.py:172-175) and adds the shard's global index offset
+//    (retrieval.py:292-293).
 //  * dwa_merge_topk: the cross-shard merge after the all-gather, i.e. the
 //    transpose/reshape + top_k + take of _chip_topk (retrieval.py:299-302).
 //    Flattening [P, M, k] chip-major and taking top_k with lower position first
 //    among ties equals ordering by (v desc, global index asc), because shard p's
 //    global indices all precede shard p+1's and each list is already sorted.
 //
-// One thread per query row; its k-entry heap sits in shared memory.
+// One warp per query row.  Lane l holds the heads of lists l, l+32, l+64,
+// l+96 (up to kMaxSplits lists), each with the next few entries cached in
+// registers; every output step is a warp arg-max over the lane heads followed
+// by an advance of the winning list.  Lists must be sorted best first
+// (score descending, lower index first among equal scores).
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -22,6 +27,10 @@
 namespace dwa {
 
 namespace {
+
+constexpr int kWarps = 8;           // rows per block
+constexpr int kSlots = kMaxSplits / 32;  // lists per lane
+constexpr int kCache = 4;           // entries cached per list
 
 struct MergeArgs {
   const float* cv;
@@ -44,92 +53,143 @@ __device__ __forceinline__ float fused_score(float s, int use_sigmoid, float lam
   return g * e;
 }
 
-template <int TPB>
-__global__ void __launch_bounds__(TPB) merge_topk_kernel(const MergeArgs a) {
-  extern __shared__ uint8_t smem[];
-  float* hs = reinterpret_cast<float*>(smem);
-  int32_t* hi = reinterpret_cast<int32_t*>(smem + static_cast<size_t>(a.k) * TPB * 4);
-  const int t = threadIdx.x;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * TPB + t;
-  if (row >= a.M) return;  // each thread touches only its own heap column
+template <typename V>
+__device__ __forceinline__ V pick4(const V (&c)[kCache], int j) {
+  const V lo = (j & 1) ? c[1] : c[0];
+  const V hi = (j & 1) ? c[3] : c[2];
+  return (j & 2) ? hi : lo;
+}
 
-  const SmemHeap heap{hs, hi, TPB, a.k};
-  heap.init(t);
-  float rs = -INFINITY;
-  int32_t ri = kSentinelIdx;
-  for (int l = 0; l < a.n_lists; ++l) {
-    const float* vp = a.cv + l * a.stride_list + row * a.stride_row;
-    const int32_t* ip = a.ci + l * a.stride_list + row * a.stride_row;
-    int p = 0;
-    for (; p + 4 <= a.k_in; p += 4) {
-      float s[4];
-      int32_t ix[4];
+struct ListCursor {
+  float s[kCache];
+  int32_t i[kCache];
+  int base;  // position of s[0] in the list
+  int off;   // current head = entry `off` of the cache
+};
+
+__device__ __forceinline__ void load_block(ListCursor& L, const float* vp, const int32_t* ip,
+                                           int64_t stride_pos, int k_in) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        s[u] = __ldg(vp + (p + u) * a.stride_pos);
-        ix[u] = __ldg(ip + (p + u) * a.stride_pos);
-      }
+  for (int e = 0; e < kCache; ++e) {
+    const int p = L.base + e;
+    const bool in = p < k_in;
+    L.s[e] = in ? __ldg(vp + p * stride_pos) : -INFINITY;
+    L.i[e] = in ? __ldg(ip + p * stride_pos) : kSentinelIdx;
+  }
+}
+
+__global__ void __launch_bounds__(kWarps * 32) merge_sorted_kernel(const MergeArgs a) {
+  __shared__ float st_s[kWarps][DWA_MERGE_MAX_K];
+  __shared__ int32_t st_i[kWarps][DWA_MERGE_MAX_K];
+  const int w = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + w;
+  if (row >= a.M) return;  // warp-uniform; only warp-level synchronisation below
+
+  ListCursor cur[kSlots];
+  const float* vbase[kSlots];
+  const int32_t* ibase[kSlots];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (topk_worse(rs, ri, s[u], ix[u])) {
-          heap.replace_root(t, s[u], ix[u]);
-          rs = heap.S(0, t);
-          ri = heap.I(0, t);
-        }
-      }
-    }
-    for (; p < a.k_in; ++p) {
-      const float s = __ldg(vp + p * a.stride_pos);
-      const int32_t ix = __ldg(ip + p * a.stride_pos);
-      if (topk_worse(rs, ri, s, ix)) {
-        heap.replace_root(t, s, ix);
-        rs = heap.S(0, t);
-        ri = heap.I(0, t);
+  for (int u = 0; u < kSlots; ++u) {
+    const int l = lane + 32 * u;
+    cur[u].base = 0;
+    cur[u].off = 0;
+    if (l < a.n_lists) {
+      vbase[u] = a.cv + l * a.stride_list + row * a.stride_row;
+      ibase[u] = a.ci + l * a.stride_list + row * a.stride_row;
+      load_block(cur[u], vbase[u], ibase[u], a.stride_pos, a.k_in);
+    } else {
+      vbase[u] = nullptr;
+      ibase[u] = nullptr;
+#pragma unroll
+      for (int e = 0; e < kCache; ++e) {
+        cur[u].s[e] = -INFINITY;
+        cur[u].i[e] = kSentinelIdx;
       }
     }
   }
-  heap.sort_best_first(t);
+
+  for (int j = 0; j < a.k; ++j) {
+    // best head of this lane's lists
+    float bs = -INFINITY;
+    int32_t bi = kSentinelIdx;
+    int bu = 0;
+#pragma unroll
+    for (int u = 0; u < kSlots; ++u) {
+      const float hs = pick4(cur[u].s, cur[u].off);
+      const int32_t hi = pick4(cur[u].i, cur[u].off);
+      if (topk_worse(bs, bi, hs, hi)) {
+        bs = hs;
+        bi = hi;
+        bu = u;
+      }
+    }
+    // warp arg-best; (score, index) pairs are unique except for sentinels
+    float ws = bs;
+    int32_t wi = bi;
+    int wl = lane;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float os = __shfl_xor_sync(0xffffffffu, ws, o);
+      const int32_t oi = __shfl_xor_sync(0xffffffffu, wi, o);
+      const int ol = __shfl_xor_sync(0xffffffffu, wl, o);
+      if (topk_worse(ws, wi, os, oi) || (ws == os && wi == oi && ol < wl)) {
+        ws = os;
+        wi = oi;
+        wl = ol;
+      }
+    }
+    if (lane == 0) {
+      st_s[w][j] = ws;
+      st_i[w][j] = wi;
+    }
+    if (lane == wl) {
+#pragma unroll
+      for (int u = 0; u < kSlots; ++u) {
+        if (u == bu) {
+          if (++cur[u].off == kCache) {
+            cur[u].off = 0;
+            cur[u].base += kCache;
+            if (vbase[u] != nullptr) {
+              load_block(cur[u], vbase[u], ibase[u], a.stride_pos, a.k_in);
+            }
+          }
+        }
+      }
+    }
+  }
+  __syncwarp();
 
   if (a.transform) {
-    for (int p = 0; p < a.k; ++p)
-      heap.S(p, t) = fused_score(heap.S(p, t), a.use_sigmoid, a.lambda_sharp, a.tau, a.T);
+    for (int j = lane; j < a.k; j += 32)
+      st_s[w][j] = fused_score(st_s[w][j], a.use_sigmoid, a.lambda_sharp, a.tau, a.T);
+    __syncwarp();
     // v is non-decreasing in s, so the list is ordered by v already; entries
     // whose v became equal must still be ordered by lower index first.
-    for (int p = 1; p < a.k; ++p) {
-      const float vs = heap.S(p, t);
-      const int32_t vi = heap.I(p, t);
-      int q = p - 1;
-      while (q >= 0 && topk_worse(heap.S(q, t), heap.I(q, t), vs, vi)) {
-        heap.S(q + 1, t) = heap.S(q, t);
-        heap.I(q + 1, t) = heap.I(q, t);
-        --q;
+    if (lane == 0) {
+      for (int p = 1; p < a.k; ++p) {
+        const float vs = st_s[w][p];
+        const int32_t vi = st_i[w][p];
+        int q = p - 1;
+        while (q >= 0 && topk_worse(st_s[w][q], st_i[w][q], vs, vi)) {
+          st_s[w][q + 1] = st_s[w][q];
+          st_i[w][q + 1] = st_i[w][q];
+          --q;
+        }
+        st_s[w][q + 1] = vs;
+        st_i[w][q + 1] = vi;
       }
-      heap.S(q + 1, t) = vs;
-      heap.I(q + 1, t) = vi;
     }
+    __syncwarp();
   }
 
   float* ov = a.out_v + row * a.k;
   int32_t* oi = a.out_i + row * a.k;
-  for (int p = 0; p < a.k; ++p) {
-    const int32_t ix = heap.I(p, t);
-    ov[p] = heap.S(p, t);
-    oi[p] = ix == kSentinelIdx ? -1 : static_cast<int32_t>(ix + a.idx_offset);
+  for (int j = lane; j < a.k; j += 32) {
+    const int32_t ix = st_i[w][j];
+    ov[j] = st_s[w][j];
+    oi[j] = ix == kSentinelIdx ? -1 : static_cast<int32_t>(ix + a.idx_offset);
   }
-}
-
-template <int TPB>
-cudaError_t launch_tpb(const MergeArgs& a, cudaStream_t stream) {
-  const size_t smem = static_cast<size_t>(a.k) * TPB * 8;
-  if (smem > 48 * 1024) {
-    cudaError_t e =
-        cudaFuncSetAttribute(merge_topk_kernel<TPB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-  }
-  const int64_t blocks = (a.M + TPB - 1) / TPB;
-  merge_topk_kernel<TPB><<<static_cast<unsigned>(blocks), TPB, smem, stream>>>(a);
-  return cudaGetLastError();
 }
 
 }  // namespace
@@ -141,6 +201,8 @@ cudaError_t launch_merge_topk(const float* cand_vals, const int32_t* cand_idx, i
                               int64_t idx_offset, float* out_vals, int32_t* out_idx,
                               cudaStream_t stream) {
   if (M <= 0) return cudaSuccess;
+  if (n_lists < 1 || n_lists > kMaxSplits || k < 1 || k > DWA_MERGE_MAX_K)
+    return cudaErrorInvalidValue;
   MergeArgs a;
   a.cv = cand_vals;
   a.ci = cand_idx;
@@ -159,9 +221,9 @@ cudaError_t launch_merge_topk(const float* cand_vals, const int32_t* cand_idx, i
   a.T = T;
   a.out_v = out_vals;
   a.out_i = out_idx;
-  // Keep the per-block heap at <= 32 KB so several blocks share an SM.
-  if (k <= 64) return launch_tpb<64>(a, stream);
-  return launch_tpb<32>(a, stream);
+  const int64_t blocks = (M + kWarps - 1) / kWarps;
+  merge_sorted_kernel<<<static_cast<unsigned>(blocks), kWarps * 32, 0, stream>>>(a);
+  return cudaGetLastError();
 }
 
 }  // namespace dwa

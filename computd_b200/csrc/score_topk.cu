@@ -6,25 +6,30 @@
 //     sims = jnp.dot(queries, keys.T); score = gate(sims) * exp(sims / T);
 //     lax.top_k(score, k_max)
 // which materialises the whole [M, N] score matrix before a sort-based top-k.
-// Here the [128 x 256] score tile lives only in tensor memory (TMEM); the
+// Here each [256 x 256] score tile lives only in tensor memory (TMEM); the
 // epilogue keeps the k best (score, index) per query row in a shared-memory
-// heap and the full score matrix never reaches HBM.
+// heap, so the full score matrix never reaches HBM.
 //
-// CTA = 6 warps, warp-specialised:
-//   warp 0     TMA producer: bf16 query tile [128 x 64] and key tile [256 x 64]
-//              per k-block, 128-byte swizzled, into a STAGES-deep ring
-//   warp 1     TMEM allocator + UMMA issuer: tcgen05.mma.cta_group::1.kind::f16
-//              128x256x16, fp32 accumulators double-buffered in TMEM (2 x 256 cols)
+// Launch unit = a CTA pair (cluster of 2 on neighbouring SMs) running
+// tcgen05.mma.cta_group::2: one 256 x 256 x 16 MMA covers 256 query rows (128
+// per CTA) against 256 keys (128 staged per CTA), so each SM stages only half
+// of the key tile and half of the pair's query rows per k-block.
+// Each CTA = 6 warps, warp-specialised:
+//   warp 0     TMA producer: its 128 query rows x 64 and its 128 keys x 64
+//              (bf16, 128-byte swizzle) per k-block into a STAGES-deep ring;
+//              the byte counts complete on the leader CTA's "full" barrier
+//   warp 1     TMEM allocator (both CTAs) + UMMA issuer (leader CTA only):
+//              fp32 accumulators double-buffered in TMEM (2 x 256 columns)
 //   warps 2-5  epilogue: warp w reads TMEM lanes 32*(w%4).. with tcgen05.ld;
-//              thread = one query row, register threshold = heap root, warp-wide
-//              OR of the "beats threshold" masks skips clean 32-column chunks
+//              thread = one query row; heap root = admission threshold; each
+//              lane walks only its own candidates
 //
-// Work unit = (query tile, contiguous range of key tiles).  Units are ordered
-// split-major so the CTAs resident at one time sweep the same few key ranges:
-// every key tile is fetched from HBM about once and re-served from L2 to all
-// query tiles.  Each unit leaves one partial top-k list per row in the
-// workspace; merge_topk.cu merges the splits, sorts, applies the gate/exp and
-// adds the global index offset.
+// Work unit = (pair query tile, contiguous range of key tiles).  Units are
+// ordered split-major so the pairs resident at one time sweep the same few
+// key ranges: each key tile is fetched from HBM about once and re-served
+// from L2 to every query tile.  Each unit leaves one sorted partial top-k list
+// per row in the workspace; merge_topk.cu merges the splits, applies the
+// gate/exp and adds the global index offset.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -44,36 +49,71 @@ namespace {
 
 constexpr int kThreads = 192;
 constexpr int kMaxDynSmem = 232448;  // 227 KB opt-in limit on sm_100
+constexpr int kPairRows = 2 * kTileM;      // 256 query rows per CTA pair
+constexpr int kKeysPerCta = kTileN / 2;    // 128 keys of each 256-key tile per CTA
 
 template <int KCAP>
 struct TopkCfg {
-  static constexpr int kStageA = kTileM * kTileK * 2;  // 16 KB query tile
-  static constexpr int kStageB = kTileN * kTileK * 2;  // 32 KB key tile
+  static constexpr int kStageA = kTileM * kTileK * 2;       // 16 KB: this CTA's query rows
+  static constexpr int kStageB = kKeysPerCta * kTileK * 2;  // 16 KB: this CTA's half of the keys
   static constexpr int kStageBytes = kStageA + kStageB;
   static constexpr int kHeapBytes = KCAP * kTileM * 8;
   static constexpr int kBarBytes = 256;
   static constexpr int kStagesFit = (kMaxDynSmem - 1024 - kHeapBytes - kBarBytes) / kStageBytes;
-  static constexpr int kStages = kStagesFit > 4 ? 4 : kStagesFit;
+  static constexpr int kStages = kStagesFit > 6 ? 6 : kStagesFit;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kHeapBytes + kBarBytes;
   static_assert(kStages >= 2, "pipeline needs at least two stages");
   static_assert(kSmemBytes <= kMaxDynSmem, "shared memory budget exceeded");
 };
 
+// v[j] for a runtime j without indexing the register array dynamically (which
+// would spill it to local memory): a 5-level select tree, 31 selects.
+__device__ __forceinline__ float pick32(const float (&v)[32], int j) {
+  float a[16], b[8], c[4], d[2];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) a[i] = (j & 1) ? v[2 * i + 1] : v[2 * i];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) b[i] = (j & 2) ? a[2 * i + 1] : a[2 * i];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) c[i] = (j & 4) ? b[2 * i + 1] : b[2 * i];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) d[i] = (j & 8) ? c[2 * i + 1] : c[2 * i];
+  return (j & 16) ? d[1] : d[0];
+}
+
+// Order-preserving map float -> int32 (signed integer order = float order),
+// so atomicMax on the image maximises the float.
+__device__ __forceinline__ int32_t ordered_int(float f) {
+  const int32_t i = __float_as_int(f);
+  return i >= 0 ? i : (i ^ 0x7FFFFFFF);
+}
+__device__ __forceinline__ float ordered_float(int32_t i) {
+  return __int_as_float(i >= 0 ? i : (i ^ 0x7FFFFFFF));
+}
+// Largest float strictly below x: "s >= x" <=> "s > float_below(x)"; -inf stays -inf.
+__device__ __forceinline__ float float_below(float x) {
+  if (x == -INFINITY) return -INFINITY;
+  if (x == 0.0f) return -1.40129846e-45f;
+  const int32_t i = __float_as_int(x);
+  return __int_as_float(x > 0.0f ? i - 1 : i + 1);
+}
+
 struct TopkKernelArgs {
   int64_t N;         // keys in this shard
-  int64_t n_kt;      // key tiles
-  int64_t m_pad;     // padded query rows (row stride of the partial lists)
+  int64_t n_kt;      // 256-key tiles
+  int64_t m_pad;     // padded query rows (row count of the partial lists)
   int num_kb;        // 64-wide k-blocks along d
   int k;             // kept per row
-  int n_qt;          // query tiles
+  int n_qt;          // 256-row pair query tiles
   int n_split;       // key-range splits
-  float* ws_vals;    // [n_split][k][m_pad] raw scores
-  int32_t* ws_idx;   // [n_split][k][m_pad] local key indices
+  int32_t* row_bound;  // [m_pad] shared admission bound per query row (ordered_int image)
+  float* ws_vals;    // [n_split][m_pad][k] raw scores, sorted best first
+  int32_t* ws_idx;   // [n_split][m_pad][k] local key indices
   int* status;       // device status word
 };
 
 template <int KCAP>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     score_topk_kernel(const __grid_constant__ CUtensorMap tmap_q,
                       const __grid_constant__ CUtensorMap tmap_k, const TopkKernelArgs a) {
   using C = TopkCfg<KCAP>;
@@ -84,16 +124,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
   uint8_t* smem = smem_raw + (base - raw_addr);
 
-  const uint32_t sA0 = base;               // stage s query tile at sA0 + s * kStageBytes
-  const uint32_t sB0 = base + C::kStageA;  // stage s key tile   at sB0 + s * kStageBytes
+  const uint32_t sA0 = base;               // stage s query rows at sA0 + s * kStageBytes
+  const uint32_t sB0 = base + C::kStageA;  // stage s keys       at sB0 + s * kStageBytes
   float* heap_s = reinterpret_cast<float*>(smem + S * C::kStageBytes);
   int32_t* heap_i = reinterpret_cast<int32_t*>(smem + S * C::kStageBytes + KCAP * kTileM * 4);
   uint8_t* bar_area = smem + S * C::kStageBytes + C::kHeapBytes;
   const uint32_t bar0 = smem_u32(bar_area);
-  auto full_bar = [&](int s) { return bar0 + 8u * s; };
-  auto empty_bar = [&](int s) { return bar0 + 8u * (S + s); };
-  auto tfull_bar = [&](int acc) { return bar0 + 8u * (2 * S + acc); };
-  auto tempty_bar = [&](int acc) { return bar0 + 8u * (2 * S + 2 + acc); };
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };             // leader: TMA bytes, both CTAs
+  auto empty_bar = [&](int s) { return bar0 + 8u * (S + s); };      // each: stage free again
+  auto tfull_bar = [&](int acc) { return bar0 + 8u * (2 * S + acc); };       // each: acc ready
+  auto tempty_bar = [&](int acc) { return bar0 + 8u * (2 * S + 2 + acc); };  // leader: 8 warps
   const uint32_t drain_bar = bar0 + 8u * (2 * S + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_area + 8 * (2 * S + 5));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -102,13 +142,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t cta = cluster_cta_rank();  // 0 = leader (issues the MMAs), 1 = peer
+  const bool leader = cta == 0;
 
-  const int unit = blockIdx.x;
-  const int qt = unit % a.n_qt;
-  const int split = unit / a.n_qt;
+  const int pair = blockIdx.x >> 1;
+  const int qt = pair % a.n_qt;
+  const int split = pair / a.n_qt;
   const int64_t kt_begin = static_cast<int64_t>(split) * a.n_kt / a.n_split;
   const int64_t kt_end = static_cast<int64_t>(split + 1) * a.n_kt / a.n_split;
   const int n_tiles = static_cast<int>(kt_end - kt_begin);
+  const int32_t row0 = qt * kPairRows + static_cast<int32_t>(cta) * kTileM;  // this CTA's rows
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -117,7 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int acc = 0; acc < 2; ++acc) {
       mbar_init(tfull_bar(acc), 1);
-      mbar_init(tempty_bar(acc), 4);
+      mbar_init(tempty_bar(acc), 8);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -128,11 +171,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmap_k);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), 2 * kTileN);
-    tmem_relinquish();
+    tmem_alloc_pair(smem_u32(tmem_slot), 2 * kTileN);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated in both
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -144,7 +187,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int it = 0;
       bool ok = true;
       for (int t = 0; t < n_tiles && ok; ++t) {
-        const int32_t krow = static_cast<int32_t>((kt_begin + t) * kTileN);
+        const int32_t krow =
+            static_cast<int32_t>((kt_begin + t) * kTileN) + static_cast<int32_t>(cta) * kKeysPerCta;
         for (int kb = 0; kb < a.num_kb; ++kb, ++it) {
           const int s = it % S;
           const uint32_t r = static_cast<uint32_t>(it / S);
@@ -152,30 +196,31 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(full_bar(s), C::kStageBytes);
-          tma_load_2d(sA0 + s * C::kStageBytes, &tmap_q, full_bar(s), kb * kTileK, qt * kTileM,
-                      pol_q);
-          tma_load_2d(sB0 + s * C::kStageBytes, &tmap_k, full_bar(s), kb * kTileK, krow, pol_k);
+          // The leader expects the bytes of both CTAs on its own barrier.
+          if (leader) mbar_arrive_expect_tx(full_bar(s), 2 * C::kStageBytes);
+          const uint32_t lead_full = map_to_cta(full_bar(s), 0);
+          tma_load_2d_pair(sA0 + s * C::kStageBytes, &tmap_q, lead_full, kb * kTileK, row0, pol_q);
+          tma_load_2d_pair(sB0 + s * C::kStageBytes, &tmap_k, lead_full, kb * kTileK, krow, pol_k);
         }
       }
       *n_issued = it;
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ UMMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16_f32(kTileM, kTileN);
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16_f32(kPairRows, kTileN);
       int it = 0;
       bool ok = true;
       for (int t = 0; t < n_tiles && ok; ++t) {
         const int acc = t & 1;
         const uint32_t use = static_cast<uint32_t>(t >> 1);
-        if (!mbar_wait(tempty_bar(acc), (use & 1u) ^ 1u, a.status, abort_flag)) break;
+        if (!mbar_wait_cluster(tempty_bar(acc), (use & 1u) ^ 1u, a.status, abort_flag)) break;
         tc_fence_after();
         const uint32_t tmem_d = tmem_base + static_cast<uint32_t>(acc * kTileN);
         for (int kb = 0; kb < a.num_kb; ++kb, ++it) {
           const int s = it % S;
           const uint32_t r = static_cast<uint32_t>(it / S);
-          if (!mbar_wait(full_bar(s), r & 1u, a.status, abort_flag)) {
+          if (!mbar_wait_cluster(full_bar(s), r & 1u, a.status, abort_flag)) {
             ok = false;
             break;
           }
@@ -185,24 +230,36 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kTileK / 16; ++kk) {
             // +32 bytes along K inside the swizzled 128-byte row = +2 in the address field
-            umma_bf16_ss(tmem_d, ad + 2u * kk, bd + 2u * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+            umma_bf16_ss_pair(tmem_d, ad + 2u * kk, bd + 2u * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
           }
-          umma_commit(empty_bar(s));
+          umma_commit_pair_all(empty_bar(s), 0x3);  // frees stage s in both CTAs
         }
-        if (ok) umma_commit(tfull_bar(acc));
+        if (ok) umma_commit_pair_all(tfull_bar(acc), 0x3);
       }
       *n_consumed = it;
-      // All MMAs this thread issued must finish before TMEM is released.
-      umma_commit(drain_bar);
+      // Every MMA must finish (it reads both CTAs' shared memory and writes
+      // both TMEMs) before either CTA releases them.
+      umma_commit_pair_local(drain_bar);
       mbar_wait(drain_bar, 0u, a.status, nullptr);
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // Admission: a score enters this unit's heap when it beats the heap root
+    // (theta_loc; strict, since indices only grow inside a unit) AND is not
+    // below the row's shared bound.  The bound is the best k-th score any unit
+    // of the same query row has published; the union's k-th best is at least
+    // that, so lower scores can never reach the final top-k.  Scores equal to
+    // the bound stay admissible (they may win an index tie).
     const int ew = warp & 3;           // TMEM lane quarter this warp may access
-    const int row = ew * 32 + lane;    // query row within the tile
+    const int row = ew * 32 + lane;    // query row within this CTA's 128
     const SmemHeap heap{heap_s, heap_i, kTileM, a.k};
     heap.init(row);
-    float theta = -INFINITY;           // score of the heap root (worst kept)
+    int32_t* bound_ptr = a.row_bound + row0 + row;
+    float theta_loc = -INFINITY;       // score of the heap root (worst kept)
+    float bound = ordered_float(__ldcg(bound_ptr));
+    float cut = fmaxf(theta_loc, float_below(bound));  // admit iff score > cut
+    const uint32_t lead_tempty0 = map_to_cta(tempty_bar(0), 0);
+    const uint32_t lead_tempty1 = map_to_cta(tempty_bar(1), 0);
     for (int t = 0; t < n_tiles; ++t) {
       const int acc = t & 1;
       const uint32_t use = static_cast<uint32_t>(t >> 1);
@@ -215,48 +272,72 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < valid; c += 32) {
         float v[32];
         tmem_ld_32x32b_x32_sync(taddr + c, v);
+        const int rem = valid - c;
+        // Warp-wide prefilter: skip the chunk when no lane has a score above its cut.
+        float mx[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) mx[i] = fmaxf(v[2 * i], v[2 * i + 1]);
+#pragma unroll
+        for (int w2 = 8; w2 > 0; w2 >>= 1)
+#pragma unroll
+          for (int i = 0; i < w2; ++i) mx[i] = fmaxf(mx[i], mx[i + w2]);
+        const bool maybe = rem < 32 || mx[0] > cut;
+        if (!__any_sync(0xffffffffu, maybe)) continue;
         uint32_t m = 0;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) m |= (v[j] > theta ? 1u : 0u) << j;
-        const int rem = valid - c;
+        for (int j = 0; j < 32; ++j) m |= (v[j] > cut ? 1u : 0u) << j;
         if (rem < 32) m &= (1u << rem) - 1u;
-        uint32_t wm = __reduce_or_sync(0xffffffffu, m);
-        while (wm) {
-          const int j = __ffs(wm) - 1;
-          wm &= wm - 1u;
-          // Re-read column j for all 32 rows (warp-collective) rather than
-          // index the register array dynamically.
-          const float s = tmem_ld_32x32b_x1_sync(taddr + c + j);
-          if (((m >> j) & 1u) && s > theta) {
+        // Each lane walks only its own candidates; the warp runs as many
+        // iterations as its busiest lane, not the union over lanes.
+        while (m) {
+          const int j = __ffs(m) - 1;
+          m &= m - 1u;
+          const float s = pick32(v, j);
+          if (s > cut) {
             heap.replace_root(row, s, static_cast<int32_t>(n0 + c + j));
-            theta = heap.S(0, row);
+            theta_loc = heap.S(0, row);
+            cut = fmaxf(theta_loc, float_below(bound));
           }
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(tempty_bar(acc));
+      if (lane == 0) mbar_arrive_cluster(acc ? lead_tempty1 : lead_tempty0);
+      // Publish this unit's k-th best and pick up the row's best bound.
+      if (theta_loc > -INFINITY) {
+        const int32_t mine = ordered_int(theta_loc);
+        const int32_t seen = atomicMax(bound_ptr, mine);
+        bound = ordered_float(max(seen, mine));
+        cut = fmaxf(theta_loc, float_below(bound));
+      }
     }
-    // Flush this unit's partial list: [split][pos][row], coalesced across rows.
-    const int64_t col = static_cast<int64_t>(qt) * kTileM + row;
+    // Flush this unit's list for the row, best first: [split][row][pos].
+    heap.sort_best_first(row);
+    const int64_t o = (static_cast<int64_t>(split) * a.m_pad + row0 + row) * a.k;
     for (int p = 0; p < a.k; ++p) {
-      const int64_t o = (static_cast<int64_t>(split) * a.k + p) * a.m_pad + col;
-      a.ws_vals[o] = heap.S(p, row);
-      a.ws_idx[o] = heap.I(p, row);
+      a.ws_vals[o + p] = heap.S(p, row);
+      a.ws_idx[o + p] = heap.I(p, row);
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (leader && threadIdx.x == 0) {
     // Loads issued but never consumed (only after an abort) must land before exit.
     for (int i = *n_consumed; i < *n_issued; ++i)
-      mbar_wait(full_bar(i % S), static_cast<uint32_t>(i / S) & 1u, a.status, nullptr);
+      mbar_wait_cluster(full_bar(i % S), static_cast<uint32_t>(i / S) & 1u, a.status, nullptr);
   }
+  tc_fence_before();
+  cluster_sync();  // the leader's MMAs are done; the peer may release its memory
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 2 * kTileN);
+    tmem_dealloc_pair(tmem_base, 2 * kTileN);
   }
+}
+
+__global__ void fill_i32_kernel(int32_t* p, int64_t n, int32_t v) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) p[i] = v;
 }
 
 // ---------------------------------------------------------------- host side
@@ -308,7 +389,7 @@ cudaError_t launch_variant(const ScoreTopkPlan& p, const CUtensorMap& mq, const 
                            const TopkKernelArgs& args, cudaStream_t stream) {
   cudaError_t e = configure_once<KCAP>();
   if (e != cudaSuccess) return e;
-  const unsigned grid = static_cast<unsigned>(p.n_qt) * static_cast<unsigned>(p.n_split);
+  const unsigned grid = 2u * static_cast<unsigned>(p.n_qt) * static_cast<unsigned>(p.n_split);
   score_topk_kernel<KCAP><<<grid, kThreads, TopkCfg<KCAP>::kSmemBytes, stream>>>(mq, mk, args);
   return cudaGetLastError();
 }
@@ -328,7 +409,7 @@ int device_sm_count() {
 }
 
 bool plan_score_topk(int64_t M, int64_t N, int d, int k, int num_sms, ScoreTopkPlan* plan) {
-  if (M <= 0 || N <= 0 || d <= 0 || k <= 0 || num_sms <= 0) return false;
+  if (M <= 0 || N <= 0 || d <= 0 || k <= 0 || num_sms <= 1) return false;
   ScoreTopkPlan p;
   p.M = M;
   p.N = N;
@@ -336,22 +417,26 @@ bool plan_score_topk(int64_t M, int64_t N, int d, int k, int num_sms, ScoreTopkP
   p.k = k;
   p.kcap = k <= 16 ? 16 : k <= 32 ? 32 : k <= 64 ? 64 : k <= 128 ? 128 : 0;
   if (p.kcap == 0) return false;
-  const int64_t n_qt = (M + kTileM - 1) / kTileM;
+  const int64_t n_qt = (M + kPairRows - 1) / kPairRows;
   if (n_qt > (1 << 24)) return false;
   p.n_qt = static_cast<int>(n_qt);
   p.n_kt = (N + kTileN - 1) / kTileN;
   p.num_kb = (d + kTileK - 1) / kTileK;
-  p.m_pad = n_qt * kTileM;
+  p.m_pad = n_qt * kPairRows;
   // Choose the number of key-range splits: minimise the modelled makespan
-  // waves * (tiles per unit + per-unit overhead), one CTA per SM.
-  const double unit_overhead_tiles = 1.5;
+  // waves * (tiles per unit + per-unit overhead), one CTA pair per two SMs.
+  // Per-unit overhead in tile-times: pipeline fill/drain, the heap warm-up at
+  // the start of every unit (the first tiles insert most candidates), the
+  // sorted flush and one more list for the split merge.
+  const double unit_overhead_tiles = 8.0;
+  const int64_t pairs = num_sms / 2;
   int best_s = 1;
   double best_cost = 1e300;
-  const int64_t s_max = std::min<int64_t>(p.n_kt, 4096);
+  const int64_t s_max = std::min<int64_t>(p.n_kt, kMaxSplits);
   for (int64_t s = 1; s <= s_max; ++s) {
     const int64_t units = n_qt * s;
-    if (units > (1ll << 31) - 1) break;
-    const int64_t waves = (units + num_sms - 1) / num_sms;
+    if (2 * units > (1ll << 31) - 1) break;
+    const int64_t waves = (units + pairs - 1) / pairs;
     const int64_t tiles_per_unit = (p.n_kt + s - 1) / s;
     const double cost =
         static_cast<double>(waves) * (static_cast<double>(tiles_per_unit) + unit_overhead_tiles);
@@ -361,8 +446,9 @@ bool plan_score_topk(int64_t M, int64_t N, int d, int k, int num_sms, ScoreTopkP
     }
   }
   p.n_split = best_s;
-  p.ws_bytes = kStatusBytes + static_cast<size_t>(p.n_split) * static_cast<size_t>(k) *
-                                  static_cast<size_t>(p.m_pad) * 8u;
+  p.ws_bytes = kStatusBytes + static_cast<size_t>(p.m_pad) * 4u +
+               static_cast<size_t>(p.n_split) * static_cast<size_t>(k) *
+                   static_cast<size_t>(p.m_pad) * 8u;
   *plan = p;
   return true;
 }
@@ -375,7 +461,7 @@ cudaError_t launch_score_topk(const ScoreTopkPlan& p, const void* q, int64_t ldq
   if (!make_bf16_tile_map(&mq, q, static_cast<uint64_t>(p.d), static_cast<uint64_t>(p.M),
                           static_cast<uint64_t>(ldq), kTileK, kTileM) ||
       !make_bf16_tile_map(&mk, keys, static_cast<uint64_t>(p.d), static_cast<uint64_t>(p.N),
-                          static_cast<uint64_t>(ldk), kTileK, kTileN)) {
+                          static_cast<uint64_t>(ldk), kTileK, kKeysPerCta)) {
     if (err_detail) *err_detail = "cuTensorMapEncodeTiled failed for the query or key tensor";
     return cudaErrorInvalidValue;
   }
@@ -390,10 +476,18 @@ cudaError_t launch_score_topk(const ScoreTopkPlan& p, const void* q, int64_t ldq
   args.n_split = p.n_split;
   args.status = reinterpret_cast<int*>(wsb);
   const size_t list_elems = static_cast<size_t>(p.n_split) * p.k * p.m_pad;
-  args.ws_vals = reinterpret_cast<float*>(wsb + kStatusBytes);
-  args.ws_idx = reinterpret_cast<int32_t*>(wsb + kStatusBytes + list_elems * 4);
+  const size_t bound_bytes = static_cast<size_t>(p.m_pad) * 4u;
+  args.row_bound = reinterpret_cast<int32_t*>(wsb + kStatusBytes);
+  args.ws_vals = reinterpret_cast<float*>(wsb + kStatusBytes + bound_bytes);
+  args.ws_idx = reinterpret_cast<int32_t*>(wsb + kStatusBytes + bound_bytes + list_elems * 4);
 
   cudaError_t e = cudaMemsetAsync(ws, 0, sizeof(int), stream);
+  if (e != cudaSuccess) return e;
+  // The ordered image of -inf: "no bound yet" (every score is admissible).
+  constexpr int32_t kImageNegInf = static_cast<int32_t>(0xFF800000u ^ 0x7FFFFFFFu);
+  fill_i32_kernel<<<static_cast<unsigned>((p.m_pad + 255) / 256), 256, 0, stream>>>(
+      args.row_bound, p.m_pad, kImageNegInf);
+  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   switch (p.kcap) {
     case 16: e = launch_variant<16>(p, mq, mk, args, stream); break;
@@ -404,7 +498,7 @@ cudaError_t launch_score_topk(const ScoreTopkPlan& p, const void* q, int64_t ldq
   }
   if (e != cudaSuccess) return e;
   return launch_merge_topk(args.ws_vals, args.ws_idx, p.n_split, p.k,
-                           static_cast<int64_t>(p.k) * p.m_pad, p.m_pad, 1, p.M, p.k,
+                           static_cast<int64_t>(p.k) * p.m_pad, 1, p.k, p.M, p.k,
                            /*transform=*/1, lambda_sharp, tau, T, use_sigmoid, idx_offset, out_vals,
                            out_idx, stream);
 }

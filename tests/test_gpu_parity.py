@@ -259,3 +259,21 @@ def test_op_at_scale_properties(lib):
     # value side on the sampled rows
     want = torch.einsum("mk,mkd->md", alpha[rows].double(), values[ti[rows].long()].double())
     assert O.compare_rows(out[rows].cpu().numpy(), want.cpu().numpy(), rtol=RTOL) == []
+
+
+@pytest.mark.parametrize("M,N,d,k", [(300, 40000, 64, 16), (512, 70000, 128, 64), (100, 9000, 32, 128)])
+def test_exact_ties_across_key_splits(lib, M, N, d, k):
+    """Integer-valued inputs make every score exact, and duplicated key rows
+    spread over the whole pool create ties between key-range splits; the
+    shared admission bound must still return exactly lax.top_k's indices
+    (lower index first among equal scores)."""
+    rng = np.random.default_rng(M + N + k)
+    q = rng.integers(-2, 3, size=(M, d)).astype(np.float32)
+    base = rng.integers(-2, 3, size=(N // 8, d)).astype(np.float32)
+    keys = base[rng.integers(0, base.shape[0], size=N)]
+    T = 64.0  # keeps exp(s / T) finite and exactly ordered
+    v, i = lib.tiled_topk_fused(from_f32(q), from_f32(keys), k, 1.0, 0.0, T, False)
+    torch.cuda.synchronize()
+    rv, ri = O.tiled_topk(q, keys, k, 1.0, 0.0, T, False)
+    np.testing.assert_array_equal(i.cpu().numpy(), ri)
+    np.testing.assert_allclose(v.cpu().numpy(), rv, rtol=1e-6)
