@@ -44,6 +44,14 @@ dwa_status ok() {
 
 }  // namespace
 
+namespace dwa {
+// Lets other translation units of the library report through dwa_last_error().
+dwa_status record_error(dwa_status s, const char* msg) {
+  g_last_error = msg ? msg : "";
+  return s;
+}
+}  // namespace dwa
+
 extern "C" {
 
 int32_t dwa_abi_version(void) { return DWA_ABI_VERSION; }

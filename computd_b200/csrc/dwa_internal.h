@@ -32,6 +32,9 @@ struct ScoreTopkPlan {
   size_t ws_bytes = 0; // status block + per-row bounds + partial lists
 };
 
+// Sets the thread-local message dwa_last_error() returns; returns `s`.
+int32_t record_error(int32_t s, const char* msg);
+
 // Returns false when the shape is outside what the kernel supports.
 bool plan_score_topk(int64_t M, int64_t N, int d, int k, int num_sms, ScoreTopkPlan* plan);
 

@@ -96,6 +96,28 @@ DWA_API dwa_status dwa_score_topk(const void* q, int64_t M, int64_t ldq,
                           void* ws, size_t ws_bytes, dwa_stream_t stream);
 
 /*
+ * dwa_score_topk without a caller workspace, for callers that cannot allocate
+ * device memory (e.g. a plugin inside a framework whose allocator already owns
+ * most of the GPU, or a binding with no scratch-buffer argument).  No
+ * counterpart in the reference (its JAX path lets XLA allocate everything).
+ *
+ * Same arguments, validation, kernels and results as dwa_score_topk; the
+ * workspace is a 128 MiB scratch array built into the library, held in device
+ * memory by every GPU this entry point runs on until the process exits.
+ * Shapes needing more than that return DWA_ERR_UNSUPPORTED_SHAPE (nothing
+ * launched).  The first call on a device looks up the scratch address with
+ * that device current; make it before any stream capture.  Every call on a
+ * device shares the scratch: calls must be stream-ordered, overlapping calls
+ * race.  Allocates nothing.
+ */
+DWA_API dwa_status dwa_score_topk_noalloc(const void* q, int64_t M, int64_t ldq,
+                          const void* keys, int64_t N_local, int64_t ldk,
+                          int32_t d, int32_t k,
+                          float lambda_sharp, float tau, float T, int32_t use_sigmoid,
+                          int64_t idx_offset,
+                          float* out_vals, int32_t* out_idx, dwa_stream_t stream);
+
+/*
  * Merge P per-shard candidate lists into the global top-k.
  * Replaces the all_gather transpose/reshape + second top_k + take of
  * _chip_topk (src/model/retrieval.py:295-302).
