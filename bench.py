@@ -44,6 +44,15 @@ WORKLOADS = {
     "profile_small": dict(M=8192, N=131072, d=1024, k=64, use_sigmoid=False,
                           desc="profiling case: queries [8192,1024]; pool 131,072x1024 (256 MiB "
                                "keys, larger than L2); top-k 64"),
+    "lm_small_layer": dict(M=4096, N=65536, d=384, k=32, use_sigmoid=False,
+                           desc="small DWA LM, one layer's retrieval: 16x256 tokens against a "
+                                "65,536x384 pool, top-k 32"),
+    "lm1b_shard8": dict(M=16384, N=524288, d=2048, k=64, use_sigmoid=False,
+                        desc="1B-scale DWA LM, one layer's retrieval on one GPU of 8: 8x2048 "
+                             "tokens against a 524,288x2048 shard (4,194,304 rows / 8), top-k 64"),
+    "lm7b_shard8": dict(M=16384, N=2097152, d=4096, k=128, use_sigmoid=False,
+                        desc="7B-scale DWA LM, one layer's retrieval on one GPU of 8: 4x4096 "
+                             "tokens against a 2,097,152x4096 shard (16,777,216 rows / 8), top-k 128"),
     "c1_op": dict(M=2048, N=16384, d=128, k=16, use_sigmoid=False,
                   desc="queries [2048,128]; pool [16384,128]; top-k 16; softmax-weighted sum"),
 }

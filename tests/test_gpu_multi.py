@@ -1,0 +1,102 @@
+"""Multi-GPU parity: the row-sharded path (one process per GPU, NCCL) returns
+the same top-k and value sums as the single-GPU path on the same pool.
+
+Runs only when 2 or more CUDA devices are visible.  Each rank generates its
+own shard with the counter-based generator, so every shard count sees the
+same pool; rank 0 also runs the unsharded retrieval on its GPU as the
+reference and compares.  The process group has a short timeout, so a rank
+that fails ends the others' next collective with an error instead of a hang.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    import computd_b200 as cb
+    from oracle import dwa_oracle as O
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        M, N, d, k = 1000, 96 * 1024, 256, 32
+        spec = cb.ShardSpec(N, rank, world)
+        keys = cb.new_normal(spec.n_local, d, seed=2, stddev=d ** -0.5, row_offset=spec.row_begin,
+                             device=dev)
+        values = cb.new_normal(spec.n_local, d, seed=3, row_offset=spec.row_begin, device=dev)
+        queries = cb.new_normal(M, d, seed=4, device=dev)
+        r = cb.Retriever(keys, values, M, k, lambda_sharp=3.0, tau=0.5, T=0.8, use_sigmoid=True)
+        out, alpha, tv, ti = r(queries)
+        # chip_topk (the shard_map body) must agree with the Retriever
+        cv, ci = cb.chip_topk(queries, keys, k, 3.0, 0.5, 0.8, True)
+        torch.cuda.synchronize()
+        same_chip = bool(torch.equal(ci, ti))
+        msg = "ok"
+        if rank == 0:
+            full_k = cb.new_normal(N, d, seed=2, stddev=d ** -0.5, device=dev)
+            full_v = cb.new_normal(N, d, seed=3, device=dev)
+            r1 = cb.Retriever(full_k, full_v, M, k, lambda_sharp=3.0, tau=0.5, T=0.8,
+                              use_sigmoid=True, group=dist.new_group([0]))
+            o1, a1, v1, i1 = r1(queries)
+            torch.cuda.synchronize()
+            qn = queries.float().cpu().numpy()
+            kn = full_k.float().cpu().numpy()
+            errs = O.compare_topk(tv.cpu().numpy(), ti.cpu().numpy(), v1.cpu().numpy(),
+                                  i1.cpu().numpy(), qn, kn, 3.0, 0.5, 0.8, True, rtol=1e-2)
+            if errs:
+                msg = "; ".join(errs)
+            elif not torch.equal(ti, i1):
+                msg = "sharded indices differ from the single-GPU indices"
+            else:
+                errs = O.compare_rows(out.cpu().numpy(), o1.cpu().numpy(), rtol=1e-2)
+                if errs:
+                    msg = "; ".join(errs)
+        else:
+            dist.new_group([0])  # every rank takes part in group creation
+        q.put((rank, same_chip, msg, r.status()))
+        dist.barrier(device_ids=[rank])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sharded_matches_single_gpu(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, same_chip, msg, status in sorted(results):
+        assert status == 0, f"rank {rank}: device status {status}"
+        assert same_chip, f"rank {rank}: chip_topk differs from Retriever.topk"
+        assert msg == "ok", f"rank {rank}: {msg}"
