@@ -12,7 +12,7 @@
 #include <cstring>
 #include <string>
 
-#include "../../include/dwa_retrieval.h"
+#include "dwa_retrieval.h"
 #include "dwa_internal.h"
 
 namespace {

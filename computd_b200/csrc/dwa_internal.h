@@ -28,6 +28,7 @@ struct ScoreTopkPlan {
   int n_split = 0;     // key-range splits per query tile
   int num_kb = 0;      // k-blocks of 64 along d
   int kcap = 0;        // heap capacity variant (16, 32, 64, 128)
+  int nwg = 1;         // epilogue warpgroups (1 or 2), one partial list each per unit
   int64_t m_pad = 0;   // n_qt * 256
   size_t ws_bytes = 0; // status block + per-row bounds + partial lists
 };

@@ -47,20 +47,23 @@ namespace dwa {
 
 namespace {
 
-constexpr int kThreads = 192;
+// 2 non-epilogue warps (TMA, MMA) + NWG epilogue warpgroups of 4 warps.
+constexpr int threads_for(int nwg) { return 64 + 128 * nwg; }
 constexpr int kMaxDynSmem = 232448;  // 227 KB opt-in limit on sm_100
 constexpr int kPairRows = 2 * kTileM;      // 256 query rows per CTA pair
 constexpr int kKeysPerCta = kTileN / 2;    // 128 keys of each 256-key tile per CTA
 
-template <int KCAP>
+template <int KCAP, int NWG>
 struct TopkCfg {
   static constexpr int kStageA = kTileM * kTileK * 2;       // 16 KB: this CTA's query rows
   static constexpr int kStageB = kKeysPerCta * kTileK * 2;  // 16 KB: this CTA's half of the keys
   static constexpr int kStageBytes = kStageA + kStageB;
-  static constexpr int kHeapBytes = KCAP * kTileM * 8;
+  // k <= 64 keeps its lists in registers; k = 128 uses one shared-memory heap
+  // per row per warpgroup
+  static constexpr int kHeapBytes = KCAP > 64 ? KCAP * kTileM * 8 * NWG : 0;
   static constexpr int kBarBytes = 256;
   static constexpr int kStagesFit = (kMaxDynSmem - 1024 - kHeapBytes - kBarBytes) / kStageBytes;
-  static constexpr int kStages = kStagesFit > 6 ? 6 : kStagesFit;
+  static constexpr int kStages = kStagesFit > 7 ? 7 : kStagesFit;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kHeapBytes + kBarBytes;
   static_assert(kStages >= 2, "pipeline needs at least two stages");
   static_assert(kSmemBytes <= kMaxDynSmem, "shared memory budget exceeded");
@@ -80,6 +83,82 @@ __device__ __forceinline__ float pick32(const float (&v)[32], int j) {
   for (int i = 0; i < 2; ++i) d[i] = (j & 8) ? c[2 * i + 1] : c[2 * i];
   return (j & 16) ? d[1] : d[0];
 }
+
+// Per-row top-k of one unit held in registers, sorted best first, for
+// k <= KCAP <= 64.  Slots [0, KCAP - k) are pinned at +inf so the admission
+// threshold is always the static slot KCAP - 1.  Insertion is a branch-free
+// network: every slot takes its own value, the new entry or its upper
+// neighbour's old value, so all slots update in parallel from old values and
+// nothing touches memory (a shared-memory heap competes with the tensor core
+// for shared-memory bandwidth and measured ~900 cycles per insert).
+template <int KCAP>
+struct RegTopK {
+  float s[KCAP];
+  int32_t i[KCAP];
+  __device__ __forceinline__ void init(int k) {
+#pragma unroll
+    for (int p = 0; p < KCAP; ++p) {
+      s[p] = p < KCAP - k ? INFINITY : -INFINITY;
+      i[p] = kSentinelIdx;
+    }
+  }
+  __device__ __forceinline__ float worst() const { return s[KCAP - 1]; }
+  // (x, xi) must rank above the worst entry; inside a unit indices only
+  // grow, so "above" is a strict score comparison and equal scores keep the
+  // older (lower) index first.
+  __device__ __forceinline__ void insert(float x, int32_t xi) {
+    bool hi = true;
+#pragma unroll
+    for (int p = KCAP - 1; p >= 1; --p) {
+      const bool lo = x > s[p - 1];
+      const float ns = lo ? s[p - 1] : (hi ? x : s[p]);
+      const int32_t ni = lo ? i[p - 1] : (hi ? xi : i[p]);
+      s[p] = ns;
+      i[p] = ni;
+      hi = lo;
+    }
+    if (hi) {
+      s[0] = x;
+      i[0] = xi;
+    }
+  }
+  __device__ __forceinline__ void write_out(float* vs, int32_t* is, int k) const {
+#pragma unroll
+    for (int p = 0; p < KCAP; ++p)
+      if (p >= KCAP - k) {
+        vs[p - (KCAP - k)] = s[p];
+        is[p - (KCAP - k)] = i[p];
+      }
+  }
+};
+
+// Per-row top-k in a shared-memory heap, for KCAP = 128 (too many registers).
+struct HeapTopK {
+  SmemHeap heap;
+  int row;
+  __device__ __forceinline__ void init(int) { heap.init(row); }
+  __device__ __forceinline__ float worst() const { return heap.score(0, row); }
+  __device__ __forceinline__ void insert(float x, int32_t xi) { heap.replace_root(row, x, xi); }
+  __device__ __forceinline__ void write_out(float* vs, int32_t* is, int k) const {
+    heap.sort_best_first(row);
+    for (int p = 0; p < k; ++p) {
+      float hs;
+      int32_t hi;
+      heap.load(p, row, hs, hi);
+      vs[p] = hs;
+      is[p] = hi;
+    }
+  }
+};
+
+template <int KCAP>
+struct TopKFor {
+  using type = RegTopK<KCAP>;
+};
+template <>
+struct TopKFor<128> {
+  using type = HeapTopK;
+};
 
 // Order-preserving map float -> int32 (signed integer order = float order),
 // so atomicMax on the image maximises the float.
@@ -107,16 +186,16 @@ struct TopkKernelArgs {
   int n_qt;          // 256-row pair query tiles
   int n_split;       // key-range splits
   int32_t* row_bound;  // [m_pad] shared admission bound per query row (ordered_int image)
-  float* ws_vals;    // [n_split][m_pad][k] raw scores, sorted best first
-  int32_t* ws_idx;   // [n_split][m_pad][k] local key indices
+  float* ws_vals;    // [n_split * NWG][m_pad][k] raw scores, sorted best first
+  int32_t* ws_idx;   // [n_split * NWG][m_pad][k] local key indices
   int* status;       // device status word
 };
 
-template <int KCAP>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+template <int KCAP, int NWG>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
     score_topk_kernel(const __grid_constant__ CUtensorMap tmap_q,
                       const __grid_constant__ CUtensorMap tmap_k, const TopkKernelArgs a) {
-  using C = TopkCfg<KCAP>;
+  using C = TopkCfg<KCAP, NWG>;
   constexpr int S = C::kStages;
 
   extern __shared__ uint8_t smem_raw[];
@@ -126,8 +205,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
   const uint32_t sA0 = base;               // stage s query rows at sA0 + s * kStageBytes
   const uint32_t sB0 = base + C::kStageA;  // stage s keys       at sB0 + s * kStageBytes
-  float* heap_s = reinterpret_cast<float*>(smem + S * C::kStageBytes);
-  int32_t* heap_i = reinterpret_cast<int32_t*>(smem + S * C::kStageBytes + KCAP * kTileM * 4);
+  // heaps: warpgroup g's 8-byte entries at heap0 + g * KCAP * 128 * 8
+  const uint32_t heap0 = base + S * C::kStageBytes;
   uint8_t* bar_area = smem + S * C::kStageBytes + C::kHeapBytes;
   const uint32_t bar0 = smem_u32(bar_area);
   auto full_bar = [&](int s) { return bar0 + 8u * s; };             // leader: TMA bytes, both CTAs
@@ -250,17 +329,63 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // of the same query row has published; the union's k-th best is at least
     // that, so lower scores can never reach the final top-k.  Scores equal to
     // the bound stay admissible (they may win an index tie).
+    // With two warpgroups, warpgroup g takes the tiles t = g, g + 2, ...: it
+    // owns TMEM accumulator buffer g and has two MMA tile-times per tile.
+    const int g = (warp - 2) >> 2;     // epilogue warpgroup
     const int ew = warp & 3;           // TMEM lane quarter this warp may access
     const int row = ew * 32 + lane;    // query row within this CTA's 128
-    const SmemHeap heap{heap_s, heap_i, kTileM, a.k};
-    heap.init(row);
+    typename TopKFor<KCAP>::type topk;
+    if constexpr (KCAP > 64) {
+      topk.heap = SmemHeap{heap0 + static_cast<uint32_t>(g * KCAP * kTileM * 8), kTileM, a.k};
+      topk.row = row;
+    }
+    topk.init(a.k);
     int32_t* bound_ptr = a.row_bound + row0 + row;
-    float theta_loc = -INFINITY;       // score of the heap root (worst kept)
+    float theta_loc = -INFINITY;       // worst kept score of this unit
     float bound = ordered_float(__ldcg(bound_ptr));
     float cut = fmaxf(theta_loc, float_below(bound));  // admit iff score > cut
+    // Scan 32 scores of this row (columns col0 .. col0 + min(rem, 32) - 1).
+    auto scan_chunk = [&](const uint32_t (&r)[32], int rem, int32_t col0) {
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+      // Warp-wide prefilter: skip the chunk when no lane has a score above its cut.
+      float mx[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) mx[i] = fmaxf(v[2 * i], v[2 * i + 1]);
+#pragma unroll
+      for (int w2 = 8; w2 > 0; w2 >>= 1)
+#pragma unroll
+        for (int i = 0; i < w2; ++i) mx[i] = fmaxf(mx[i], mx[i + w2]);
+      const bool maybe = rem < 32 || mx[0] > cut;
+      if (!__any_sync(0xffffffffu, maybe)) return;
+      // candidate bit mask, combined as a tree (short dependency chains)
+      uint32_t b[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        b[i] = (v[2 * i] > cut ? 1u : 0u) | (v[2 * i + 1] > cut ? 2u : 0u);
+#pragma unroll
+      for (int w2 = 8, sh = 2; w2 > 0; w2 >>= 1, sh <<= 1)
+#pragma unroll
+        for (int i = 0; i < w2; ++i) b[i] = b[2 * i] | (b[2 * i + 1] << sh);
+      uint32_t m = b[0];
+      if (rem < 32) m &= (1u << rem) - 1u;
+      // Each lane walks only its own candidates; the warp runs as many
+      // iterations as its busiest lane, not the union over lanes.
+      while (m) {
+        const int j = __ffs(m) - 1;
+        m &= m - 1u;
+        const float s = pick32(v, j);
+        if (s > cut) {
+          topk.insert(s, col0 + j);
+          theta_loc = topk.worst();
+          cut = fmaxf(theta_loc, float_below(bound));
+        }
+      }
+    };
     const uint32_t lead_tempty0 = map_to_cta(tempty_bar(0), 0);
     const uint32_t lead_tempty1 = map_to_cta(tempty_bar(1), 0);
-    for (int t = 0; t < n_tiles; ++t) {
+    for (int t = g; t < n_tiles; t += NWG) {
       const int acc = t & 1;
       const uint32_t use = static_cast<uint32_t>(t >> 1);
       if (!mbar_wait(tfull_bar(acc), use & 1u, a.status, abort_flag)) break;
@@ -269,35 +394,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int valid = static_cast<int>(min(static_cast<int64_t>(kTileN), a.N - n0));
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + static_cast<uint32_t>(acc * kTileN);
-      for (int c = 0; c < valid; c += 32) {
-        float v[32];
-        tmem_ld_32x32b_x32_sync(taddr + c, v);
-        const int rem = valid - c;
-        // Warp-wide prefilter: skip the chunk when no lane has a score above its cut.
-        float mx[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) mx[i] = fmaxf(v[2 * i], v[2 * i + 1]);
-#pragma unroll
-        for (int w2 = 8; w2 > 0; w2 >>= 1)
-#pragma unroll
-          for (int i = 0; i < w2; ++i) mx[i] = fmaxf(mx[i], mx[i + w2]);
-        const bool maybe = rem < 32 || mx[0] > cut;
-        if (!__any_sync(0xffffffffu, maybe)) continue;
-        uint32_t m = 0;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) m |= (v[j] > cut ? 1u : 0u) << j;
-        if (rem < 32) m &= (1u << rem) - 1u;
-        // Each lane walks only its own candidates; the warp runs as many
-        // iterations as its busiest lane, not the union over lanes.
-        while (m) {
-          const int j = __ffs(m) - 1;
-          m &= m - 1u;
-          const float s = pick32(v, j);
-          if (s > cut) {
-            heap.replace_root(row, s, static_cast<int32_t>(n0 + c + j));
-            theta_loc = heap.S(0, row);
-            cut = fmaxf(theta_loc, float_below(bound));
-          }
+      // Chunks of 32 columns, two register sets in flight: the TMEM load of the
+      // next chunk overlaps the scan of the current one.
+      uint32_t ra[32], rb[32];
+      tmem_ld_32x32b_x32_async(taddr, ra);
+      tmem_wait_ld_pin(ra);
+      for (int c = 0; c < valid; c += 64) {
+        const bool has_b = c + 32 < valid;   // warp-uniform
+        if (has_b) tmem_ld_32x32b_x32_async(taddr + c + 32, rb);
+        scan_chunk(ra, valid - c, static_cast<int32_t>(n0 + c));
+        if (has_b) {
+          tmem_wait_ld_pin(rb);
+          const bool has_next = c + 64 < valid;
+          if (has_next) tmem_ld_32x32b_x32_async(taddr + c + 64, ra);
+          scan_chunk(rb, valid - c - 32, static_cast<int32_t>(n0 + c + 32));
+          if (has_next) tmem_wait_ld_pin(ra);
         }
       }
       tc_fence_before();
@@ -311,13 +422,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         cut = fmaxf(theta_loc, float_below(bound));
       }
     }
-    // Flush this unit's list for the row, best first: [split][row][pos].
-    heap.sort_best_first(row);
-    const int64_t o = (static_cast<int64_t>(split) * a.m_pad + row0 + row) * a.k;
-    for (int p = 0; p < a.k; ++p) {
-      a.ws_vals[o + p] = heap.S(p, row);
-      a.ws_idx[o + p] = heap.I(p, row);
-    }
+    // Flush this unit's list for the row, best first: [split * NWG + g][row][pos].
+    const int64_t o = (static_cast<int64_t>(split * NWG + g) * a.m_pad + row0 + row) * a.k;
+    topk.write_out(a.ws_vals + o, a.ws_idx + o, a.k);
   }
 
   tc_fence_before();
@@ -370,7 +477,7 @@ bool make_bf16_tile_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint6
   return r == CUDA_SUCCESS;
 }
 
-template <int KCAP>
+template <int KCAP, int NWG>
 cudaError_t configure_once() {
   static std::atomic<uint64_t> done_mask{0};
   int dev = 0;
@@ -378,23 +485,28 @@ cudaError_t configure_once() {
   if (e != cudaSuccess) return e;
   const uint64_t bit = 1ull << (dev & 63);
   if (done_mask.load(std::memory_order_acquire) & bit) return cudaSuccess;
-  e = cudaFuncSetAttribute(score_topk_kernel<KCAP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           TopkCfg<KCAP>::kSmemBytes);
+  e = cudaFuncSetAttribute(score_topk_kernel<KCAP, NWG>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           TopkCfg<KCAP, NWG>::kSmemBytes);
   if (e == cudaSuccess) done_mask.fetch_or(bit, std::memory_order_acq_rel);
   return e;
 }
 
-template <int KCAP>
+template <int KCAP, int NWG>
 cudaError_t launch_variant(const ScoreTopkPlan& p, const CUtensorMap& mq, const CUtensorMap& mk,
                            const TopkKernelArgs& args, cudaStream_t stream) {
-  cudaError_t e = configure_once<KCAP>();
+  cudaError_t e = configure_once<KCAP, NWG>();
   if (e != cudaSuccess) return e;
   const unsigned grid = 2u * static_cast<unsigned>(p.n_qt) * static_cast<unsigned>(p.n_split);
-  score_topk_kernel<KCAP><<<grid, kThreads, TopkCfg<KCAP>::kSmemBytes, stream>>>(mq, mk, args);
+  score_topk_kernel<KCAP, NWG><<<grid, threads_for(NWG), TopkCfg<KCAP, NWG>::kSmemBytes, stream>>>(
+      mq, mk, args);
   return cudaGetLastError();
 }
 
 }  // namespace
+
+cudaError_t launch_plan(const ScoreTopkPlan& p, const CUtensorMap& mq, const CUtensorMap& mk,
+                        const TopkKernelArgs& args, cudaStream_t stream);
 
 int device_sm_count() {
   static std::atomic<int> cache[64] = {};
@@ -423,6 +535,9 @@ bool plan_score_topk(int64_t M, int64_t N, int d, int k, int num_sms, ScoreTopkP
   p.n_kt = (N + kTileN - 1) / kTileN;
   p.num_kb = (d + kTileK - 1) / kTileK;
   p.m_pad = n_qt * kPairRows;
+  // Two epilogue warpgroups (one list each, alternating tiles) for k <= 32,
+  // where the register lists leave room for 10 warps; k >= 64 keeps one.
+  p.nwg = p.kcap <= 32 ? 2 : 1;
   // Choose the number of key-range splits: minimise the modelled makespan
   // waves * (tiles per unit + per-unit overhead), one CTA pair per two SMs.
   // Per-unit overhead in tile-times: pipeline fill/drain, the heap warm-up at
@@ -432,7 +547,7 @@ bool plan_score_topk(int64_t M, int64_t N, int d, int k, int num_sms, ScoreTopkP
   const int64_t pairs = num_sms / 2;
   int best_s = 1;
   double best_cost = 1e300;
-  const int64_t s_max = std::min<int64_t>(p.n_kt, kMaxSplits);
+  const int64_t s_max = std::min<int64_t>(p.n_kt, kMaxSplits / p.nwg);
   for (int64_t s = 1; s <= s_max; ++s) {
     const int64_t units = n_qt * s;
     if (2 * units > (1ll << 31) - 1) break;
@@ -447,7 +562,7 @@ bool plan_score_topk(int64_t M, int64_t N, int d, int k, int num_sms, ScoreTopkP
   }
   p.n_split = best_s;
   p.ws_bytes = kStatusBytes + static_cast<size_t>(p.m_pad) * 4u +
-               static_cast<size_t>(p.n_split) * static_cast<size_t>(k) *
+               static_cast<size_t>(p.n_split) * p.nwg * static_cast<size_t>(k) *
                    static_cast<size_t>(p.m_pad) * 8u;
   *plan = p;
   return true;
@@ -475,7 +590,7 @@ cudaError_t launch_score_topk(const ScoreTopkPlan& p, const void* q, int64_t ldq
   args.n_qt = p.n_qt;
   args.n_split = p.n_split;
   args.status = reinterpret_cast<int*>(wsb);
-  const size_t list_elems = static_cast<size_t>(p.n_split) * p.k * p.m_pad;
+  const size_t list_elems = static_cast<size_t>(p.n_split) * p.nwg * p.k * p.m_pad;
   const size_t bound_bytes = static_cast<size_t>(p.m_pad) * 4u;
   args.row_bound = reinterpret_cast<int32_t*>(wsb + kStatusBytes);
   args.ws_vals = reinterpret_cast<float*>(wsb + kStatusBytes + bound_bytes);
@@ -489,18 +604,25 @@ cudaError_t launch_score_topk(const ScoreTopkPlan& p, const void* q, int64_t ldq
       args.row_bound, p.m_pad, kImageNegInf);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  switch (p.kcap) {
-    case 16: e = launch_variant<16>(p, mq, mk, args, stream); break;
-    case 32: e = launch_variant<32>(p, mq, mk, args, stream); break;
-    case 64: e = launch_variant<64>(p, mq, mk, args, stream); break;
-    case 128: e = launch_variant<128>(p, mq, mk, args, stream); break;
-    default: return cudaErrorInvalidValue;
-  }
+  e = launch_plan(p, mq, mk, args, stream);
   if (e != cudaSuccess) return e;
-  return launch_merge_topk(args.ws_vals, args.ws_idx, p.n_split, p.k,
+  return launch_merge_topk(args.ws_vals, args.ws_idx, p.n_split * p.nwg, p.k,
                            static_cast<int64_t>(p.k) * p.m_pad, 1, p.k, p.M, p.k,
                            /*transform=*/1, lambda_sharp, tau, T, use_sigmoid, idx_offset, out_vals,
                            out_idx, stream);
+}
+
+cudaError_t launch_plan(const ScoreTopkPlan& p, const CUtensorMap& mq, const CUtensorMap& mk,
+                        const TopkKernelArgs& args, cudaStream_t stream) {
+  cudaError_t e;
+  switch (p.kcap * 4 + p.nwg) {
+    case 16 * 4 + 2: e = launch_variant<16, 2>(p, mq, mk, args, stream); break;
+    case 32 * 4 + 2: e = launch_variant<32, 2>(p, mq, mk, args, stream); break;
+    case 64 * 4 + 1: e = launch_variant<64, 1>(p, mq, mk, args, stream); break;
+    case 128 * 4 + 1: e = launch_variant<128, 1>(p, mq, mk, args, stream); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return e;
 }
 
 }  // namespace dwa

@@ -27,7 +27,7 @@
 #include <cstdio>
 #include <mutex>
 
-#include "../../include/dwa_retrieval.h"
+#include "dwa_retrieval.h"
 #include "dwa_internal.h"
 
 namespace {

@@ -2,9 +2,12 @@
 //
 // One thread owns one query row.  Its heap holds the k best (score, index)
 // pairs seen so far as a binary heap whose root is the WORST kept pair, so the
-// root score is the admission threshold.  Entries of all threads are
-// interleaved ([pos][thread], stride = threads) so that threads touching the
-// same heap position hit distinct shared-memory banks.
+// root score is the admission threshold.  An entry is 8 bytes (score bits,
+// index), read and written with one 64-bit shared-memory access.  Entries of
+// all threads are interleaved ([pos][thread], stride = threads): at any heap
+// position the 32 lanes of a warp touch 32 consecutive entries, and because
+// the stride is a multiple of 32 entries, lanes at DIFFERENT positions still
+// map to distinct bank pairs, so sift-downs never conflict.
 //
 // Order ("better"): higher score first; among equal scores the LOWER index
 // first — the tie rule of jax.lax.top_k that the reference relies on
@@ -24,60 +27,45 @@ __device__ __forceinline__ bool topk_worse(float as, int32_t ai, float bs, int32
 }
 
 struct SmemHeap {
-  float* s;      // scores,  element (pos, thread) at s[pos * stride + thread]
-  int32_t* i;    // indices, same layout
-  int stride;    // number of threads sharing the arrays
-  int k;         // heap size (entries per thread)
+  uint32_t base;  // shared-memory address of entry (0, 0)
+  int stride;     // number of threads sharing the array
+  int k;          // heap size (entries per thread)
 
-  __device__ __forceinline__ float& S(int pos, int t) const { return s[pos * stride + t]; }
-  __device__ __forceinline__ int32_t& I(int pos, int t) const { return i[pos * stride + t]; }
+  __device__ __forceinline__ uint32_t addr(int pos, int t) const {
+    return base + static_cast<uint32_t>(pos * stride + t) * 8u;
+  }
+  __device__ __forceinline__ void load(int pos, int t, float& s, int32_t& i) const {
+    uint32_t a, b;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(a), "=r"(b) : "r"(addr(pos, t)));
+    s = __uint_as_float(a);
+    i = static_cast<int32_t>(b);
+  }
+  __device__ __forceinline__ void store(int pos, int t, float s, int32_t i) const {
+    asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(addr(pos, t)), "r"(__float_as_uint(s)),
+                 "r"(static_cast<uint32_t>(i))
+                 : "memory");
+  }
+  __device__ __forceinline__ float score(int pos, int t) const {
+    float s;
+    int32_t i;
+    load(pos, t, s, i);
+    return s;
+  }
 
   __device__ __forceinline__ void init(int t) const {
-    for (int p = 0; p < k; ++p) {
-      S(p, t) = -INFINITY;
-      I(p, t) = kSentinelIdx;
-    }
+    for (int p = 0; p < k; ++p) store(p, t, -INFINITY, kSentinelIdx);
   }
 
-  // Replace the root (worst entry) by (ns, ni), which must rank above it, and
-  // restore the heap order by sifting down.
-  __device__ __forceinline__ void replace_root(int t, float ns, int32_t ni) const {
-    int p = 0;
-    while (true) {
-      int c = 2 * p + 1;
-      if (c >= k) break;
-      float cs = S(c, t);
-      int32_t ci = I(c, t);
-      if (c + 1 < k) {
-        const float c2s = S(c + 1, t);
-        const int32_t c2i = I(c + 1, t);
-        if (topk_worse(c2s, c2i, cs, ci)) {
-          c = c + 1;
-          cs = c2s;
-          ci = c2i;
-        }
-      }
-      if (!topk_worse(cs, ci, ns, ni)) break;
-      S(p, t) = cs;
-      I(p, t) = ci;
-      p = c;
-    }
-    S(p, t) = ns;
-    I(p, t) = ni;
-  }
-
-  // Sift entry at position p down within heap prefix [0, n).
-  __device__ __forceinline__ void sift_down(int t, int p, int n) const {
-    const float ns = S(p, t);
-    const int32_t ni = I(p, t);
+  // Sift (ns, ni) down from position p within the heap prefix [0, n).
+  __device__ __forceinline__ void sift_from(int t, int p, int n, float ns, int32_t ni) const {
     while (true) {
       int c = 2 * p + 1;
       if (c >= n) break;
-      float cs = S(c, t);
-      int32_t ci = I(c, t);
+      float cs, c2s;
+      int32_t ci, c2i;
+      load(c, t, cs, ci);
       if (c + 1 < n) {
-        const float c2s = S(c + 1, t);
-        const int32_t c2i = I(c + 1, t);
+        load(c + 1, t, c2s, c2i);
         if (topk_worse(c2s, c2i, cs, ci)) {
           c = c + 1;
           cs = c2s;
@@ -85,25 +73,27 @@ struct SmemHeap {
         }
       }
       if (!topk_worse(cs, ci, ns, ni)) break;
-      S(p, t) = cs;
-      I(p, t) = ci;
+      store(p, t, cs, ci);
       p = c;
     }
-    S(p, t) = ns;
-    I(p, t) = ni;
+    store(p, t, ns, ni);
+  }
+
+  // Replace the root (worst entry) by (ns, ni), which must rank above it.
+  __device__ __forceinline__ void replace_root(int t, float ns, int32_t ni) const {
+    sift_from(t, 0, k, ns, ni);
   }
 
   // In-place heapsort: afterwards position 0 holds the best entry and
   // position k-1 the worst.
   __device__ __forceinline__ void sort_best_first(int t) const {
     for (int end = k - 1; end > 0; --end) {
-      const float rs = S(0, t);
-      const int32_t ri = I(0, t);
-      S(0, t) = S(end, t);
-      I(0, t) = I(end, t);
-      S(end, t) = rs;
-      I(end, t) = ri;
-      sift_down(t, 0, end);
+      float rs, es;
+      int32_t ri, ei;
+      load(0, t, rs, ri);
+      load(end, t, es, ei);
+      store(end, t, rs, ri);
+      sift_from(t, 0, end, es, ei);
     }
   }
 };
