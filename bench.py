@@ -334,11 +334,74 @@ def run_ours(args, wl):
         dist.barrier(device_ids=[local_rank])
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = _cpu_baseline(args, wl, keys, values, queries[0])
+    if args.lm:
+        del r, keys, values, queries, q_dev
+        torch.cuda.empty_cache()
+        names = [n for n in args.lm.split(",") if n and (n != "small_char" or world == 1)]
+        line["lm"] = [measure_lm(n, world, rank, local_rank) for n in names]
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
     return 0
+
+
+def measure_lm(cfg_name, world, rank, local_rank, warmup=3, steps=3):
+    """DWA LM forward tokens/s (all ranks run the same forward; the pool is row-sharded)."""
+    import torch
+    import torch.distributed as dist
+
+    import computd_b200 as cb
+    from computd_b200 import dwa_lm
+
+    cfg = {"small_char": dwa_lm.SMALL_CHAR, "large_1b": dwa_lm.LARGE_1B}[cfg_name]
+    dev = torch.device("cuda", local_rank)
+    spec = cb.ShardSpec(cfg.pool_rows, rank, world)
+    std = cfg.d_model ** -0.5
+    keys = cb.new_normal(spec.n_local, cfg.d_model, seed=31, stddev=std, row_offset=spec.row_begin,
+                         device=dev)
+    values = cb.new_normal(spec.n_local, cfg.d_model, seed=32, stddev=std,
+                           row_offset=spec.row_begin, device=dev)
+    model = dwa_lm.DWALM(cfg, keys, values)
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    tokens = torch.randint(0, cfg.vocab, (cfg.batch, cfg.seq_len), device=dev, generator=g)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+
+    for _ in range(warmup):
+        model(tokens)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        model(tokens)
+    e1.record()
+    barrier()
+    t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t[0])
+    d, n_tok = cfg.d_model, cfg.tokens
+    retr = cfg.n_layers * 2.0 * n_tok * spec.n_local * d
+    dense = n_tok * (cfg.n_layers * (12.0 * d * d + 2.0 * cfg.seq_len * d)
+                     + 8.0 * d * d + 8.0 * d * cfg.vocab)
+    burst = _peaks()[0]
+    t_roof = (retr + dense) / (burst * 1e12)
+    status = model.retriever.status()
+    del model, keys, values
+    torch.cuda.empty_cache()
+    return {"config": cfg_name, "tokens_per_s": n_tok / (ms * 1e-3),
+            "unit": "tokens/s", "ms_per_forward": ms, "tokens_per_forward": n_tok,
+            "layers": cfg.n_layers, "d_model": d, "pool_rows": cfg.pool_rows,
+            "pool_rows_per_gpu": spec.n_local, "top_k": cfg.top_k,
+            "roofline": {"t_roof_ms": t_roof * 1e3, "frac": t_roof * 1e3 / ms,
+                         "flops_retrieval_per_gpu": retr, "flops_dense": dense,
+                         "peak": "bf16 burst (MEASURED_PEAKS.json)"},
+            "warmup": warmup, "steps": steps, "device_status": status}
 
 
 def _ncu_traffic(workload, world):
@@ -391,6 +454,8 @@ def main(argv=None):
     ap.add_argument("--cpu-queries", type=int, default=64,
                     help="queries per CPU sample (CPU baseline / reference arm)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--lm", default="small_char,large_1b",
+                    help="DWA LM forwards to time after the op (comma list; empty to skip)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -1,0 +1,152 @@
+"""DWA language model forward — the call site of the retrieval path.
+
+Mirrors the reference's ``DWAModel`` / ``DWABlock`` (src/model/dwa.py:77-216)
+to measure the path inside a model (tokens/s):
+
+    h = PartA(tokens)                                  parts.py:88-143 (embedding + proj + LayerNorm)
+    for each block (dwa.py:100-130):
+        h = h + attn(LayerNorm(h))                      parts.py:30-83 (causal, RoPE)
+        z = query_proj(h)                               dwa.py:105
+        top_vals, top_idx = retrieval(z, pool keys)     retrieval.py:204-343 (this repo's kernels)
+        alpha, b_delta = normalise + gathered sum       retrieval.py:326, assembly.py:104,127
+        h = LayerNorm(h + gamma * (h W_base^T + b_base + b_delta))   assembly.py:130
+    logits = PartB(h)                                   parts.py:146-176
+
+The pool is one (keys, values) pair shared by every block, as the reference
+shares ``pool.vectors`` (dwa.py:182,195), optionally row-sharded over a
+process group (one retrieval all-gather + merge + value all-reduce per block).
+Differences from the reference, by scope: the query/key aspect projections of
+``MultiAspectRetrieval`` are folded into ``query_proj`` (the pool keys are
+taken as already projected), and the low-rank U.V assembly term (``h_delta``)
+is not computed (a "next" item).  Dense layers are plain torch/cuBLAS; all
+retrieval work runs in libdwa_b200.so.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .retrieval import Retriever
+
+
+@dataclass(frozen=True)
+class DWALMConfig:
+    vocab: int
+    d_model: int
+    n_layers: int
+    n_heads: int
+    seq_len: int
+    batch: int
+    pool_rows: int
+    top_k: int
+    T: float = 1.0
+    lambda_sharp: float = 1.0
+    use_sigmoid: bool = False
+
+    @property
+    def tokens(self) -> int:
+        return self.batch * self.seq_len
+
+
+# Shapes of the benchmark configurations.
+SMALL_CHAR = DWALMConfig(vocab=65, d_model=384, n_layers=6, n_heads=6, seq_len=256, batch=16,
+                         pool_rows=65536, top_k=32)
+LARGE_1B = DWALMConfig(vocab=32000, d_model=2048, n_layers=24, n_heads=16, seq_len=2048, batch=8,
+                       pool_rows=4194304, top_k=64)
+LARGE_7B = DWALMConfig(vocab=32000, d_model=4096, n_layers=32, n_heads=32, seq_len=4096, batch=4,
+                       pool_rows=16777216, top_k=128)
+
+
+def _rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    # rotate (even, odd) pairs, concatenated like the reference (parts.py:17-25)
+    x1, x2 = x[..., ::2], x[..., 1::2]
+    return torch.cat([x1 * cos - x2 * sin, x1 * sin + x2 * cos], dim=-1)
+
+
+class CausalSelfAttention(nn.Module):
+    """parts.py:30-83: LayerNorm -> QKV -> RoPE -> causal softmax attention -> proj, residual."""
+
+    def __init__(self, d: int, n_heads: int, seq_len: int, device, dtype):
+        super().__init__()
+        assert d % n_heads == 0
+        self.h, self.dh = n_heads, d // n_heads
+        self.norm = nn.LayerNorm(d, device=device, dtype=dtype)
+        self.qkv = nn.Linear(d, 3 * d, bias=False, device=device, dtype=dtype)
+        self.proj = nn.Linear(d, d, bias=False, device=device, dtype=dtype)
+        theta = 1.0 / (10000.0 ** (torch.arange(0, self.dh, 2, device=device) / self.dh))
+        f = torch.outer(torch.arange(seq_len, device=device, dtype=torch.float32), theta)
+        self.register_buffer("cos", f.cos().to(dtype), persistent=False)
+        self.register_buffer("sin", f.sin().to(dtype), persistent=False)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        B, S, C = x.shape
+        q, k, v = self.qkv(self.norm(x)).split(C, dim=-1)
+        q = q.view(B, S, self.h, self.dh).transpose(1, 2)
+        k = k.view(B, S, self.h, self.dh).transpose(1, 2)
+        v = v.view(B, S, self.h, self.dh).transpose(1, 2)
+        q = _rope(q, self.cos[:S], self.sin[:S])
+        k = _rope(k, self.cos[:S], self.sin[:S])
+        o = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+        return x + self.proj(o.transpose(1, 2).reshape(B, S, C))
+
+
+class DWABlock(nn.Module):
+    """dwa.py:77-130 with the retrieval and gathered sum on this repo's kernels."""
+
+    def __init__(self, cfg: DWALMConfig, device, dtype):
+        super().__init__()
+        d = cfg.d_model
+        self.attn = CausalSelfAttention(d, cfg.n_heads, cfg.seq_len, device, dtype)
+        self.query_proj = nn.Linear(d, d, device=device, dtype=dtype)
+        self.W_base = nn.Linear(d, d, device=device, dtype=dtype)      # h_base (assembly.py:128)
+        self.gamma = nn.Parameter(torch.ones((), device=device, dtype=dtype))
+        self.norm = nn.LayerNorm(d, device=device, dtype=dtype)
+
+    def forward(self, h: torch.Tensor, retriever: Retriever) -> torch.Tensor:
+        B, S, C = h.shape
+        h = self.attn(h)
+        z = self.query_proj(h).reshape(B * S, C)
+        out, alpha, _, _ = retriever(z)                  # fused score+top-k, merge, gathered sum
+        b_delta = out.view(B, S, -1).to(h.dtype)
+        return self.norm(h + self.gamma * (self.W_base(h) + b_delta))
+
+
+class DWALM(nn.Module):
+    """dwa.py:133-216 forward: PartA -> DWABlocks over one shared pool -> PartB."""
+
+    def __init__(self, cfg: DWALMConfig, pool_keys: torch.Tensor, pool_values: torch.Tensor,
+                 group=None, dtype=torch.bfloat16, seed: int = 0):
+        super().__init__()
+        device = pool_keys.device
+        torch.manual_seed(seed)
+        d = cfg.d_model
+        self.cfg = cfg
+        self.embed = nn.Embedding(cfg.vocab, d, device=device, dtype=dtype)   # PartA (parts.py:97-98)
+        self.embed_proj = nn.Linear(d, d, bias=False, device=device, dtype=dtype)
+        self.embed_norm = nn.LayerNorm(d, device=device, dtype=dtype)
+        self.blocks = nn.ModuleList(DWABlock(cfg, device, dtype) for _ in range(cfg.n_layers))
+        self.head_norm = nn.LayerNorm(d, device=device, dtype=dtype)        # PartB (parts.py:146-176)
+        self.fc1 = nn.Linear(d, 4 * d, device=device, dtype=dtype)
+        self.fc2 = nn.Linear(4 * d, cfg.vocab, device=device, dtype=dtype)
+        for m in self.modules():
+            if isinstance(m, nn.Linear):
+                nn.init.normal_(m.weight, std=math.sqrt(2.0 / m.in_features))
+                if m.bias is not None:
+                    nn.init.zeros_(m.bias)
+        for blk in self.blocks:  # W_base starts at zero (assembly.py:37-39)
+            nn.init.zeros_(blk.W_base.weight)
+        # one retrieval plan shared by all blocks (same pool, same token count)
+        self.retriever = Retriever(pool_keys, pool_values, cfg.tokens, cfg.top_k,
+                                   lambda_sharp=cfg.lambda_sharp, T=cfg.T,
+                                   use_sigmoid=cfg.use_sigmoid, group=group)
+
+    @torch.no_grad()
+    def forward(self, token_ids: torch.Tensor) -> torch.Tensor:
+        h = self.embed_norm(self.embed_proj(self.embed(token_ids)))
+        for blk in self.blocks:
+            h = blk(h, self.retriever)
+        return self.fc2(F.gelu(self.fc1(self.head_norm(h))))
