@@ -245,32 +245,44 @@ def run_ours(args, wl):
     for i in range(args.warmup):
         r(queries[i % 2])
     barrier()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
-           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    n_ph = 6  # start | local score+top-k | exchange | merge | gather | reduce
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(n_ph)] for _ in range(args.steps)]
     with ClockSampler(local_rank) as clocks:
         barrier()
         t_start = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
         t_start.record()
         for i in range(args.steps):
-            e0, e1, e2 = ev[i]
-            e0.record()
+            e = ev[i]
+            e[0].record()
             r.topk_local(queries[i % 2])     # fused kernel + split merge on this rank
-            e1.record()
-            r.finish()                       # exchange + merge + gather + reduce
-            e2.record()
+            e[1].record()
+            r.exchange()                     # all-gather of [M, k] candidates (N > 1)
+            e[2].record()
+            r.merge()                        # global top-k merge (N > 1)
+            e[3].record()
+            r.gather()                       # alpha + owner-computes gathered sum
+            e[4].record()
+            r.reduce()                       # all-reduce of the partial sums (N > 1)
+            e[5].record()
         t_end.record()
         barrier()
     status = r.status()
     total_ms = t_start.elapsed_time(t_end)
-    topk_ms = [a.elapsed_time(b) for a, b, _ in ev]
-    t = torch.tensor([total_ms, sum(topk_ms) / len(topk_ms)], dtype=torch.float64, device=dev)
+    phase_ms = [sum(e[j].elapsed_time(e[j + 1]) for e in ev) / args.steps for j in range(n_ph - 1)]
+    t = torch.tensor([total_ms] + phase_ms, dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms, topk_avg_ms = float(t[0]), float(t[1])
+    total_ms = float(t[0])
+    phases = dict(zip(["score_topk_local", "exchange", "merge", "gather", "reduce"],
+                      [round(float(x), 4) for x in t[1:]]))
+    topk_avg_ms = phases["score_topk_local"]
     ms_per_step = total_ms / args.steps
 
     # ------------------------------------------------ end to end (host buffers)
+    # The queries arrive in pinned host memory at rank 0, are copied to its GPU
+    # and broadcast over NVLink to the other ranks; the replicated result
+    # (out, alpha, top_idx) is read back to the host at rank 0.
     q_host = [queries[i].cpu().pin_memory() for i in range(2)]
     out_host = torch.empty((M, d), dtype=torch.float32).pin_memory()
     alpha_host = torch.empty((M, k), dtype=torch.float32).pin_memory()
@@ -278,11 +290,15 @@ def run_ours(args, wl):
     q_dev = torch.empty_like(queries[0])
 
     def e2e_step(i):
-        q_dev.copy_(q_host[i % 2], non_blocking=True)
+        if rank == 0:
+            q_dev.copy_(q_host[i % 2], non_blocking=True)
+        if world > 1:
+            dist.broadcast(q_dev, src=0)
         out, alpha, tv, ti = r(q_dev)
-        out_host.copy_(out, non_blocking=True)
-        alpha_host.copy_(alpha, non_blocking=True)
-        idx_host.copy_(ti, non_blocking=True)
+        if rank == 0:
+            out_host.copy_(out, non_blocking=True)
+            alpha_host.copy_(alpha, non_blocking=True)
+            idx_host.copy_(ti, non_blocking=True)
 
     for i in range(args.warmup):
         e2e_step(i)
@@ -310,7 +326,7 @@ def run_ours(args, wl):
                 "unit": "TFLOP/s", "frac": achieved_tflops / burst,
                 "frac_of_sustained": achieved_tflops / sustained,
                 "peak_source": f"{peak_src} bf16 dense burst (MEASURED_PEAKS.json)",
-                "kernel": "score_topk_kernel + split merge (dwa_score_topk)",
+                "kernel": "score_topk_kernel + split merge (dwa_score_topk) on this GPU's shard",
                 "flops_per_launch": flops, "ms_per_launch": topk_avg_ms,
                 "traffic": _ncu_traffic(args.workload, world)}
 
@@ -324,8 +340,10 @@ def run_ours(args, wl):
                    "parallelism": f"pool rows sharded x{world}" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (2 GiB keys + 2 GiB values)"},
         "e2e": {"value": M / (e2e_ms * 1e-3), "unit": "queries/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                "path": "pinned host -> rank 0 -> NCCL broadcast; result read back at rank 0"},
         "roofline": roofline,
+        "phase_ms": phases,
         "gpu_launches": r.kernels_per_call * args.steps,
         "clocks": clocks.summary(),
         "device_status": status,

@@ -40,6 +40,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                       _c_void_p]),
     "dwa_merge_topk": (_i32, [_c_void_p, _c_void_p, _i32, _i64, _i32, _c_void_p, _c_void_p,
                               _c_void_p]),
+    "dwa_merge_topk_strided": (_i32, [_c_void_p, _c_void_p, _i32, _i64, _i32, _i64, _i64, _i64,
+                                      _c_void_p, _c_void_p, _c_void_p]),
     "dwa_weighted_gather": (_i32, [_c_void_p, _c_void_p, _i64, _i32, _c_void_p, _i64, _i64,
                                    _i64, _i32, _c_void_p, _c_void_p, _c_void_p]),
     "dwa_pool_init_normal": (_i32, [_c_void_p, _i64, _i64, _i64, _i64, ctypes.c_uint64, _f32,

@@ -153,6 +153,32 @@ dwa_status dwa_merge_topk(const float* cand_vals, const int32_t* cand_idx, int32
   return ok();
 }
 
+dwa_status dwa_merge_topk_strided(const float* cand_vals, const int32_t* cand_idx, int32_t P,
+                                  int64_t M, int32_t k, int64_t stride_list, int64_t stride_pos,
+                                  int64_t stride_row, float* out_vals, int32_t* out_idx,
+                                  dwa_stream_t stream) {
+  if (M < 0) return fail(DWA_ERR_INVALID_ARG, "negative M");
+  if (M == 0) return ok();
+  if (!cand_vals || !cand_idx || !out_vals || !out_idx)
+    return fail(DWA_ERR_INVALID_ARG, "null pointer");
+  if (P < 1) return fail(DWA_ERR_INVALID_ARG, "P=%d must be >= 1", P);
+  if (P > dwa::kMaxSplits)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "P=%d exceeds %d lists", P, dwa::kMaxSplits);
+  if (k < 1) return fail(DWA_ERR_INVALID_ARG, "k=%d must be >= 1", k);
+  if (k > DWA_MAX_K)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "k=%d exceeds DWA_MAX_K=%d", k, DWA_MAX_K);
+  if (stride_list < 0 || stride_pos < 0 || stride_row < 0)
+    return fail(DWA_ERR_INVALID_ARG, "negative stride");
+  if (!aligned(cand_vals, 4) || !aligned(cand_idx, 4))
+    return fail(DWA_ERR_INVALID_ARG, "candidate arrays must be 4-byte aligned");
+  cudaError_t e = dwa::launch_merge_topk(cand_vals, cand_idx, P, k, stride_list, stride_pos,
+                                         stride_row, M, k, /*transform=*/0, 0.f, 0.f, 1.f, 0,
+                                         /*idx_offset=*/0, out_vals, out_idx,
+                                         static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_merge_topk_strided launch");
+  return ok();
+}
+
 dwa_status dwa_weighted_gather(const float* vals, const int32_t* gidx, int64_t M, int32_t k,
                                const void* values, int64_t row_begin, int64_t row_end,
                                int64_t ldv, int32_t d, float* out, float* alpha_out,

@@ -124,21 +124,19 @@ __global__ void __launch_bounds__(kWarps * 32) merge_sorted_kernel(const MergeAr
         bu = u;
       }
     }
-    // warp arg-best; (score, index) pairs are unique except for sentinels
-    float ws = bs;
-    int32_t wi = bi;
-    int wl = lane;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float os = __shfl_xor_sync(0xffffffffu, ws, o);
-      const int32_t oi = __shfl_xor_sync(0xffffffffu, wi, o);
-      const int ol = __shfl_xor_sync(0xffffffffu, wl, o);
-      if (topk_worse(ws, wi, os, oi) || (ws == os && wi == oi && ol < wl)) {
-        ws = os;
-        wi = oi;
-        wl = ol;
-      }
-    }
+    // Warp arg-best with two hardware max-reductions: first over an unsigned
+    // image of the score that preserves float order, then over the reversed
+    // index among the lanes holding that score (lower index wins ties).
+    uint32_t su = __float_as_uint(bs);
+    if (su == 0x80000000u) su = 0u;  // -0.0 ties with +0.0, as in the float comparison
+    const uint32_t skey = (su & 0x80000000u) ? ~su : (su | 0x80000000u);
+    const uint32_t ikey = 0x7FFFFFFFu - static_cast<uint32_t>(bi);  // bi >= 0 or the sentinel
+    const uint32_t smax = __reduce_max_sync(0xffffffffu, skey);
+    const uint32_t imax = __reduce_max_sync(0xffffffffu, skey == smax ? ikey : 0u);
+    const uint32_t win = __ballot_sync(0xffffffffu, skey == smax && ikey == imax);
+    const int wl = __ffs(win) - 1;
+    const float ws = __shfl_sync(0xffffffffu, bs, wl);
+    const int32_t wi = __shfl_sync(0xffffffffu, bi, wl);
     if (lane == 0) {
       st_s[w][j] = ws;
       st_i[w][j] = wi;

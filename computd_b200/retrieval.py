@@ -124,8 +124,8 @@ class Retriever:
         self.local_vals = torch.empty((self.M, self.k), dtype=f32, device=dev)
         self.local_idx = torch.empty((self.M, self.k), dtype=i32, device=dev)
         if self.world > 1:
-            self.cand_vals = torch.empty((self.world, self.M, self.k), dtype=f32, device=dev)
-            self.cand_idx = torch.empty((self.world, self.M, self.k), dtype=i32, device=dev)
+            self._packed_local = torch.empty((self.M, self.k, 2), dtype=i32, device=dev)
+            self._packed_all = torch.empty((self.world, self.M, self.k, 2), dtype=i32, device=dev)
             self.top_vals = torch.empty((self.M, self.k), dtype=f32, device=dev)
             self.top_idx = torch.empty((self.M, self.k), dtype=i32, device=dev)
         else:
@@ -140,9 +140,10 @@ class Retriever:
 
     @property
     def kernels_per_call(self) -> int:
-        """Kernels of this library one full call launches (NCCL kernels not counted):
-        fused score + top-k, split merge, [cross-shard merge,] weighted gather."""
-        return 3 if self.world == 1 else 4
+        """Kernels of this library one full call launches (NCCL and torch copy kernels
+        not counted): bound reset, fused score + top-k, split merge,
+        [cross-shard merge,] weighted gather."""
+        return 4 if self.world == 1 else 5
 
     def topk_local(self, queries: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         """This rank's shard only: fused score + top-k and the split merge
@@ -154,17 +155,44 @@ class Retriever:
                         idx_offset=self.shard.row_begin)
         return self.local_vals, self.local_idx
 
-    def _merge_shards(self) -> None:
+    def exchange(self) -> None:
+        """All-gather every rank's [M, k] candidates into [P, M, k] (retrieval.py:295-296).
+
+        Scores and indices travel together as one int32 [M, k, 2] buffer, so
+        the exchange is a single collective.
+        """
         if self.world == 1:
             return
-        exchange_candidates(self.local_vals, self.local_idx, self.group, self.cand_vals,
-                            self.cand_idx)
+        self._packed_local[..., 0].copy_(self.local_vals.view(torch.int32))
+        self._packed_local[..., 1].copy_(self.local_idx)
+        if dist.get_backend(self.group) == "nccl":
+            dist.all_gather_into_tensor(self._packed_all, self._packed_local, group=self.group)
+        else:
+            dist.all_gather(list(self._packed_all.unbind(0)), self._packed_local, group=self.group)
+
+    def merge(self) -> None:
+        """Global top-k of the gathered [P, M, k] lists (retrieval.py:299-302), on the device."""
+        if self.world == 1:
+            return
         lib = _lib.load()
         with torch.cuda.device(self.device):
-            st = lib.dwa_merge_topk(self.cand_vals.data_ptr(), self.cand_idx.data_ptr(),
-                                    self.world, self.M, self.k, self.top_vals.data_ptr(),
-                                    self.top_idx.data_ptr(), _stream_handle(self.device))
-        _lib.check(st, "dwa_merge_topk")
+            st = lib.dwa_merge_topk_strided(
+                self._packed_all.data_ptr(), self._packed_all.data_ptr() + 4, self.world,
+                self.M, self.k, 2 * self.M * self.k, 2, 2 * self.k,
+                self.top_vals.data_ptr(), self.top_idx.data_ptr(), _stream_handle(self.device))
+        _lib.check(st, "dwa_merge_topk_strided")
+
+    def _merge_shards(self) -> None:
+        self.exchange()
+        self.merge()
+
+    def gather(self) -> None:
+        """Owner-computes alpha-weighted sum over this rank's pool rows."""
+        weighted_gather_into(self.top_vals, self.top_idx, self.values, self.out, self.alpha,
+                             self.shard.row_begin, self.shard.row_end)
+
+    def reduce(self) -> None:
+        reduce_partials(self.out, self.group)
 
     def topk(self, queries: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         """Global top-k only (fused scores f32, global indices i32), same on every rank."""
@@ -175,10 +203,10 @@ class Retriever:
     def finish(self):
         """After ``topk_local``: cross-shard merge, alpha, owner-computes weighted
         sum and the all-reduce of the partial sums."""
-        self._merge_shards()
-        weighted_gather_into(self.top_vals, self.top_idx, self.values, self.out, self.alpha,
-                             self.shard.row_begin, self.shard.row_end)
-        reduce_partials(self.out, self.group)
+        self.exchange()
+        self.merge()
+        self.gather()
+        self.reduce()
         return self.out, self.alpha, self.top_vals, self.top_idx
 
     def __call__(self, queries: torch.Tensor):

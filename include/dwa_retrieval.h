@@ -132,6 +132,20 @@ DWA_API dwa_status dwa_merge_topk(const float* cand_vals, const int32_t* cand_id
                           float* out_vals, int32_t* out_idx, dwa_stream_t stream);
 
 /*
+ * dwa_merge_topk over candidates at arbitrary element strides: candidate
+ * (list l, position p, row r) is cand_vals[l*stride_list + p*stride_pos +
+ * r*stride_row] (and likewise cand_idx).  Lets scores and indices travel in
+ * one interleaved int32 buffer [P, M, k, 2] — one all-gather instead of two —
+ * with cand_idx = cand_vals + 1 element.  Same merge, lists sorted best
+ * first, P <= 128.  Replaces the same reference lines as dwa_merge_topk
+ * (src/model/retrieval.py:295-302).
+ */
+DWA_API dwa_status dwa_merge_topk_strided(const float* cand_vals, const int32_t* cand_idx,
+                          int32_t P, int64_t M, int32_t k,
+                          int64_t stride_list, int64_t stride_pos, int64_t stride_row,
+                          float* out_vals, int32_t* out_idx, dwa_stream_t stream);
+
+/*
  * Alpha normalisation + gathered-value weighted sum (owner-computes form).
  * Replaces retrieval.py:326 (alpha = v / (sum v + 1e-8)) and the gather +
  * alpha-weighted sum of WeightAssembler (src/model/assembly.py:104,127):
