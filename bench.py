@@ -390,13 +390,16 @@ def measure_lm(cfg_name, world, rank, local_rank, warmup=3, steps=3):
             dist.barrier(device_ids=[local_rank])
         torch.cuda.synchronize()
 
+    # one process: replay the whole forward as one CUDA graph; sharded: eager
+    # (the blocks' collectives stay outside graphs)
+    fwd = dwa_lm.GraphedForward(model, tokens) if world == 1 else model
     for _ in range(warmup):
-        model(tokens)
+        fwd(tokens)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(steps):
-        model(tokens)
+        fwd(tokens)
     e1.record()
     barrier()
     t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
@@ -410,7 +413,8 @@ def measure_lm(cfg_name, world, rank, local_rank, warmup=3, steps=3):
     burst = _peaks()[0]
     t_roof = (retr + dense) / (burst * 1e12)
     status = model.retriever.status()
-    del model, keys, values
+    graphed = fwd is not model
+    del fwd, model, keys, values
     torch.cuda.empty_cache()
     return {"config": cfg_name, "tokens_per_s": n_tok / (ms * 1e-3),
             "unit": "tokens/s", "ms_per_forward": ms, "tokens_per_forward": n_tok,
@@ -419,7 +423,8 @@ def measure_lm(cfg_name, world, rank, local_rank, warmup=3, steps=3):
             "roofline": {"t_roof_ms": t_roof * 1e3, "frac": t_roof * 1e3 / ms,
                          "flops_retrieval_per_gpu": retr, "flops_dense": dense,
                          "peak": "bf16 burst (MEASURED_PEAKS.json)"},
-            "warmup": warmup, "steps": steps, "device_status": status}
+            "warmup": warmup, "steps": steps, "device_status": status,
+            "cuda_graph": graphed}
 
 
 def _ncu_traffic(workload, world):

@@ -8,15 +8,16 @@ and the softmax-weighted gather of pool value rows.  All compute runs in
 provides device memory, streams and torch.distributed plumbing only.
 """
 from ._lib import DWA_MAX_K, DWAArgumentError, DWAError, load as load_library
-from .assembly import weighted_gather_into, weighted_value_sum
+from .assembly import normalise_alpha, weighted_gather_into, weighted_value_sum
 from .pool import ShardSpec, init_normal, new_normal
-from .retrieval import Retriever, chip_topk, exchange_candidates, reduce_partials
+from .retrieval import (MultiAspectRetrieval, Retriever, chip_topk, exchange_candidates,
+                        reduce_partials)
 from .tiled_topk import (merge_topk, score_topk_into, tiled_topk_fallback, tiled_topk_fused,
                          workspace_bytes)
 
 __all__ = [
     "DWA_MAX_K", "DWAArgumentError", "DWAError", "load_library",
-    "weighted_gather_into", "weighted_value_sum",
+    "normalise_alpha", "weighted_gather_into", "weighted_value_sum", "MultiAspectRetrieval",
     "ShardSpec", "init_normal", "new_normal",
     "Retriever", "chip_topk", "exchange_candidates", "reduce_partials",
     "merge_topk", "score_topk_into", "tiled_topk_fallback", "tiled_topk_fused", "workspace_bytes",

@@ -185,7 +185,10 @@ dwa_status dwa_weighted_gather(const float* vals, const int32_t* gidx, int64_t M
                                dwa_stream_t stream) {
   if (M < 0) return fail(DWA_ERR_INVALID_ARG, "negative M");
   if (M == 0) return ok();
-  if (!vals || !gidx || !out) return fail(DWA_ERR_INVALID_ARG, "null vals/gidx/out pointer");
+  if (!vals || !gidx) return fail(DWA_ERR_INVALID_ARG, "null vals/gidx pointer");
+  if (!out && row_end > row_begin)
+    return fail(DWA_ERR_INVALID_ARG, "null out with a non-empty owned row range");
+  if (!out && !alpha_out) return fail(DWA_ERR_INVALID_ARG, "nothing to compute (out and alpha_out null)");
   if (k < 1) return fail(DWA_ERR_INVALID_ARG, "k=%d must be >= 1", k);
   if (k > DWA_MAX_K)
     return fail(DWA_ERR_UNSUPPORTED_SHAPE, "k=%d exceeds DWA_MAX_K=%d", k, DWA_MAX_K);
@@ -202,7 +205,7 @@ dwa_status dwa_weighted_gather(const float* vals, const int32_t* gidx, int64_t M
     if (!aligned(values, 16))
       return fail(DWA_ERR_INVALID_ARG, "values must be 16-byte aligned");
   }
-  if (!aligned(out, 16)) return fail(DWA_ERR_INVALID_ARG, "out must be 16-byte aligned");
+  if (out && !aligned(out, 16)) return fail(DWA_ERR_INVALID_ARG, "out must be 16-byte aligned");
   cudaError_t e = dwa::launch_weighted_gather(vals, gidx, M, k, values, row_begin, row_end, ldv, d,
                                               out, alpha_out, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "dwa_weighted_gather launch");

@@ -81,6 +81,7 @@ __global__ void __launch_bounds__(kWarps * 32) weighted_gather_kernel(const Gath
     n_own += __popc(mask);
   }
   __syncwarp();
+  if (a.out == nullptr) return;  // alpha only
 
   float* orow = a.out + m * a.d;
   for (int c0 = 0; c0 < a.d; c0 += 256) {

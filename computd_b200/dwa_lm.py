@@ -150,3 +150,34 @@ class DWALM(nn.Module):
         for blk in self.blocks:
             h = blk(h, self.retriever)
         return self.fc2(F.gelu(self.fc1(self.head_norm(h))))
+
+
+class GraphedForward:
+    """The LM forward captured once in a CUDA graph and replayed.
+
+    Every launch of the forward — dense layers, the retrieval kernels of each
+    block, their bound resets — goes into one graph, so a small model is not
+    bound by per-kernel launch latency.  Capture runs after two eager warm-up
+    forwards on a side stream (kernel attributes and tensor maps are set up
+    there).  Single-process use only: the graph must not contain collectives.
+    """
+
+    def __init__(self, model: DWALM, token_ids: torch.Tensor):
+        if model.retriever.world != 1:
+            raise ValueError("GraphedForward is for one process; sharded pools use eager forward")
+        self.model = model
+        self.tokens = token_ids.clone()
+        side = torch.cuda.Stream(device=token_ids.device)
+        side.wait_stream(torch.cuda.current_stream(token_ids.device))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                model(self.tokens)
+        torch.cuda.current_stream(token_ids.device).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.logits = model(self.tokens)
+
+    def __call__(self, token_ids: torch.Tensor) -> torch.Tensor:
+        self.tokens.copy_(token_ids)
+        self.graph.replay()
+        return self.logits

@@ -22,7 +22,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from .assembly import _check_values, weighted_gather_into
+from .assembly import _check_values, normalise_alpha, weighted_gather_into
 from .pool import ShardSpec
 from .tiled_topk import (_as_bf16_rows, _stream_handle, merge_topk, score_topk_into,
                          tiled_topk_fused, workspace_bytes)
@@ -224,3 +224,75 @@ class Retriever:
                                           ctypes.byref(v))
         _lib.check(st, "dwa_workspace_status")
         return int(v.value)
+
+
+class MultiAspectRetrieval:
+    """Parameters and ``pallas_hybrid_forward`` of the reference's retrieval
+    module (src/model/retrieval.py:7-46, 204-343) on B200.
+
+    The projection, normalisation and aspect collapse (241-263) are dense
+    einsums on cuBLAS; the per-shard score + top-k, the cross-shard merge and
+    the alpha normalisation (280-326) run on this library's kernels.  ``mesh``
+    takes a torch.distributed process group (the reference's ``Mesh``); with
+    ``tp_axis`` None or no group the single-chip path is used, as in the
+    reference (314-319).  ``tau`` is read to the host once per call (the C ABI
+    takes it as a scalar).
+    """
+
+    def __init__(self, D: int, d_A: int, S: int, d_k: int, N: int, device=None,
+                 dtype=torch.bfloat16, seed: int = 0):
+        dev = torch.device(device) if device is not None else torch.device("cuda")
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        self.S, self.d_k, self.N = S, d_k, N
+        self.W_Q = (torch.randn(S, d_k, d_A, device=dev, generator=g) * d_A ** -0.5).to(dtype)
+        self.W_K = (torch.randn(S, d_k, D, device=dev, generator=g) * D ** -0.5).to(dtype)
+        self.aspect_logits = torch.zeros(S, device=dev)
+        self.tau = torch.zeros(S, device=dev)
+
+    @staticmethod
+    def _normalize(x: torch.Tensor) -> torch.Tensor:
+        return x / (torch.linalg.norm(x, dim=-1, keepdim=True) + 1e-8)
+
+    def project_keys(self, vectors: torch.Tensor, w: torch.Tensor, chunk_rows: int = 1 << 18
+                     ) -> torch.Tensor:
+        """keys_w = sum_s w_s normalize(W_K[s] v) for every pool row (retrieval.py:241-242,261),
+        chunked over rows so the (S, N, d_k) tensor is never materialised."""
+        N = vectors.shape[0]
+        out = torch.empty((N, self.d_k), dtype=torch.bfloat16, device=vectors.device)
+        WK = self.W_K.float()
+        for r0 in range(0, N, chunk_rows):
+            v = vectors[r0:r0 + chunk_rows].float()
+            acc = torch.zeros((v.shape[0], self.d_k), device=v.device)
+            for s in range(self.S):
+                acc += w[s] * self._normalize(v @ WK[s].T)
+            out[r0:r0 + chunk_rows] = acc.to(torch.bfloat16)
+        return out
+
+    def pallas_hybrid_forward(self, z: torch.Tensor, vectors: torch.Tensor, k_max: int,
+                              T: float = 1.0, lambda_sharp: float = 1.0, use_sigmoid: bool = True,
+                              tp_axis: str | None = "tp", mesh=None):
+        """Returns (alpha [B, seq, k], top_idx [B, seq, k], sims_seq [B, N_local],
+        alpha_raw_seq [B, N_local]) like retrieval.py:204-343."""
+        B, seq, d_A = z.shape
+        w = torch.softmax(self.aspect_logits.float(), dim=0)                     # 253
+        tau = float(torch.dot(w, self.tau.float())) if use_sigmoid else 0.0    # 254
+        keys_w = self.project_keys(vectors, w)                                  # 241-242, 261
+        zf = z.float()
+        queries_s = self._normalize(torch.einsum("skd,btd->sbtk", self.W_Q.float(), zf))  # 247-248
+        queries_w = torch.einsum("s,sbtk->btk", w, queries_s)                   # 262
+        queries_flat = queries_w.reshape(B * seq, self.d_k).to(torch.bfloat16)  # 263
+        group = mesh if (tp_axis is not None and mesh is not None) else None
+        final_v, final_i = chip_topk(queries_flat, keys_w, k_max, lambda_sharp, tau, T,
+                                     use_sigmoid, group=group)                  # 280-319
+        alpha = normalise_alpha(final_v).view(B, seq, k_max)                    # 324-326
+        top_idx = final_i.view(B, seq, k_max)
+        z_mean = zf.mean(dim=1)                                                 # 332-336
+        q_mean_s = self._normalize(torch.einsum("skd,bd->sbk", self.W_Q.float(), z_mean))
+        q_mean_w = torch.einsum("s,sbk->bk", w, q_mean_s)
+        sims_seq = q_mean_w @ keys_w.float().T
+        if use_sigmoid:                                                         # 338-341
+            alpha_raw_seq = torch.sigmoid(lambda_sharp * (sims_seq - tau)) * torch.exp(sims_seq / T)
+        else:
+            alpha_raw_seq = torch.exp(sims_seq / T)
+        return alpha, top_idx, sims_seq, alpha_raw_seq

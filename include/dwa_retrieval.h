@@ -157,7 +157,9 @@ DWA_API dwa_status dwa_merge_topk_strided(const float* cand_vals, const int32_t*
  * [row_begin, row_end) (the caller's shard; the whole pool on one GPU).
  * out f32 [M, d] is overwritten (rows owned elsewhere contribute zero, so the
  * partial sums of all shards add up to the full result).  alpha_out f32 [M, k]
- * may be NULL.  Requirements: d % 8 == 0, ldv % 8 == 0, 16-byte aligned values.
+ * may be NULL.  With an empty row range (row_begin == row_end) `out` may be
+ * NULL and only alpha is computed.  Requirements: d % 8 == 0, ldv % 8 == 0,
+ * 16-byte aligned values.
  */
 DWA_API dwa_status dwa_weighted_gather(const float* vals, const int32_t* gidx,
                                int64_t M, int32_t k,

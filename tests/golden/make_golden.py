@@ -125,6 +125,14 @@ def case_sharded(ref_tk, ref_ret, ref_asm, rng, out, n_chips=4):
     out["sharded/vectors"] = _bits(vectors)
     out["sharded/b_slice"] = np.array([asm._off_b, asm._end_b])
     out["sharded/b_delta"] = np.asarray(b, np.float32).reshape(B * seq, d_B)
+    # raw inputs and aux outputs of pallas_hybrid_forward itself
+    out["sharded/z"] = z.astype(np.float32)
+    out["sharded/W_Q"] = self.W_Q.value
+    out["sharded/W_K"] = self.W_K.value
+    out["sharded/aspect_logits"] = self.aspect_logits.value
+    out["sharded/tau_param"] = self.tau.value
+    out["sharded/sims_seq"] = np.asarray(sims_seq, np.float32)
+    out["sharded/alpha_raw_seq"] = np.asarray(alpha_raw_seq, np.float32)
 
 
 def main(argv=None) -> int:

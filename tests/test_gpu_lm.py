@@ -40,3 +40,25 @@ def test_dwa_lm_forward_and_block_retrieval():
     assert O.compare_topk(tv.cpu().numpy(), ti.cpu().numpy(), rv, ri, qn, kn, rtol=1e-2) == []
     want = O.weighted_sum(O.normalise(tv.cpu().numpy()), ti.cpu().numpy(), vn)
     assert O.compare_rows(out.cpu().numpy(), want, rtol=1e-2) == []
+
+
+def test_dwa_lm_graph_replay_matches_eager():
+    import computd_b200 as cb
+    from computd_b200.dwa_lm import DWALM, DWALMConfig, GraphedForward
+
+    dev = torch.device("cuda", 0)
+    cfg = DWALMConfig(vocab=65, d_model=128, n_layers=3, n_heads=4, seq_len=64, batch=2,
+                      pool_rows=4096, top_k=8)
+    keys = cb.new_normal(cfg.pool_rows, cfg.d_model, seed=21, stddev=cfg.d_model ** -0.5, device=dev)
+    values = cb.new_normal(cfg.pool_rows, cfg.d_model, seed=22, stddev=cfg.d_model ** -0.5, device=dev)
+    model = DWALM(cfg, keys, values)
+    t1 = torch.randint(0, cfg.vocab, (cfg.batch, cfg.seq_len), device=dev)
+    t2 = torch.randint(0, cfg.vocab, (cfg.batch, cfg.seq_len), device=dev)
+    eager1, eager2 = model(t1).clone(), model(t2).clone()
+    gf = GraphedForward(model, t1)
+    g1 = gf(t1).clone()
+    g2 = gf(t2).clone()
+    torch.cuda.synchronize()
+    torch.testing.assert_close(g1, eager1, rtol=0, atol=0)
+    torch.testing.assert_close(g2, eager2, rtol=0, atol=0)
+    assert model.retriever.status() == 0
