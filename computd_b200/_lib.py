@@ -44,6 +44,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                       _c_void_p, _c_void_p, _c_void_p]),
     "dwa_weighted_gather": (_i32, [_c_void_p, _c_void_p, _i64, _i32, _c_void_p, _i64, _i64,
                                    _i64, _i32, _c_void_p, _c_void_p, _c_void_p]),
+    "dwa_gather_dot": (_i32, [_c_void_p, _i32, _i64, _c_void_p, _i64, _i32, _c_void_p, _i64, _i64,
+                              _i64, _i32, _c_void_p, _c_void_p]),
+    "dwa_score_backward": (_i32, [_c_void_p, _c_void_p, _c_void_p, _i64, _i32, _f32, _f32, _f32,
+                                  _i32, _c_void_p, _c_void_p, _c_void_p]),
+    "dwa_gather_rows": (_i32, [_c_void_p, _c_void_p, _i64, _i32, _c_void_p, _i64, _i64, _i64, _i32,
+                               _c_void_p, _i32, _c_void_p]),
+    "dwa_scatter_add_rows": (_i32, [_c_void_p, _c_void_p, _i64, _i32, _c_void_p, _i32, _i64, _i64,
+                                    _i64, _c_void_p, _i64, _i32, _c_void_p]),
     "dwa_pool_init_normal": (_i32, [_c_void_p, _i64, _i64, _i64, _i64, ctypes.c_uint64, _f32,
                                     _c_void_p]),
     "dwa_workspace_status": (_i32, [_c_void_p, _c_void_p, ctypes.POINTER(_i32)]),

@@ -1,0 +1,236 @@
+// backward.cu — gradients of the retrieval path (selected indices fixed).
+//
+// The reference trains through the plain-jnp path because its Pallas kernel
+// has no VJP (src/model/retrieval.py:268-271).  With the top-k indices held
+// fixed, the path  out = sum_j alpha_j V[idx_j],  alpha = v / (sum v + 1e-8),
+// v = gate(s) * exp(s / T),  s_j = <q, K[idx_j]>  differentiates into:
+//
+//   dalpha_j = <dout, V[idx_j]>                               gather_dot
+//   dv_j     = dalpha_j / (S + e) - (sum_i dalpha_i v_i) / (S + e)^2
+//   ds_j     = dv_j * v_j * (lambda (1 - g_j) + 1 / T)  (gate)  or  dv_j * v_j / T
+//   dq       = sum_j ds_j K[idx_j]                            gather_rows (raw weights)
+//   dV[idx_j] += alpha_j dout,  dK[idx_j] += ds_j q           scatter_add_rows
+//   dlambda, dtau, dT: sums over (m, j)                       score_backward
+//
+// Every kernel works on an owned row range [row_begin, row_end) of the pool
+// (owner-computes): on a sharded pool each rank's partial dalpha / s / dq are
+// summed with one all-reduce, and each rank updates only its own rows.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "dwa_internal.h"
+
+namespace dwa {
+
+namespace {
+
+constexpr int kWarps = 8;
+
+__device__ __forceinline__ void bf16x8(const uint4 x, float (&f)[8]) {
+  f[0] = __uint_as_float(x.x << 16);
+  f[1] = __uint_as_float(x.x & 0xFFFF0000u);
+  f[2] = __uint_as_float(x.y << 16);
+  f[3] = __uint_as_float(x.y & 0xFFFF0000u);
+  f[4] = __uint_as_float(x.z << 16);
+  f[5] = __uint_as_float(x.z & 0xFFFF0000u);
+  f[6] = __uint_as_float(x.w << 16);
+  f[7] = __uint_as_float(x.w & 0xFFFF0000u);
+}
+
+// 8 consecutive elements of row vector `a` (f32 or bf16) starting at col.
+__device__ __forceinline__ void load_a8(const void* a, int a_bf16, int64_t off, float (&f)[8]) {
+  if (a_bf16) {
+    bf16x8(__ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a) + off)), f);
+  } else {
+    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(a) + off);
+    const float4 x = __ldg(p), y = __ldg(p + 1);
+    f[0] = x.x; f[1] = x.y; f[2] = x.z; f[3] = x.w;
+    f[4] = y.x; f[5] = y.y; f[6] = y.z; f[7] = y.w;
+  }
+}
+
+// out[m, j] = <a[m, :], rows[idx[m, j] - row_begin, :]> for owned rows, else 0.
+// One warp per (m): lanes cover d in 8-wide slices; k dot products per row.
+__global__ void __launch_bounds__(kWarps * 32)
+    gather_dot_kernel(const void* a, int a_bf16, int64_t lda, const int32_t* idx, int64_t M, int k,
+                      const uint16_t* rows, int64_t row_begin, int64_t row_end, int64_t ldr, int d,
+                      float* out) {
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t m = static_cast<int64_t>(blockIdx.x) * kWarps + w;
+  if (m >= M) return;
+  for (int j = 0; j < k; ++j) {
+    const int32_t g = idx[m * k + j];
+    const bool own = g >= row_begin && g < row_end;  // warp-uniform
+    float acc = 0.f;
+    if (own) {
+      const uint16_t* r = rows + static_cast<int64_t>(g - row_begin) * ldr;
+      for (int c = lane * 8; c < d; c += 256) {
+        float fa[8], fr[8];
+        load_a8(a, a_bf16, m * lda + c, fa);
+        bf16x8(__ldg(reinterpret_cast<const uint4*>(r + c)), fr);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc = fmaf(fa[e], fr[e], acc);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    }
+    if (lane == 0) out[m * k + j] = acc;
+  }
+}
+
+// Per row m (one warp): ds[m, j] from v, s, dalpha; scalar parameter grads
+// accumulated into dparams[0..2] = (dlambda, dtau, dT).
+__global__ void __launch_bounds__(kWarps * 32)
+    score_backward_kernel(const float* v, const float* s, const float* dalpha, int64_t M, int k,
+                          float lambda_sharp, float tau, float T, int use_sigmoid, float* ds,
+                          float* dparams) {
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t m = static_cast<int64_t>(blockIdx.x) * kWarps + w;
+  if (m >= M) return;
+  float sv = 0.f, sdv = 0.f;
+  for (int j = lane; j < k; j += 32) {
+    const float vj = v[m * k + j];
+    sv += vj;
+    sdv += dalpha[m * k + j] * vj;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    sv += __shfl_xor_sync(0xffffffffu, sv, o);
+    sdv += __shfl_xor_sync(0xffffffffu, sdv, o);
+  }
+  const float den = sv + 1e-8f;
+  float g_lam = 0.f, g_tau = 0.f, g_T = 0.f;
+  for (int j = lane; j < k; j += 32) {
+    const float vj = v[m * k + j];
+    const float sj = s[m * k + j];
+    const float dv = dalpha[m * k + j] / den - sdv / (den * den);
+    float dvds;
+    if (use_sigmoid) {
+      const float gj = 1.0f / (1.0f + expf(-(lambda_sharp * (sj - tau))));
+      dvds = vj * (lambda_sharp * (1.0f - gj) + 1.0f / T);
+      g_lam += dv * vj * (1.0f - gj) * (sj - tau);
+      g_tau += -dv * vj * lambda_sharp * (1.0f - gj);
+    } else {
+      dvds = vj / T;
+    }
+    g_T += -dv * vj * sj / (T * T);
+    ds[m * k + j] = dv * dvds;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    g_lam += __shfl_xor_sync(0xffffffffu, g_lam, o);
+    g_tau += __shfl_xor_sync(0xffffffffu, g_tau, o);
+    g_T += __shfl_xor_sync(0xffffffffu, g_T, o);
+  }
+  if (lane == 0 && dparams) {
+    atomicAdd(dparams + 0, g_lam);
+    atomicAdd(dparams + 1, g_tau);
+    atomicAdd(dparams + 2, g_T);
+  }
+}
+
+// out[m, :] (=|+=) sum_j w[m, j] rows[idx[m, j] - row_begin, :] over owned rows.
+__global__ void __launch_bounds__(kWarps * 32)
+    gather_rows_kernel(const float* wts, const int32_t* idx, int64_t M, int k,
+                       const uint16_t* rows, int64_t row_begin, int64_t row_end, int64_t ldr, int d,
+                       float* out, int accumulate) {
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t m = static_cast<int64_t>(blockIdx.x) * kWarps + w;
+  if (m >= M) return;
+  for (int c0 = 0; c0 < d; c0 += 256) {
+    const int col = c0 + lane * 8;
+    if (col >= d) continue;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < k; ++j) {
+      const int32_t g = idx[m * k + j];
+      if (g < row_begin || g >= row_end) continue;  // warp-uniform
+      const float wj = wts[m * k + j];
+      float f[8];
+      bf16x8(__ldg(reinterpret_cast<const uint4*>(rows + static_cast<int64_t>(g - row_begin) * ldr +
+                                                  col)),
+             f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = fmaf(wj, f[e], acc[e]);
+    }
+    float4* dst = reinterpret_cast<float4*>(out + m * d + col);
+    if (accumulate) {
+      const float4 p = dst[0], q = dst[1];
+      acc[0] += p.x; acc[1] += p.y; acc[2] += p.z; acc[3] += p.w;
+      acc[4] += q.x; acc[5] += q.y; acc[6] += q.z; acc[7] += q.w;
+    }
+    dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+  }
+}
+
+// grad[idx[m, j] - row_begin, :] += w[m, j] * a[m, :] for owned rows (f32 atomics).
+__global__ void __launch_bounds__(kWarps * 32)
+    scatter_add_rows_kernel(const float* wts, const int32_t* idx, int64_t M, int k, const void* a,
+                            int a_bf16, int64_t lda, int64_t row_begin, int64_t row_end,
+                            float* grad, int64_t ldg, int d) {
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t m = static_cast<int64_t>(blockIdx.x) * kWarps + w;
+  if (m >= M) return;
+  for (int j = 0; j < k; ++j) {
+    const int32_t g = idx[m * k + j];
+    if (g < row_begin || g >= row_end) continue;  // warp-uniform
+    const float wj = wts[m * k + j];
+    float* gr = grad + static_cast<int64_t>(g - row_begin) * ldg;
+    for (int c = lane * 8; c < d; c += 256) {
+      float fa[8];
+      load_a8(a, a_bf16, m * lda + c, fa);
+#pragma unroll
+      for (int e = 0; e < 8; e += 4) {
+        asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(gr + c + e),
+                     "f"(wj * fa[e]), "f"(wj * fa[e + 1]), "f"(wj * fa[e + 2]), "f"(wj * fa[e + 3])
+                     : "memory");
+      }
+    }
+  }
+}
+
+inline unsigned blocks_for(int64_t M) { return static_cast<unsigned>((M + kWarps - 1) / kWarps); }
+
+}  // namespace
+
+cudaError_t launch_gather_dot(const void* a, int a_bf16, int64_t lda, const int32_t* idx, int64_t M,
+                              int k, const void* rows, int64_t row_begin, int64_t row_end,
+                              int64_t ldr, int d, float* out, cudaStream_t stream) {
+  if (M <= 0) return cudaSuccess;
+  gather_dot_kernel<<<blocks_for(M), kWarps * 32, 0, stream>>>(
+      a, a_bf16, lda, idx, M, k, static_cast<const uint16_t*>(rows), row_begin, row_end, ldr, d,
+      out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_score_backward(const float* v, const float* s, const float* dalpha, int64_t M,
+                                  int k, float lambda_sharp, float tau, float T, int use_sigmoid,
+                                  float* ds, float* dparams, cudaStream_t stream) {
+  if (M <= 0) return cudaSuccess;
+  score_backward_kernel<<<blocks_for(M), kWarps * 32, 0, stream>>>(
+      v, s, dalpha, M, k, lambda_sharp, tau, T, use_sigmoid, ds, dparams);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gather_rows(const float* wts, const int32_t* idx, int64_t M, int k,
+                               const void* rows, int64_t row_begin, int64_t row_end, int64_t ldr,
+                               int d, float* out, int accumulate, cudaStream_t stream) {
+  if (M <= 0) return cudaSuccess;
+  gather_rows_kernel<<<blocks_for(M), kWarps * 32, 0, stream>>>(
+      wts, idx, M, k, static_cast<const uint16_t*>(rows), row_begin, row_end, ldr, d, out,
+      accumulate);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scatter_add_rows(const float* wts, const int32_t* idx, int64_t M, int k,
+                                    const void* a, int a_bf16, int64_t lda, int64_t row_begin,
+                                    int64_t row_end, float* grad, int64_t ldg, int d,
+                                    cudaStream_t stream) {
+  if (M <= 0) return cudaSuccess;
+  scatter_add_rows_kernel<<<blocks_for(M), kWarps * 32, 0, stream>>>(
+      wts, idx, M, k, a, a_bf16, lda, row_begin, row_end, grad, ldg, d);
+  return cudaGetLastError();
+}
+
+}  // namespace dwa

@@ -212,6 +212,104 @@ dwa_status dwa_weighted_gather(const float* vals, const int32_t* gidx, int64_t M
   return ok();
 }
 
+namespace {
+// Shared checks of the backward entry points; returns DWA_OK or a failure.
+dwa_status check_rows_args(const char* fn, const int32_t* gidx, int64_t M, int32_t k,
+                           const void* rows_or_grad, int64_t row_begin, int64_t row_end,
+                           int64_t ld, int32_t d, int ld_mult) {
+  if (!gidx) return fail(DWA_ERR_INVALID_ARG, "%s: null index array", fn);
+  if (k < 1) return fail(DWA_ERR_INVALID_ARG, "%s: k=%d must be >= 1", fn, k);
+  if (d < 8 || d % 8 != 0)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "%s: d=%d must be a positive multiple of 8", fn, d);
+  if (row_begin < 0 || row_end < row_begin || row_end > INT32_MAX)
+    return fail(DWA_ERR_INVALID_ARG, "%s: bad owned row range", fn);
+  if (row_end > row_begin) {
+    if (!rows_or_grad) return fail(DWA_ERR_INVALID_ARG, "%s: null rows with a non-empty range", fn);
+    if (ld < d) return fail(DWA_ERR_INVALID_ARG, "%s: row stride below d", fn);
+    if (ld % ld_mult != 0)
+      return fail(DWA_ERR_UNSUPPORTED_SHAPE, "%s: row stride must be a multiple of %d", fn, ld_mult);
+    if (!aligned(rows_or_grad, 16)) return fail(DWA_ERR_INVALID_ARG, "%s: rows not 16-byte aligned", fn);
+  }
+  (void)M;
+  return DWA_OK;
+}
+dwa_status check_vec_arg(const char* fn, const void* a, int32_t a_bf16, int64_t lda, int32_t d) {
+  if (!a) return fail(DWA_ERR_INVALID_ARG, "%s: null row-vector array", fn);
+  if (lda < d) return fail(DWA_ERR_INVALID_ARG, "%s: lda below d", fn);
+  if (lda % (a_bf16 ? 8 : 4) != 0 || !aligned(a, 16))
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "%s: row vectors need 16-byte aligned rows", fn);
+  return DWA_OK;
+}
+}  // namespace
+
+dwa_status dwa_gather_dot(const void* a, int32_t a_is_bf16, int64_t lda, const int32_t* gidx,
+                          int64_t M, int32_t k, const void* rows, int64_t row_begin,
+                          int64_t row_end, int64_t ldr, int32_t d, float* out,
+                          dwa_stream_t stream) {
+  if (M < 0) return fail(DWA_ERR_INVALID_ARG, "negative M");
+  if (M == 0) return ok();
+  if (!out) return fail(DWA_ERR_INVALID_ARG, "dwa_gather_dot: null out");
+  dwa_status st = check_rows_args("dwa_gather_dot", gidx, M, k, rows, row_begin, row_end, ldr, d, 8);
+  if (st == DWA_OK) st = check_vec_arg("dwa_gather_dot", a, a_is_bf16, lda, d);
+  if (st != DWA_OK) return st;
+  cudaError_t e = dwa::launch_gather_dot(a, a_is_bf16 ? 1 : 0, lda, gidx, M, k, rows, row_begin,
+                                         row_end, ldr, d, out, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_gather_dot launch");
+  return ok();
+}
+
+dwa_status dwa_score_backward(const float* vals, const float* scores, const float* dalpha,
+                              int64_t M, int32_t k, float lambda_sharp, float tau, float T,
+                              int32_t use_sigmoid, float* dscores, float* dparams,
+                              dwa_stream_t stream) {
+  if (M < 0) return fail(DWA_ERR_INVALID_ARG, "negative M");
+  if (M == 0) return ok();
+  if (!vals || !scores || !dalpha || !dscores)
+    return fail(DWA_ERR_INVALID_ARG, "dwa_score_backward: null pointer");
+  if (k < 1) return fail(DWA_ERR_INVALID_ARG, "k=%d must be >= 1", k);
+  if (!(T > 0.f) || !std::isfinite(T))
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "temperature T must be finite and > 0");
+  cudaError_t e = dwa::launch_score_backward(vals, scores, dalpha, M, k, lambda_sharp, tau, T,
+                                             use_sigmoid ? 1 : 0, dscores, dparams,
+                                             static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_score_backward launch");
+  return ok();
+}
+
+dwa_status dwa_gather_rows(const float* weights, const int32_t* gidx, int64_t M, int32_t k,
+                           const void* rows, int64_t row_begin, int64_t row_end, int64_t ldr,
+                           int32_t d, float* out, int32_t accumulate, dwa_stream_t stream) {
+  if (M < 0) return fail(DWA_ERR_INVALID_ARG, "negative M");
+  if (M == 0) return ok();
+  if (!weights || !out) return fail(DWA_ERR_INVALID_ARG, "dwa_gather_rows: null pointer");
+  if (!aligned(out, 16)) return fail(DWA_ERR_INVALID_ARG, "dwa_gather_rows: out not 16-byte aligned");
+  dwa_status st = check_rows_args("dwa_gather_rows", gidx, M, k, rows, row_begin, row_end, ldr, d, 8);
+  if (st != DWA_OK) return st;
+  cudaError_t e = dwa::launch_gather_rows(weights, gidx, M, k, rows, row_begin, row_end, ldr, d,
+                                          out, accumulate ? 1 : 0,
+                                          static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_gather_rows launch");
+  return ok();
+}
+
+dwa_status dwa_scatter_add_rows(const float* weights, const int32_t* gidx, int64_t M, int32_t k,
+                                const void* a, int32_t a_is_bf16, int64_t lda, int64_t row_begin,
+                                int64_t row_end, float* grad, int64_t ldg, int32_t d,
+                                dwa_stream_t stream) {
+  if (M < 0) return fail(DWA_ERR_INVALID_ARG, "negative M");
+  if (M == 0) return ok();
+  if (!weights) return fail(DWA_ERR_INVALID_ARG, "dwa_scatter_add_rows: null weights");
+  dwa_status st =
+      check_rows_args("dwa_scatter_add_rows", gidx, M, k, grad, row_begin, row_end, ldg, d, 4);
+  if (st == DWA_OK) st = check_vec_arg("dwa_scatter_add_rows", a, a_is_bf16, lda, d);
+  if (st != DWA_OK) return st;
+  cudaError_t e = dwa::launch_scatter_add_rows(weights, gidx, M, k, a, a_is_bf16 ? 1 : 0, lda,
+                                               row_begin, row_end, grad, ldg, d,
+                                               static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_scatter_add_rows launch");
+  return ok();
+}
+
 dwa_status dwa_pool_init_normal(void* out, int64_t rows, int64_t cols, int64_t ld,
                                 int64_t row_offset, uint64_t seed, float stddev,
                                 dwa_stream_t stream) {

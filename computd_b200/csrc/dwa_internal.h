@@ -66,6 +66,20 @@ cudaError_t launch_weighted_gather(const float* vals, const int32_t* gidx, int64
                                    int64_t ldv, int d, float* out, float* alpha_out,
                                    cudaStream_t stream);
 
+cudaError_t launch_gather_dot(const void* a, int a_bf16, int64_t lda, const int32_t* idx, int64_t M,
+                              int k, const void* rows, int64_t row_begin, int64_t row_end,
+                              int64_t ldr, int d, float* out, cudaStream_t stream);
+cudaError_t launch_score_backward(const float* v, const float* s, const float* dalpha, int64_t M,
+                                  int k, float lambda_sharp, float tau, float T, int use_sigmoid,
+                                  float* ds, float* dparams, cudaStream_t stream);
+cudaError_t launch_gather_rows(const float* wts, const int32_t* idx, int64_t M, int k,
+                               const void* rows, int64_t row_begin, int64_t row_end, int64_t ldr,
+                               int d, float* out, int accumulate, cudaStream_t stream);
+cudaError_t launch_scatter_add_rows(const float* wts, const int32_t* idx, int64_t M, int k,
+                                    const void* a, int a_bf16, int64_t lda, int64_t row_begin,
+                                    int64_t row_end, float* grad, int64_t ldg, int d,
+                                    cudaStream_t stream);
+
 cudaError_t launch_pool_init_normal(void* out, int64_t rows, int64_t cols, int64_t ld,
                                     int64_t row_offset, uint64_t seed, float stddev,
                                     cudaStream_t stream);

@@ -167,6 +167,46 @@ DWA_API dwa_status dwa_weighted_gather(const float* vals, const int32_t* gidx,
                                int64_t ldv, int32_t d,
                                float* out, float* alpha_out, dwa_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Backward of the path with the selected indices fixed (the reference trains
+ * through the plain-jnp path because its Pallas kernel has no VJP,
+ * src/model/retrieval.py:268-271).  With out = sum_j alpha_j V[idx_j],
+ * alpha = v / (sum v + 1e-8), v = gate(s) exp(s / T), s_j = <q, K[idx_j]>:
+ *   dalpha = dwa_gather_dot(dout, V, idx)        s = dwa_gather_dot(q, K, idx)
+ *   ds, dparams = dwa_score_backward(v, s, dalpha)
+ *   dq = dwa_gather_rows(ds, idx, K)
+ *   dV += dwa_scatter_add_rows(alpha, idx, dout), dK += dwa_scatter_add_rows(ds, idx, q)
+ * All four work on an owned pool row range [row_begin, row_end) (rows of
+ * `rows`/`grad` are global rows row_begin..): on a sharded pool each rank's
+ * partial dalpha / s / dq are summed across ranks, and each rank updates only
+ * its own rows.  Row vectors `a` are f32 (a_is_bf16 = 0) or bf16; d % 8 == 0;
+ * 16-byte aligned bases, row strides multiples of 8 elements.
+ * ------------------------------------------------------------------------ */
+
+/* out[m, j] = <a[m, :], rows[gidx[m, j] - row_begin, :]> (0 for rows owned elsewhere). */
+DWA_API dwa_status dwa_gather_dot(const void* a, int32_t a_is_bf16, int64_t lda,
+                          const int32_t* gidx, int64_t M, int32_t k,
+                          const void* rows, int64_t row_begin, int64_t row_end, int64_t ldr,
+                          int32_t d, float* out, dwa_stream_t stream);
+
+/* dscores[m, j] from fused scores v, raw scores s and dalpha; dparams (3
+ * floats: dlambda, dtau, dT) is accumulated into (atomically) and may be NULL. */
+DWA_API dwa_status dwa_score_backward(const float* vals, const float* scores, const float* dalpha,
+                          int64_t M, int32_t k,
+                          float lambda_sharp, float tau, float T, int32_t use_sigmoid,
+                          float* dscores, float* dparams, dwa_stream_t stream);
+
+/* out[m, :] (= or +=) sum_j w[m, j] rows[gidx[m, j] - row_begin, :] over owned rows. */
+DWA_API dwa_status dwa_gather_rows(const float* weights, const int32_t* gidx, int64_t M, int32_t k,
+                          const void* rows, int64_t row_begin, int64_t row_end, int64_t ldr,
+                          int32_t d, float* out, int32_t accumulate, dwa_stream_t stream);
+
+/* grad[gidx[m, j] - row_begin, :] += w[m, j] * a[m, :] over owned rows (f32 atomics). */
+DWA_API dwa_status dwa_scatter_add_rows(const float* weights, const int32_t* gidx,
+                          int64_t M, int32_t k, const void* a, int32_t a_is_bf16, int64_t lda,
+                          int64_t row_begin, int64_t row_end, float* grad, int64_t ldg,
+                          int32_t d, dwa_stream_t stream);
+
 /*
  * Deterministic pool / query initialisation: element (r, c) of a logical
  * [rows_total, cols] matrix is  stddev * N(0,1)  drawn from Philox4x32-10

@@ -52,11 +52,12 @@ def _worker(rank, world, port, q):
         torch.cuda.synchronize()
         same_chip = bool(torch.equal(ci, ti))
         msg = "ok"
+        g0 = dist.new_group([0])  # every rank takes part in group creation
         if rank == 0:
             full_k = cb.new_normal(N, d, seed=2, stddev=d ** -0.5, device=dev)
             full_v = cb.new_normal(N, d, seed=3, device=dev)
             r1 = cb.Retriever(full_k, full_v, M, k, lambda_sharp=3.0, tau=0.5, T=0.8,
-                              use_sigmoid=True, group=dist.new_group([0]))
+                              use_sigmoid=True, group=g0)
             o1, a1, v1, i1 = r1(queries)
             torch.cuda.synchronize()
             qn = queries.float().cpu().numpy()
@@ -71,8 +72,33 @@ def _worker(rank, world, port, q):
                 errs = O.compare_rows(out.cpu().numpy(), o1.cpu().numpy(), rtol=1e-2)
                 if errs:
                     msg = "; ".join(errs)
-        else:
-            dist.new_group([0])  # every rank takes part in group creation
+        # sharded backward: dq equal on every rank; dK/dV = this rank's rows of the full grads
+        from computd_b200.autograd import retrieve
+        qg = queries.clone().requires_grad_()
+        kg = keys.clone().requires_grad_()
+        vg = values.clone().requires_grad_()
+        W = cb.new_normal(M, d, seed=9, device=dev).float()
+        out_s, _, ti_s = retrieve(qg, kg, vg, k, 3.0, 0.5, 0.8, True)
+        (out_s * W).sum().backward()
+        if rank == 0 and msg == "ok":
+            full_k = cb.new_normal(N, d, seed=2, stddev=d ** -0.5, device=dev).requires_grad_()
+            full_v = cb.new_normal(N, d, seed=3, device=dev).requires_grad_()
+            q1 = queries.clone().requires_grad_()
+            out_1, _, ti_1 = retrieve(q1, full_k, full_v, k, 3.0, 0.5, 0.8, True, group=g0)
+            (out_1 * W).sum().backward()
+            torch.cuda.synchronize()
+            if not torch.equal(ti_1, ti_s):
+                msg = "backward: selections differ"
+            else:
+                def close(a, b):
+                    a, b = a.float(), b.float()
+                    return float((a - b).abs().max()) <= 1e-2 * float(b.abs().max().clamp_min(1e-12))
+                if not close(qg.grad, q1.grad):
+                    msg = "backward: dq differs from the single-GPU dq"
+                elif not close(kg.grad, full_k.grad[:spec.n_local]):
+                    msg = "backward: dK rows differ"
+                elif not close(vg.grad, full_v.grad[:spec.n_local]):
+                    msg = "backward: dV rows differ"
         q.put((rank, same_chip, msg, r.status()))
         dist.barrier(device_ids=[rank])
     finally:
