@@ -434,7 +434,9 @@ def _ncu_traffic(workload, world):
         with open(path) as f:
             for line in f:
                 if line.startswith("traffic_bytes_per_launch_full_size:") and world == 1:
-                    return float(line.split(":", 1)[1].split()[0])
+                    return {"bytes_per_launch": float(line.split(":", 1)[1].split()[0]),
+                            "source": os.path.relpath(path, ROOT) + " (ncu dram__bytes_read.sum"
+                                      " + dram__bytes_write.sum, full-size launch)"}
     except OSError:
         pass
     return None
