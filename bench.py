@@ -328,7 +328,10 @@ def run_ours(args, wl):
                 "peak_source": f"{peak_src} bf16 dense burst (MEASURED_PEAKS.json)",
                 "kernel": "score_topk_kernel + split merge (dwa_score_topk) on this GPU's shard",
                 "flops_per_launch": flops, "ms_per_launch": topk_avg_ms,
-                "traffic": _ncu_traffic(args.workload, world)}
+                "traffic": _ncu_traffic(args.workload, world),
+                "traffic_source": (f"profiles/score_topk_{args.workload}.md: ncu dram__bytes_read.sum"
+                                   " + dram__bytes_write.sum of one full-size launch"),
+                "algorithmic_bytes_per_launch": 2.0 * n_local * d + 2.0 * M * d + 8.0 * M * k}
 
     line = {
         "metric": METRIC, "value": M / (ms_per_step * 1e-3), "unit": "queries/s",
@@ -434,9 +437,7 @@ def _ncu_traffic(workload, world):
         with open(path) as f:
             for line in f:
                 if line.startswith("traffic_bytes_per_launch_full_size:") and world == 1:
-                    return {"bytes_per_launch": float(line.split(":", 1)[1].split()[0]),
-                            "source": os.path.relpath(path, ROOT) + " (ncu dram__bytes_read.sum"
-                                      " + dram__bytes_write.sum, full-size launch)"}
+                    return float(line.split(":", 1)[1].split()[0])
     except OSError:
         pass
     return None
