@@ -7,8 +7,9 @@
 //     lax.top_k(score, k_max)
 // which materialises the whole [M, N] score matrix before a sort-based top-k.
 // Here each [256 x 256] score tile lives only in tensor memory (TMEM); the
-// epilogue keeps the k best (score, index) per query row in a shared-memory
-// heap, so the full score matrix never reaches HBM.
+// epilogue keeps the k best (score, index) per query row in registers (a
+// sorted list, k <= 64) or in a shared-memory heap (k = 128), so the full
+// score matrix never reaches HBM.
 //
 // Launch unit = a CTA pair (cluster of 2 on neighbouring SMs) running
 // tcgen05.mma.cta_group::2: one 256 x 256 x 16 MMA covers 256 query rows (128
@@ -21,8 +22,10 @@
 //   warp 1     TMEM allocator (both CTAs) + UMMA issuer (leader CTA only):
 //              fp32 accumulators double-buffered in TMEM (2 x 256 columns)
 //   warps 2-5  epilogue: warp w reads TMEM lanes 32*(w%4).. with tcgen05.ld;
-//              thread = one query row; heap root = admission threshold; each
-//              lane walks only its own candidates
+//              thread = one query row; the list's k-th entry = admission
+//              threshold; candidates are buffered per lane and inserted in
+//              warp-wide passes (k <= 32: warps 2-9, two warpgroups taking
+//              alternate tiles)
 //
 // Work unit = (pair query tile, contiguous range of key tiles).  Units are
 // ordered split-major so the pairs resident at one time sweep the same few
@@ -323,7 +326,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    // Admission: a score enters this unit's heap when it beats the heap root
+    // Admission: a score enters this unit's list when it beats the list's k-th entry
     // (theta_loc; strict, since indices only grow inside a unit) AND is not
     // below the row's shared bound.  The bound is the best k-th score any unit
     // of the same query row has published; the union's k-th best is at least
@@ -344,6 +347,49 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
     float theta_loc = -INFINITY;       // worst kept score of this unit
     float bound = ordered_float(__ldcg(bound_ptr));
     float cut = fmaxf(theta_loc, float_below(bound));  // admit iff score > cut
+    // Deferred insertion.  Past the first tiles of a unit a row meets a
+    // candidate only every few tiles, and an immediate insert makes all 32
+    // lanes of the warp wait for the one lane that has it.  Instead each lane
+    // appends its candidates to a kDefer-entry buffer (a register shift: slot
+    // 0 newest, slot n_def - 1 oldest) and the warp drains the buffers only
+    // when one of them would overflow, so one insert pass serves every lane
+    // with an entry waiting.  Draining re-checks each entry against the cut
+    // and inserts a lane's entries in column order (buffer oldest first, then
+    // the current chunk), so the list is the one immediate insertion builds.
+    constexpr int kDefer = 4;
+    float def_s[kDefer];
+    int32_t def_i[kDefer];
+    int n_def = 0;
+    // Insert every buffered entry, then every candidate of mask m over v.
+    // One loop (one copy of the insertion network); lanes run their own
+    // iteration counts.
+    auto drain = [&](uint32_t m, const float (&v)[32], int32_t col0) {
+      while (n_def > 0 || m != 0u) {
+        float x;
+        int32_t xi;
+        if (n_def > 0) {
+          const int q = n_def - 1;  // oldest entry: a 2-level select, no dynamic indexing
+          const float s01 = (q & 1) ? def_s[1] : def_s[0];
+          const float s23 = (q & 1) ? def_s[3] : def_s[2];
+          const int32_t i01 = (q & 1) ? def_i[1] : def_i[0];
+          const int32_t i23 = (q & 1) ? def_i[3] : def_i[2];
+          x = (q & 2) ? s23 : s01;
+          xi = (q & 2) ? i23 : i01;
+          --n_def;
+        } else {
+          const int j = __ffs(m) - 1;
+          m &= m - 1u;
+          x = pick32(v, j);
+          xi = col0 + j;
+        }
+        if (x > cut) {
+          topk.insert(x, xi);
+          theta_loc = topk.worst();
+          cut = fmaxf(theta_loc, float_below(bound));
+        }
+      }
+    };
+    static_assert(kDefer == 4, "drain() selects among exactly four buffered entries");
     // Scan 32 scores of this row (columns col0 .. col0 + min(rem, 32) - 1).
     auto scan_chunk = [&](const uint32_t (&r)[32], int rem, int32_t col0) {
       float v[32];
@@ -370,16 +416,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
         for (int i = 0; i < w2; ++i) b[i] = b[2 * i] | (b[2 * i + 1] << sh);
       uint32_t m = b[0];
       if (rem < 32) m &= (1u << rem) - 1u;
-      // Each lane walks only its own candidates; the warp runs as many
-      // iterations as its busiest lane, not the union over lanes.
+      const int nc = __popc(m);
+      if (__any_sync(0xffffffffu, n_def + nc > kDefer)) {
+        drain(m, v, col0);
+        return;
+      }
       while (m) {
         const int j = __ffs(m) - 1;
         m &= m - 1u;
         const float s = pick32(v, j);
         if (s > cut) {
-          topk.insert(s, col0 + j);
-          theta_loc = topk.worst();
-          cut = fmaxf(theta_loc, float_below(bound));
+#pragma unroll
+          for (int q = kDefer - 1; q >= 1; --q) {
+            def_s[q] = def_s[q - 1];
+            def_i[q] = def_i[q - 1];
+          }
+          def_s[0] = s;
+          def_i[0] = col0 + j;
+          ++n_def;
         }
       }
     };
@@ -388,7 +442,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
     for (int t = g; t < n_tiles; t += NWG) {
       const int acc = t & 1;
       const uint32_t use = static_cast<uint32_t>(t >> 1);
-      if (!mbar_wait(tfull_bar(acc), use & 1u, a.status, abort_flag)) break;
+      // warp-uniform outcome: the votes below need all 32 lanes on the same path
+      const bool got = mbar_wait(tfull_bar(acc), use & 1u, a.status, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
       const int64_t n0 = (kt_begin + t) * kTileN;
       const int valid = static_cast<int>(min(static_cast<int64_t>(kTileN), a.N - n0));
@@ -421,6 +477,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
         bound = ordered_float(max(seen, mine));
         cut = fmaxf(theta_loc, float_below(bound));
       }
+    }
+    {
+      float none[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) none[j] = -INFINITY;
+      drain(0u, none, 0);
     }
     // Flush this unit's list for the row, best first: [split * NWG + g][row][pos].
     const int64_t o = (static_cast<int64_t>(split * NWG + g) * a.m_pad + row0 + row) * a.k;
