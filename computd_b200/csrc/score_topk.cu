@@ -163,6 +163,17 @@ struct TopKFor<128> {
   using type = HeapTopK;
 };
 
+// Shared admission bounds, kBoundSlots int32 per query row (one 64-byte line):
+//   [0]      P = 1: the best k-th score of any list of the row
+//   [1, 3)   P = 2: slot c holds the best (k/2)-th score of the lists l = c mod 2
+//   [3, 7)   P = 4: slot c holds the best (k/4)-th score of the lists l = c mod 4
+//   [7, 15)  P = 8: slot c holds the best (k/8)-th score of the lists l = c mod 8
+// Lists of distinct classes cover disjoint key sets, so for each P the P
+// class maxima name P disjoint lists holding k/P scores each that are >= the
+// smallest of them: min over the P slots is a lower bound of the row's k-th
+// best.  The bound taken is the largest of the four.
+constexpr int kBoundSlots = 16;
+
 // Order-preserving map float -> int32 (signed integer order = float order),
 // so atomicMax on the image maximises the float.
 __device__ __forceinline__ int32_t ordered_int(float f) {
@@ -188,7 +199,7 @@ struct TopkKernelArgs {
   int k;             // kept per row
   int n_qt;          // 256-row pair query tiles
   int n_split;       // key-range splits
-  int32_t* row_bound;  // [m_pad] shared admission bound per query row (ordered_int image)
+  int32_t* row_bound;  // [m_pad][kBoundSlots] shared admission bounds per query row (ordered_int images)
   float* ws_vals;    // [n_split * NWG][m_pad][k] raw scores, sorted best first
   int32_t* ws_idx;   // [n_split * NWG][m_pad][k] local key indices
   int* status;       // device status word
@@ -343,7 +354,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
       topk.row = row;
     }
     topk.init(a.k);
-    int32_t* bound_ptr = a.row_bound + row0 + row;
+    int32_t* bound_ptr = a.row_bound + static_cast<int64_t>(row0 + row) * kBoundSlots;
+    const int list_id = split * NWG + g;  // disjoint key set of this list
+    // quantile slots are static list positions when the list is exactly full-width
+    const bool quantiles = KCAP <= 64 && a.k == KCAP;
     float theta_loc = -INFINITY;       // worst kept score of this unit
     float bound = ordered_float(__ldcg(bound_ptr));
     float cut = fmaxf(theta_loc, float_below(bound));  // admit iff score > cut
@@ -446,6 +460,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
       const bool got = mbar_wait(tfull_bar(acc), use & 1u, a.status, abort_flag);
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
+      // The row's shared bounds as published so far, read before the scan so
+      // the latency hides behind it (with two warpgroups the registers are
+      // short and each warpgroup has two tile-times per tile: read after it).
+      int4 sb0, sb1, sb2, sb3;
+      if constexpr (NWG == 1) {
+        sb0 = ld_relaxed_gpu_v4(bound_ptr);
+        sb1 = ld_relaxed_gpu_v4(bound_ptr + 4);
+        sb2 = ld_relaxed_gpu_v4(bound_ptr + 8);
+        sb3 = ld_relaxed_gpu_v4(bound_ptr + 12);
+      }
       const int64_t n0 = (kt_begin + t) * kTileN;
       const int valid = static_cast<int>(min(static_cast<int64_t>(kTileN), a.N - n0));
       const uint32_t taddr =
@@ -470,13 +494,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? lead_tempty1 : lead_tempty0);
-      // Publish this unit's k-th best and pick up the row's best bound.
-      if (theta_loc > -INFINITY) {
-        const int32_t mine = ordered_int(theta_loc);
-        const int32_t seen = atomicMax(bound_ptr, mine);
-        bound = ordered_float(max(seen, mine));
-        cut = fmaxf(theta_loc, float_below(bound));
+      // Publish this list's k-th best and its (k/P)-th bests (no round trip)
+      // and take up the best bound read at the start of the tile.
+      if (theta_loc > -INFINITY) red_max_gpu(bound_ptr, ordered_int(theta_loc));
+      if constexpr (KCAP <= 64) {
+        if (quantiles) {
+          const float q2 = topk.s[KCAP / 2 - 1], q4 = topk.s[KCAP / 4 - 1], q8 = topk.s[KCAP / 8 - 1];
+          if (q2 > -INFINITY) red_max_gpu(bound_ptr + 1 + (list_id & 1), ordered_int(q2));
+          if (q4 > -INFINITY) red_max_gpu(bound_ptr + 3 + (list_id & 3), ordered_int(q4));
+          if (q8 > -INFINITY) red_max_gpu(bound_ptr + 7 + (list_id & 7), ordered_int(q8));
+        }
       }
+      if constexpr (NWG != 1) {
+        sb0 = ld_relaxed_gpu_v4(bound_ptr);
+        sb1 = ld_relaxed_gpu_v4(bound_ptr + 4);
+        sb2 = ld_relaxed_gpu_v4(bound_ptr + 8);
+        sb3 = ld_relaxed_gpu_v4(bound_ptr + 12);
+      }
+      {
+        int32_t bi = sb0.x;
+        bi = max(bi, min(sb0.y, sb0.z));
+        bi = max(bi, min(min(sb0.w, sb1.x), min(sb1.y, sb1.z)));
+        bi = max(bi, min(min(min(sb1.w, sb2.x), min(sb2.y, sb2.z)),
+                         min(min(sb2.w, sb3.x), min(sb3.y, sb3.z))));
+        bound = fmaxf(bound, ordered_float(bi));
+      }
+      cut = fmaxf(theta_loc, float_below(bound));
     }
     {
       float none[32];
@@ -623,7 +666,7 @@ bool plan_score_topk(int64_t M, int64_t N, int d, int k, int num_sms, ScoreTopkP
     }
   }
   p.n_split = best_s;
-  p.ws_bytes = kStatusBytes + static_cast<size_t>(p.m_pad) * 4u +
+  p.ws_bytes = kStatusBytes + static_cast<size_t>(p.m_pad) * kBoundSlots * 4u +
                static_cast<size_t>(p.n_split) * p.nwg * static_cast<size_t>(k) *
                    static_cast<size_t>(p.m_pad) * 8u;
   *plan = p;
@@ -653,7 +696,7 @@ cudaError_t launch_score_topk(const ScoreTopkPlan& p, const void* q, int64_t ldq
   args.n_split = p.n_split;
   args.status = reinterpret_cast<int*>(wsb);
   const size_t list_elems = static_cast<size_t>(p.n_split) * p.nwg * p.k * p.m_pad;
-  const size_t bound_bytes = static_cast<size_t>(p.m_pad) * 4u;
+  const size_t bound_bytes = static_cast<size_t>(p.m_pad) * kBoundSlots * 4u;
   args.row_bound = reinterpret_cast<int32_t*>(wsb + kStatusBytes);
   args.ws_vals = reinterpret_cast<float*>(wsb + kStatusBytes + bound_bytes);
   args.ws_idx = reinterpret_cast<int32_t*>(wsb + kStatusBytes + bound_bytes + list_elems * 4);
@@ -662,8 +705,9 @@ cudaError_t launch_score_topk(const ScoreTopkPlan& p, const void* q, int64_t ldq
   if (e != cudaSuccess) return e;
   // The ordered image of -inf: "no bound yet" (every score is admissible).
   constexpr int32_t kImageNegInf = static_cast<int32_t>(0xFF800000u ^ 0x7FFFFFFFu);
-  fill_i32_kernel<<<static_cast<unsigned>((p.m_pad + 255) / 256), 256, 0, stream>>>(
-      args.row_bound, p.m_pad, kImageNegInf);
+  const int64_t n_bounds = p.m_pad * kBoundSlots;
+  fill_i32_kernel<<<static_cast<unsigned>((n_bounds + 255) / 256), 256, 0, stream>>>(
+      args.row_bound, n_bounds, kImageNegInf);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   e = launch_plan(p, mq, mk, args, stream);

@@ -75,6 +75,27 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* st
   }
 }
 
+// ---------------------------------------------------------------- global scalars
+// Relaxed gpu-scope load that the compiler may not move past other volatile
+// asm: issued early, its latency hides behind the work that follows.
+__device__ __forceinline__ int32_t ld_relaxed_gpu(const int32_t* p) {
+  int32_t v;
+  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ int4 ld_relaxed_gpu_v4(const int32_t* p) {  // p 16-byte aligned
+  int4 v;
+  asm volatile("ld.relaxed.gpu.global.v4.s32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+// Fire-and-forget signed max at gpu scope (no value returned, no round trip).
+__device__ __forceinline__ void red_max_gpu(int32_t* p, int32_t v) {
+  asm volatile("red.relaxed.gpu.global.max.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

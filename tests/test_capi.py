@@ -96,8 +96,8 @@ def test_workspace_plan():
     lib = _lib.load()
     # 8192 queries x 1M keys (the op-at-scale shape): 64 query tiles, 4096 key tiles
     nbytes = lib.dwa_score_topk_workspace(8192, 1 << 20, 1024, 64)
-    # status block + per-row admission bounds + one partial list per key split
-    assert nbytes > 0 and (nbytes - 256 - 8192 * 4) % (64 * 8192 * 8) == 0
+    # status block + per-row admission bounds (16 int32 slots) + one partial list per key split
+    assert nbytes > 0 and (nbytes - 256 - 8192 * 64) % (64 * 8192 * 8) == 0
     assert lib.dwa_score_topk_workspace(8192, 1 << 20, 1024, 129) == 0
     assert lib.dwa_score_topk_workspace(0, 10, 8, 1) == 0
 
