@@ -10,8 +10,8 @@ provides device memory, streams and torch.distributed plumbing only.
 from ._lib import DWA_MAX_K, DWAArgumentError, DWAError, load as load_library
 from .assembly import normalise_alpha, weighted_gather_into, weighted_value_sum
 from .pool import ShardSpec, init_normal, new_normal
-from .retrieval import (MultiAspectRetrieval, Retriever, chip_topk, exchange_candidates,
-                        reduce_partials)
+from .retrieval import (HostPipeline, MultiAspectRetrieval, Retriever, chip_topk,
+                        exchange_candidates, reduce_partials)
 from .tiled_topk import (merge_topk, score_topk_into, tiled_topk_fallback, tiled_topk_fused,
                          workspace_bytes)
 
@@ -19,6 +19,6 @@ __all__ = [
     "DWA_MAX_K", "DWAArgumentError", "DWAError", "load_library",
     "normalise_alpha", "weighted_gather_into", "weighted_value_sum", "MultiAspectRetrieval",
     "ShardSpec", "init_normal", "new_normal",
-    "Retriever", "chip_topk", "exchange_candidates", "reduce_partials",
+    "HostPipeline", "Retriever", "chip_topk", "exchange_candidates", "reduce_partials",
     "merge_topk", "score_topk_into", "tiled_topk_fallback", "tiled_topk_fused", "workspace_bytes",
 ]

@@ -226,6 +226,91 @@ class Retriever:
         return int(v.value)
 
 
+class HostPipeline:
+    """Retrieval batches streamed from pinned host memory and back, for serving.
+
+    Each ``submit`` copies one batch of queries [M, d_k] from pinned host
+    memory to the device of rank ``src`` (broadcast to the other ranks when
+    the pool is sharded), runs the retrieval and copies (out, alpha, top_idx)
+    back to the caller's pinned host buffers on rank ``src``.  The upload of a
+    batch and the read-back of the previous one run on their own streams
+    (PCIe carries both directions at once) while the previous / next batch
+    computes, so the copies overlap the kernels instead of adding to them.
+    Two ``Retriever`` instances over the same resident shard alternate, so a
+    batch's result buffers stay untouched until their read-back has finished.
+
+    Host buffers passed to ``submit`` must stay alive and unmodified until
+    ``synchronize`` (or until the result of that batch has been waited for).
+    """
+
+    def __init__(self, keys_local: torch.Tensor, values_local: torch.Tensor, M: int, k: int, *,
+                 src: int = 0, **retriever_kwargs):
+        self.ret = [Retriever(keys_local, values_local, M, k, **retriever_kwargs) for _ in range(2)]
+        r0 = self.ret[0]
+        self.device = r0.device
+        self.group, self.rank, self.world = r0.group, r0.rank, r0.world
+        self.src = int(src)
+        self.q_dev = [torch.empty((r0.M, r0.d_k), dtype=torch.bfloat16, device=self.device)
+                      for _ in range(2)]
+        self.h2d_stream = torch.cuda.Stream(self.device)
+        self.d2h_stream = torch.cuda.Stream(self.device)
+        ev = lambda: torch.cuda.Event()
+        self.h2d_done = [ev(), ev()]
+        self.compute_done = [ev(), ev()]
+        self.d2h_done = [ev(), ev()]
+        self.n = 0
+
+    def submit(self, q_host: torch.Tensor | None, out_host: torch.Tensor | None = None,
+               alpha_host: torch.Tensor | None = None, idx_host: torch.Tensor | None = None):
+        """Enqueue one batch; returns the device results (out, alpha, top_vals, top_idx)
+        of this batch, valid on the current stream."""
+        b, n = self.n % 2, self.n
+        is_src = self.rank == self.src
+        cs = torch.cuda.current_stream(self.device)
+        q = self.q_dev[b]
+        if is_src:
+            if q_host is None:
+                raise ValueError("the source rank needs host queries")
+            with torch.cuda.stream(self.h2d_stream):
+                if n >= 2:  # batch n - 2 read this query buffer
+                    self.h2d_stream.wait_event(self.compute_done[b])
+                q.copy_(q_host, non_blocking=True)
+                self.h2d_done[b].record(self.h2d_stream)
+            cs.wait_event(self.h2d_done[b])
+        if self.world > 1:
+            dist.broadcast(q, src=dist.get_global_rank(self.group, self.src)
+                           if self.group is not None else self.src, group=self.group)
+        if n >= 2:  # batch n - 2's read-back of this retriever's buffers
+            cs.wait_event(self.d2h_done[b])
+        res = self.ret[b](q)
+        self.compute_done[b].record(cs)
+        if is_src:
+            out, alpha, _, top_idx = res
+            with torch.cuda.stream(self.d2h_stream):
+                self.d2h_stream.wait_event(self.compute_done[b])
+                for dst, srct in ((out_host, out), (alpha_host, alpha), (idx_host, top_idx)):
+                    if dst is not None:
+                        dst.copy_(srct, non_blocking=True)
+                self.d2h_done[b].record(self.d2h_stream)
+        else:
+            self.d2h_done[b].record(cs)
+        self.n += 1
+        return res
+
+    def join(self) -> None:
+        """Make the current stream wait for every enqueued copy (no host sync)."""
+        cs = torch.cuda.current_stream(self.device)
+        cs.wait_stream(self.h2d_stream)
+        cs.wait_stream(self.d2h_stream)
+
+    def synchronize(self) -> None:
+        self.join()
+        torch.cuda.current_stream(self.device).synchronize()
+
+    def status(self) -> int:
+        return max(r.status() for r in self.ret)
+
+
 class MultiAspectRetrieval:
     """Parameters and ``pallas_hybrid_forward`` of the reference's retrieval
     module (src/model/retrieval.py:7-46, 204-343) on B200.

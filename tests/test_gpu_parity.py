@@ -312,3 +312,32 @@ def test_pallas_hybrid_forward_matches_reference(lib, golden):
                                atol=1e-3)
     np.testing.assert_allclose(alpha_raw.cpu().numpy(), golden["sharded/alpha_raw_seq"], rtol=RTOL,
                                atol=1e-3)
+
+
+def test_host_pipeline_matches_retriever(lib):
+    """HostPipeline (pinned host in, pinned host out, copies overlapped with the
+    neighbouring batches' kernels) returns, batch by batch, exactly what a
+    direct Retriever call returns for the same queries."""
+    M, N, d, k = 600, 40000, 256, 32
+    keys = lib.new_normal(N, d, seed=21, stddev=d ** -0.5, device=_dev())
+    values = lib.new_normal(N, d, seed=22, device=_dev())
+    batches = [lib.new_normal(M, d, seed=30 + i, device=_dev()) for i in range(5)]
+    ref = lib.Retriever(keys, values, M, k, lambda_sharp=2.0, tau=0.1, T=0.9, use_sigmoid=True)
+    want = []
+    for q in batches:
+        out, alpha, _, idx = ref(q)
+        want.append((out.cpu().clone(), alpha.cpu().clone(), idx.cpu().clone()))
+    pipe = lib.HostPipeline(keys, values, M, k, lambda_sharp=2.0, tau=0.1, T=0.9,
+                            use_sigmoid=True)
+    q_host = [q.cpu().pin_memory() for q in batches]
+    got = [(torch.empty((M, d), dtype=torch.float32).pin_memory(),
+            torch.empty((M, k), dtype=torch.float32).pin_memory(),
+            torch.empty((M, k), dtype=torch.int32).pin_memory()) for _ in batches]
+    for qh, (oh, ah, ih) in zip(q_host, got):
+        pipe.submit(qh, oh, ah, ih)
+    pipe.synchronize()
+    assert pipe.status() == 0
+    for (oh, ah, ih), (ow, aw, iw) in zip(got, want):
+        assert torch.equal(ih, iw)
+        assert torch.equal(ah, aw)
+        assert torch.equal(oh, ow)
