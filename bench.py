@@ -357,9 +357,12 @@ def run_ours(args, wl):
         dist.barrier(device_ids=[local_rank])
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = _cpu_baseline(args, wl, keys, values, queries[0])
-    if args.lm:
+    if args.lm or not args.no_assembly:
         del r, keys, values, queries
         torch.cuda.empty_cache()
+    if not args.no_assembly:
+        line["assembly"] = measure_assembly(world, rank, local_rank, group)
+    if args.lm:
         names = [n for n in args.lm.split(",") if n and (n != "small_char" or world == 1)]
         line["lm"] = [measure_lm(n, world, rank, local_rank) for n in names]
     if rank == 0:
@@ -367,6 +370,75 @@ def run_ours(args, wl):
     if world > 1:
         dist.destroy_process_group()
     return 0
+
+
+def measure_assembly(world, rank, local_rank, group, warmup=3, steps=10):
+    """WeightAssembler (per-position low-rank consumer of the retrieved rows,
+    assembly.py:75-128) on the reference's 1B layout: d_A = d_B = 1280, r = 8,
+    D = 21760, k = 16, pool of 16384 rows row-sharded over the ranks, 8192
+    tokens per step (batch 8 x seq 1024).  Indices are synthetic, uniform over
+    the pool, distinct per token; alpha normalised random weights."""
+    import torch
+    import torch.distributed as dist
+
+    import computd_b200 as cb
+
+    d_A = d_B = 1280
+    r, k, N, M = 8, 16, 16384, 8192
+    D = d_B * r + r * d_A + d_B
+    dev = torch.device("cuda", local_rank)
+    spec = cb.ShardSpec(N, rank, world)
+    vectors = cb.new_normal(spec.n_local, D, seed=41, stddev=0.02, row_offset=spec.row_begin,
+                            device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(43)
+    h = torch.randn((M, d_A), device=dev, generator=g).to(torch.bfloat16)
+    idx = torch.argsort(torch.rand((M, N), device=dev, generator=g), dim=1)[:, :k].to(torch.int32)
+    alpha = torch.rand((M, k), device=dev, generator=g)
+    alpha = alpha / alpha.sum(-1, keepdim=True)
+    asm = cb.WeightAssembler(d_A, d_B, r, device=dev)
+    asm.W_base = (torch.randn((d_B, d_A), device=dev, generator=g) * d_A ** -0.5).to(torch.bfloat16)
+    grp = group if world > 1 else None
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+
+    for _ in range(warmup):
+        asm(h, alpha, idx, vectors, group=grp)
+    barrier()
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    e0.record()
+    for _ in range(steps):
+        asm(h, alpha, idx, vectors, group=grp)
+    e1.record()
+    barrier()
+    # the fused delta kernel alone (this rank's owned rows)
+    for _ in range(steps):
+        cb.lowrank_delta(h, alpha, idx, vectors, d_A, d_B, r, row_begin=spec.row_begin)
+    e2.record()
+    barrier()
+    t = torch.tensor([e0.elapsed_time(e1) / steps, e1.elapsed_time(e2) / steps],
+                     dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, ms_delta = float(t[0]), float(t[1])
+    owned = float(((idx >= spec.row_begin) & (idx < spec.row_end)).sum())
+    # algorithmic bytes of the delta kernel: each owned selected row's U, V and b
+    # blocks once, h once per token, delta written once
+    bytes_delta = owned * (D * 2.0) + M * (d_A * 2.0 + d_B * 4.0)
+    hbm = _peaks()[2]
+    del vectors, h, idx, alpha, asm
+    torch.cuda.empty_cache()
+    return {"config": "reference 1B assembly layout (d_A=d_B=1280, r=8, D=21760, k=16, N=16384)",
+            "tokens_per_step": M, "tokens_per_s": M / (ms * 1e-3), "unit": "tokens/s",
+            "ms_per_step": ms, "pool_rows_per_gpu": spec.n_local,
+            "roofline": {"bound": "hbm", "kernel": "lowrank_delta_kernel", "ms_per_launch": ms_delta,
+                         "achieved": bytes_delta / (ms_delta * 1e-3) / 1e9, "peak": hbm,
+                         "unit": "GB/s", "frac": bytes_delta / (ms_delta * 1e-3) / 1e9 / hbm,
+                         "algorithmic_bytes_per_launch": bytes_delta},
+            "data": "synthetic: uniform distinct indices per token, random weights"}
 
 
 def measure_lm(cfg_name, world, rank, local_rank, warmup=3, steps=3):
@@ -482,6 +554,8 @@ def main(argv=None):
     ap.add_argument("--cpu-queries", type=int, default=64,
                     help="queries per CPU sample (CPU baseline / reference arm)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-assembly", action="store_true",
+                    help="skip the WeightAssembler (low-rank consumer) measurement")
     ap.add_argument("--lm", default="small_char,large_1b",
                     help="DWA LM forwards to time after the op (comma list; empty to skip)")
     args = ap.parse_args(argv)

@@ -8,6 +8,7 @@ and the softmax-weighted gather of pool value rows.  All compute runs in
 provides device memory, streams and torch.distributed plumbing only.
 """
 from ._lib import DWA_MAX_K, DWAArgumentError, DWAError, load as load_library
+from .assembler import WeightAssembler, assemble_finish, lowrank_delta, usage_ema_update
 from .assembly import normalise_alpha, weighted_gather_into, weighted_value_sum
 from .pool import ShardSpec, init_normal, new_normal
 from .retrieval import (HostPipeline, MultiAspectRetrieval, Retriever, chip_topk,
@@ -17,6 +18,7 @@ from .tiled_topk import (merge_topk, score_topk_into, tiled_topk_fallback, tiled
 
 __all__ = [
     "DWA_MAX_K", "DWAArgumentError", "DWAError", "load_library",
+    "WeightAssembler", "assemble_finish", "lowrank_delta", "usage_ema_update",
     "normalise_alpha", "weighted_gather_into", "weighted_value_sum", "MultiAspectRetrieval",
     "ShardSpec", "init_normal", "new_normal",
     "HostPipeline", "Retriever", "chip_topk", "exchange_candidates", "reduce_partials",

@@ -54,6 +54,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                     _i64, _c_void_p, _i64, _i32, _c_void_p]),
     "dwa_pool_init_normal": (_i32, [_c_void_p, _i64, _i64, _i64, _i64, ctypes.c_uint64, _f32,
                                     _c_void_p]),
+    "dwa_lowrank_delta": (_i32, [_c_void_p, _i32, _i64, _c_void_p, _c_void_p, _i64, _i32, _c_void_p,
+                                 _i64, _i64, _i64, _i32, _i32, _i32, _c_void_p, _c_void_p]),
+    "dwa_assemble_finish": (_i32, [_c_void_p, _i32, _i64, _c_void_p, _c_void_p, _i64, _i32, _f32,
+                                   _c_void_p, _c_void_p, _f32, _c_void_p, _c_void_p]),
+    "dwa_usage_ema": (_i32, [_c_void_p, _c_void_p, _i64, _i64, _i64, _f32, _f32, _c_void_p,
+                             _c_void_p]),
     "dwa_workspace_status": (_i32, [_c_void_p, _c_void_p, ctypes.POINTER(_i32)]),
 }
 

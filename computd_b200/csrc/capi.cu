@@ -326,6 +326,80 @@ dwa_status dwa_pool_init_normal(void* out, int64_t rows, int64_t cols, int64_t l
   return ok();
 }
 
+dwa_status dwa_lowrank_delta(const void* h, int32_t h_is_bf16, int64_t ldh, const float* alpha,
+                             const int32_t* gidx, int64_t M, int32_t k, const void* vectors,
+                             int64_t row_begin, int64_t row_end, int64_t ldv, int32_t d_A,
+                             int32_t d_B, int32_t r, float* delta, dwa_stream_t stream) {
+  if (M < 0) return fail(DWA_ERR_INVALID_ARG, "dwa_lowrank_delta: negative M");
+  if (M == 0) return ok();
+  if (!h || !alpha || !gidx || !delta)
+    return fail(DWA_ERR_INVALID_ARG, "dwa_lowrank_delta: null h/alpha/gidx/delta");
+  if (k < 1 || k > DWA_MAX_K)
+    return fail(k < 1 ? DWA_ERR_INVALID_ARG : DWA_ERR_UNSUPPORTED_SHAPE,
+                "dwa_lowrank_delta: k=%d outside [1, %d]", k, DWA_MAX_K);
+  if (d_A < 8 || d_A % 8 != 0 || d_A > 8192 || d_B < 8 || d_B % 8 != 0)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE,
+                "dwa_lowrank_delta: d_A=%d (multiple of 8, <= 8192) / d_B=%d (multiple of 8)", d_A,
+                d_B);
+  if (r < 1 || r > 32) return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_lowrank_delta: r=%d outside [1, 32]", r);
+  if (M > INT32_MAX) return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_lowrank_delta: M too large");
+  if (ldh < d_A) return fail(DWA_ERR_INVALID_ARG, "dwa_lowrank_delta: ldh below d_A");
+  if (row_begin < 0 || row_end < row_begin || row_end > INT32_MAX)
+    return fail(DWA_ERR_INVALID_ARG, "dwa_lowrank_delta: bad owned row range");
+  if (row_end > row_begin) {
+    const int64_t need = static_cast<int64_t>(d_B) * r + static_cast<int64_t>(r) * d_A + d_B;
+    if (!vectors) return fail(DWA_ERR_INVALID_ARG, "dwa_lowrank_delta: null vectors");
+    if (ldv < need)
+      return fail(DWA_ERR_INVALID_ARG, "dwa_lowrank_delta: ldv=%lld below d_B r + r d_A + d_B = %lld",
+                  (long long)ldv, (long long)need);
+    if (ldv % 8 != 0 || !aligned(vectors, 16))
+      return fail(DWA_ERR_UNSUPPORTED_SHAPE,
+                  "dwa_lowrank_delta: vectors need 16-byte aligned rows (ldv %% 8 == 0)");
+  }
+  cudaError_t e = dwa::launch_lowrank_delta(h, h_is_bf16 ? 1 : 0, ldh, alpha, gidx, M, k, vectors,
+                                            row_begin, row_end, ldv, d_A, d_B, r, delta,
+                                            static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_lowrank_delta launch");
+  return ok();
+}
+
+dwa_status dwa_assemble_finish(const void* residual, int32_t residual_is_bf16, int64_t ldr,
+                               const float* base, const float* delta, int64_t M, int32_t d_B,
+                               float gamma, const float* ln_scale, const float* ln_bias, float eps,
+                               float* out, dwa_stream_t stream) {
+  if (M < 0) return fail(DWA_ERR_INVALID_ARG, "dwa_assemble_finish: negative M");
+  if (M == 0) return ok();
+  if (!delta || !out) return fail(DWA_ERR_INVALID_ARG, "dwa_assemble_finish: null delta/out");
+  if (d_B < 1) return fail(DWA_ERR_INVALID_ARG, "dwa_assemble_finish: d_B=%d", d_B);
+  if (residual && ldr < d_B) return fail(DWA_ERR_INVALID_ARG, "dwa_assemble_finish: ldr below d_B");
+  if (!(eps >= 0.0f) || !std::isfinite(gamma))
+    return fail(DWA_ERR_INVALID_ARG, "dwa_assemble_finish: eps must be >= 0 and gamma finite");
+  if (M > (int64_t)INT32_MAX * 8) return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_assemble_finish: M too large");
+  cudaError_t e = dwa::launch_assemble_finish(residual, residual_is_bf16 ? 1 : 0, ldr, base, delta,
+                                              M, d_B, gamma, ln_scale, ln_bias, eps, out,
+                                              static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_assemble_finish launch");
+  return ok();
+}
+
+dwa_status dwa_usage_ema(const float* alpha, const int32_t* gidx, int64_t n, int64_t row_begin,
+                         int64_t row_end, float weight, float beta, float* ema,
+                         dwa_stream_t stream) {
+  if (n < 0) return fail(DWA_ERR_INVALID_ARG, "dwa_usage_ema: negative n");
+  if (row_begin < 0 || row_end < row_begin || row_end > INT32_MAX)
+    return fail(DWA_ERR_INVALID_ARG, "dwa_usage_ema: bad owned row range");
+  if (n > 0 && (!alpha || !gidx)) return fail(DWA_ERR_INVALID_ARG, "dwa_usage_ema: null alpha/gidx");
+  if (row_end > row_begin && !ema) return fail(DWA_ERR_INVALID_ARG, "dwa_usage_ema: null ema");
+  if (!std::isfinite(weight) || !std::isfinite(beta))
+    return fail(DWA_ERR_INVALID_ARG, "dwa_usage_ema: weight and beta must be finite");
+  if (n > (int64_t)INT32_MAX * 256 || row_end - row_begin > (int64_t)INT32_MAX * 256)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_usage_ema: too many entries");
+  cudaError_t e = dwa::launch_usage_ema(alpha, gidx, n, row_begin, row_end, weight, beta, ema,
+                                        static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_usage_ema launch");
+  return ok();
+}
+
 dwa_status dwa_workspace_status(const void* ws, dwa_stream_t stream, int32_t* out_status) {
   if (!ws || !out_status) return fail(DWA_ERR_INVALID_ARG, "null workspace or output");
   int32_t v = 0;

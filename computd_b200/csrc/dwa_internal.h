@@ -80,6 +80,20 @@ cudaError_t launch_scatter_add_rows(const float* wts, const int32_t* idx, int64_
                                     int64_t row_end, float* grad, int64_t ldg, int d,
                                     cudaStream_t stream);
 
+// assembly.cu
+size_t lowrank_delta_smem_bytes(int d_A, int k, int r);
+cudaError_t launch_lowrank_delta(const void* h, int h_bf16, int64_t ldh, const float* alpha,
+                                 const int32_t* gidx, int64_t M, int k, const void* vectors,
+                                 int64_t row_begin, int64_t row_end, int64_t ldv, int d_A, int d_B,
+                                 int r, float* delta, cudaStream_t stream);
+cudaError_t launch_assemble_finish(const void* residual, int res_bf16, int64_t ldr,
+                                   const float* base, const float* delta, int64_t M, int d_B,
+                                   float gamma, const float* ln_scale, const float* ln_bias,
+                                   float eps, float* out, cudaStream_t stream);
+cudaError_t launch_usage_ema(const float* alpha, const int32_t* gidx, int64_t n, int64_t row_begin,
+                             int64_t row_end, float weight, float beta, float* ema,
+                             cudaStream_t stream);
+
 cudaError_t launch_pool_init_normal(void* out, int64_t rows, int64_t cols, int64_t ld,
                                     int64_t row_offset, uint64_t seed, float stddev,
                                     cudaStream_t stream);

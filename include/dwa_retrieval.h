@@ -220,6 +220,55 @@ DWA_API dwa_status dwa_pool_init_normal(void* out, int64_t rows, int64_t cols, i
                                 int64_t row_offset, uint64_t seed, float stddev,
                                 dwa_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Low-rank weight assembly: the consumer of the retrieved rows in a DWA
+ * block, WeightAssembler.__call__ with per-position idx
+ * (src/model/assembly.py:75-128).  Pool row layout (assembly.py:10-14):
+ * [U (d_B x r) | V (r x d_A) | b (d_B) | unused], row-major blocks.
+ * ------------------------------------------------------------------------ */
+
+/*
+ * delta[m, :] = sum_j alpha[m, j] (U_j (V_j h[m]) + b_j), j over the entries of
+ * gidx[m, :] owned by this shard, U_j, V_j, b_j the blocks of pool row
+ * vectors[gidx[m, j] - row_begin] (assembly.py:104, 123-127: the reference's
+ * vectors[idx] gather + the three einsums, without materialising the gather).
+ * h: [M, ldh] bf16 (h_is_bf16 = 1) or f32.  alpha f32 [M, k], gidx i32 [M, k].
+ * vectors: bf16 [row_end - row_begin, ldv], ldv >= d_B r + r d_A + d_B.
+ * delta f32 [M, d_B] is overwritten; shards' partial deltas add up.
+ * Requirements: d_A and d_B multiples of 8 with d_A <= 8192, 1 <= r <= 32,
+ * ldv % 8 == 0, 16-byte aligned vectors.
+ */
+DWA_API dwa_status dwa_lowrank_delta(const void* h, int32_t h_is_bf16, int64_t ldh,
+                             const float* alpha, const int32_t* gidx, int64_t M, int32_t k,
+                             const void* vectors, int64_t row_begin, int64_t row_end,
+                             int64_t ldv, int32_t d_A, int32_t d_B, int32_t r,
+                             float* delta, dwa_stream_t stream);
+
+/*
+ * out[m, :] = LayerNorm(residual[m, :] + gamma * (base[m, :] + delta[m, :]))
+ * (assembly.py:128: residual = h_A when d_A == d_B, base = h_A W_base^T +
+ * b_base, computed by the caller's GEMM).  residual (bf16 or f32, stride
+ * ldr) and base (f32 [M, d_B]) may be NULL (zero); ln_scale / ln_bias
+ * (f32 [d_B]) may be NULL (1 / 0).  Mean and variance over the row, then
+ * (x - mean) / sqrt(var + eps) * scale + bias; out f32 [M, d_B].
+ */
+DWA_API dwa_status dwa_assemble_finish(const void* residual, int32_t residual_is_bf16, int64_t ldr,
+                               const float* base, const float* delta, int64_t M, int32_t d_B,
+                               float gamma, const float* ln_scale, const float* ln_bias,
+                               float eps, float* out, dwa_stream_t stream);
+
+/*
+ * Pool-usage EMA (src/training/trainer.py:227-233, src/model/pool.py:52-55):
+ * ema *= beta, then ema[gidx[e] - row_begin] += weight * alpha[e] for the n
+ * entries whose row this shard owns (f32 atomics).  For the reference's
+ * update pass weight = (1 - beta) / n_total; to fold several blocks' entries
+ * into one update call once with beta and then with beta = 1.
+ * ema: f32 [row_end - row_begin].
+ */
+DWA_API dwa_status dwa_usage_ema(const float* alpha, const int32_t* gidx, int64_t n,
+                         int64_t row_begin, int64_t row_end, float weight, float beta,
+                         float* ema, dwa_stream_t stream);
+
 /*
  * Device-side status word of a workspace: DWA_OK, or the first error a
  * kernel recorded there (DWA_ERR_TIMEOUT from a bounded wait).  Copies 4

@@ -17,6 +17,11 @@ reference tree):
 * ``sharded_topk``     — retrieval.py:280-313 (shard_map over a row-sharded pool)
 * ``normalise``        — retrieval.py:326 (alpha = v / (sum v + 1e-8))
 * ``weighted_sum``     — src/model/assembly.py:104,127 (vectors[idx], alpha-weighted sum)
+* ``lowrank_delta``    — src/model/assembly.py:110-127 (U/V/b split, hV, h_delta, b_delta)
+* ``assemble_forward`` — assembly.py:75-128, WeightAssembler.__call__ per-position path
+                         (+ flax nnx.LayerNorm, eps 1e-6)
+* ``usage_ema``        — src/training/trainer.py:227-233 (scatter of alpha / idx.size)
+                         + src/model/pool.py:52-55 (EMA with beta)
 * ``pool_init_normal`` — the counter-based generator of computd_b200/csrc/pool_init.cu
                          (Philox4x32-10, Salmon et al. SC'11, + Box-Muller)
 
@@ -172,6 +177,65 @@ def retrieve(q, keys, values, k, lambda_sharp=1.0, tau=0.0, T=1.0, use_sigmoid=F
         v, i = sharded_topk(q, keys, k, P, lambda_sharp, tau, T, use_sigmoid, accum=accum)
     a = normalise(v)
     return weighted_sum(a, i, values, accum=accum), a, v, i
+
+
+# --------------------------------------------------------------------------- low-rank assembly
+def split_vectors(sel: np.ndarray, d_A: int, d_B: int, r: int):
+    """assembly.py:61-63 / 110-112: pool vector = [U (d_B x r) | V (r x d_A) | b (d_B)]."""
+    off_V, off_b = d_B * r, d_B * r + r * d_A
+    U = sel[..., :off_V].reshape(*sel.shape[:-1], d_B, r)
+    V = sel[..., off_V:off_b].reshape(*sel.shape[:-1], r, d_A)
+    b = sel[..., off_b:off_b + d_B]
+    return U, V, b
+
+
+def lowrank_delta(h: np.ndarray, alpha: np.ndarray, idx: np.ndarray, vectors: np.ndarray,
+                  d_A: int, d_B: int, r: int, accum=np.float64) -> np.ndarray:
+    """assembly.py:123-127 (per-position idx): h_delta + b_delta for rows h [M, d_A].
+
+    hV = h . V_j (r values per selected vector), h_delta = sum_j alpha_j U_j hV_j,
+    b_delta = sum_j alpha_j b_j.
+    """
+    sel = np.asarray(vectors, dtype=accum)[idx]            # [M, k, D]
+    U, V, b = split_vectors(sel, d_A, d_B, r)
+    h = np.asarray(h, dtype=accum)
+    a = np.asarray(alpha, dtype=accum)
+    hV = np.einsum("md,mkrd->mkr", h, V)
+    h_delta = np.einsum("mkr,mkir->mi", hV * a[..., None], U)
+    b_delta = np.einsum("mk,mkj->mj", a, b)
+    return h_delta + b_delta
+
+
+def layer_norm(x: np.ndarray, scale: np.ndarray, bias: np.ndarray, eps: float = 1e-6) -> np.ndarray:
+    """flax.nnx.LayerNorm over the last axis (the norm of assembly.py:52): mean and
+    variance of x, (x - mean) / sqrt(var + eps) * scale + bias."""
+    x = np.asarray(x, dtype=np.float64)
+    mean = x.mean(axis=-1, keepdims=True)
+    var = np.maximum((x * x).mean(axis=-1, keepdims=True) - mean * mean, 0.0)
+    return (x - mean) / np.sqrt(var + eps) * scale + bias
+
+
+def assemble_forward(h: np.ndarray, alpha: np.ndarray, idx: np.ndarray, vectors: np.ndarray,
+                     W_base: np.ndarray, b_base: np.ndarray, gamma: float, ln_scale: np.ndarray,
+                     ln_bias: np.ndarray, d_A: int, d_B: int, r: int, eps: float = 1e-6) -> np.ndarray:
+    """WeightAssembler.__call__, per-position path (assembly.py:75-82, 84-85, 104, 110-128):
+    LayerNorm(residual + gamma * (h W_base^T + b_base + h_delta + b_delta)),
+    residual = h when d_A == d_B, else 0."""
+    h64 = np.asarray(h, dtype=np.float64)
+    base = h64 @ np.asarray(W_base, np.float64).T + np.asarray(b_base, np.float64)
+    x = gamma * (base + lowrank_delta(h, alpha, idx, vectors, d_A, d_B, r))
+    if d_A == d_B:
+        x = x + h64
+    return layer_norm(x, ln_scale, ln_bias, eps)
+
+
+def usage_ema(ema: np.ndarray, alpha: np.ndarray, idx: np.ndarray, beta: float = 0.99) -> np.ndarray:
+    """trainer.py:227-233 + pool.py:52-55 (per-position idx): alpha_sum = zeros(N) with
+    alpha / idx.size scatter-added at idx; ema' = beta * ema + (1 - beta) * alpha_sum."""
+    alpha_sum = np.zeros(ema.shape[0], dtype=np.float64)
+    np.add.at(alpha_sum, np.asarray(idx).reshape(-1),
+              np.asarray(alpha, np.float64).reshape(-1) / np.asarray(idx).size)
+    return beta * np.asarray(ema, np.float64) + (1.0 - beta) * alpha_sum
 
 
 # --------------------------------------------------------------------------- comparator

@@ -168,6 +168,24 @@ class Module:
     pass
 
 
+class LayerNorm:
+    """flax.nnx.LayerNorm's published computation over the last axis (epsilon 1e-6,
+    fast variance): mean, var = max(mean(x^2) - mean^2, 0),
+    (x - mean) / sqrt(var + eps) * scale + bias, in float32."""
+
+    def __init__(self, num_features, *, epsilon=1e-6, rngs=None, scale=None, bias=None):
+        self.epsilon = epsilon
+        self.scale = _Var(np.ones(num_features, np.float32) if scale is None else scale)
+        self.bias = _Var(np.zeros(num_features, np.float32) if bias is None else bias)
+
+    def __call__(self, x):
+        x = np.asarray(x, np.float32)
+        mean = x.mean(axis=-1, keepdims=True)
+        var = np.maximum((x * x).mean(axis=-1, keepdims=True) - mean * mean, 0.0)
+        y = (x - mean) / np.sqrt(var + np.float32(self.epsilon))
+        return (y * self.scale.value + self.bias.value).astype(np.float32)
+
+
 class Rngs:
     def __init__(self, *a, **k):
         pass
@@ -215,6 +233,7 @@ def install() -> None:
     flax = types.ModuleType("flax")
     nnx = types.ModuleType("flax.nnx")
     nnx.Module, nnx.Param, nnx.Variable, nnx.Rngs = Module, _Var, _Var, Rngs
+    nnx.LayerNorm = LayerNorm
     flax.nnx = nnx
     sys.modules.update({
         "jax": jax, "jax.numpy": jnp, "jax.lax": lax, "jax.nn": nn,

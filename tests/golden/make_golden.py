@@ -8,6 +8,9 @@ all_gather, shard_map, ...).  What runs is the reference's own source:
 * ``src/model/retrieval.py``     ``MultiAspectRetrieval.pallas_hybrid_forward``
                                   with a 4-device ``shard_map``         (lines 204-343)
 * ``src/model/assembly.py``      ``WeightAssembler.assemble``        (lines 47-73)
+                                  ``WeightAssembler.__call__``, per-position idx
+                                  with a flax-LayerNorm stand-in       (lines 75-128)
+* ``src/model/pool.py``          ``VectorPool.update_ema``           (lines 52-55)
 
 Inputs are float32 arrays holding bf16-representable values (the B200 kernel
 takes bf16, so both sides see identical inputs).  Run from the repository
@@ -135,6 +138,51 @@ def case_sharded(ref_tk, ref_ret, ref_asm, rng, out, n_chips=4):
     out["sharded/alpha_raw_seq"] = np.asarray(alpha_raw_seq, np.float32)
 
 
+def case_assembler(ref_asm, ref_pool, rng, out, name, d_A, d_B, r):
+    """WeightAssembler.__call__ on per-position (hybrid) idx, non-zero W_base / b_base /
+    gamma / LayerNorm parameters, pool rows wider than U|V|b; then VectorPool.update_ema
+    on the per-position usage scatter."""
+    B, seq, k, N = 2, 24, 6, 300
+    D = d_B * r + r * d_A + d_B + 8
+    vectors = bf16_round((rng.standard_normal((N, D)) * 0.3).astype(np.float32))
+    h = bf16_round(rng.standard_normal((B, seq, d_A)).astype(np.float32))
+    raw = np.exp(rng.standard_normal((B, seq, k))).astype(np.float32)
+    alpha = (raw / (raw.sum(-1, keepdims=True) + np.float32(1e-8))).astype(np.float32)
+    idx = np.stack([rng.choice(N, size=k, replace=False) for _ in range(B * seq)])
+    idx = idx.reshape(B, seq, k).astype(np.int32)
+    W_base = bf16_round((rng.standard_normal((d_B, d_A)) * d_A ** -0.5).astype(np.float32))
+    b_base = bf16_round((0.1 * rng.standard_normal(d_B)).astype(np.float32))
+    gamma = np.float32(0.7)
+    ln_scale = (1.0 + 0.1 * rng.standard_normal(d_B)).astype(np.float32)
+    ln_bias = (0.1 * rng.standard_normal(d_B)).astype(np.float32)
+    asm = types.SimpleNamespace(d_A=d_A, d_B=d_B, r=r, _off_V=d_B * r, _off_b=d_B * r + r * d_A,
+                                _end_b=d_B * r + r * d_A + d_B)
+    asm.W_base = types.SimpleNamespace(value=W_base)
+    asm.b_base = types.SimpleNamespace(value=b_base)
+    asm.gamma = types.SimpleNamespace(value=gamma)
+    asm.norm = jax_standin.LayerNorm(d_B, scale=ln_scale, bias=ln_bias)
+    h_mid = ref_asm.WeightAssembler.__call__(asm, h, alpha, idx, vectors)
+    out[f"{name}/dims"] = np.array([d_A, d_B, r, D])
+    out[f"{name}/vectors"] = _bits(vectors)
+    out[f"{name}/h"] = _bits(h.reshape(B * seq, d_A))
+    out[f"{name}/alpha"] = alpha.reshape(B * seq, k)
+    out[f"{name}/idx"] = idx.reshape(B * seq, k)
+    out[f"{name}/W_base"] = W_base
+    out[f"{name}/b_base"] = b_base
+    out[f"{name}/gamma"] = np.array(gamma)
+    out[f"{name}/ln_scale"] = ln_scale
+    out[f"{name}/ln_bias"] = ln_bias
+    out[f"{name}/h_mid"] = np.asarray(h_mid, np.float32).reshape(B * seq, d_B)
+    # usage EMA: trainer.py:227-233 scatter restated here, pool.py:52-55 executed
+    ema0 = np.abs(rng.standard_normal(N)).astype(np.float32) * 0.01
+    alpha_sum = np.zeros(N, np.float32)
+    np.add.at(alpha_sum, idx.reshape(-1), alpha.reshape(-1) / np.float32(idx.size))
+    pool = types.SimpleNamespace(ema_usage=types.SimpleNamespace(value=ema0.copy()))
+    ref_pool.VectorPool.update_ema(pool, alpha_sum, 0.99)
+    out[f"{name}/ema0"] = ema0
+    out[f"{name}/ema1"] = np.asarray(pool.ema_usage.value, np.float32)
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--reference", default="/root/reference",
@@ -146,6 +194,7 @@ def main(argv=None) -> int:
     sys.path.insert(0, args.reference)
     from src.kernels import tiled_topk as ref_tk  # noqa: E402  (reference code)
     from src.model import assembly as ref_asm  # noqa: E402
+    from src.model import pool as ref_pool  # noqa: E402
     from src.model import retrieval as ref_ret  # noqa: E402
 
     rng = np.random.default_rng(20261201)
@@ -155,6 +204,8 @@ def main(argv=None) -> int:
     case_tiled_topk(ref_tk, "odd", rng, 33, 777, 40, 5, 2.0, -0.25, 1.3, True, out)
     case_ties(ref_tk, rng, out)
     case_sharded(ref_tk, ref_ret, ref_asm, rng, out)
+    case_assembler(ref_asm, ref_pool, rng, out, "asm_eq", 48, 48, 4)
+    case_assembler(ref_asm, ref_pool, rng, out, "asm_ne", 40, 24, 8)
     np.savez_compressed(args.out, **out)
     print(f"wrote {args.out}: {len(out)} arrays")
     return 0

@@ -144,3 +144,40 @@ def test_compare_rows():
     bad = ref.copy()
     bad[3, 3] += 0.5
     assert O.compare_rows(bad, ref)
+
+
+def _asm_case(golden, name):
+    d_A, d_B, r, D = (int(x) for x in golden[f"{name}/dims"])
+    return dict(h=O.bits_to_f32(golden[f"{name}/h"]), alpha=golden[f"{name}/alpha"],
+                idx=golden[f"{name}/idx"], vectors=O.bits_to_f32(golden[f"{name}/vectors"]),
+                W_base=golden[f"{name}/W_base"], b_base=golden[f"{name}/b_base"],
+                gamma=float(golden[f"{name}/gamma"]), ln_scale=golden[f"{name}/ln_scale"],
+                ln_bias=golden[f"{name}/ln_bias"], d_A=d_A, d_B=d_B, r=r)
+
+
+@pytest.mark.parametrize("name", ["asm_eq", "asm_ne"])
+def test_oracle_assembler_matches_reference_call(golden, name):
+    """WeightAssembler.__call__ (per-position idx, residual when d_A == d_B) as run
+    by the reference's own code."""
+    c = _asm_case(golden, name)
+    got = O.assemble_forward(c["h"], c["alpha"], c["idx"], c["vectors"], c["W_base"], c["b_base"],
+                             c["gamma"], c["ln_scale"], c["ln_bias"], c["d_A"], c["d_B"], c["r"])
+    np.testing.assert_allclose(got, golden[f"{name}/h_mid"], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("name", ["asm_eq", "asm_ne"])
+def test_oracle_usage_ema_matches_reference(golden, name):
+    got = O.usage_ema(golden[f"{name}/ema0"], golden[f"{name}/alpha"], golden[f"{name}/idx"], 0.99)
+    np.testing.assert_allclose(got, golden[f"{name}/ema1"], rtol=1e-6, atol=1e-9)
+
+
+def test_lowrank_delta_catches_planted_factor_swap(golden):
+    """A restatement that swapped the U and V blocks of the pool rows must not pass."""
+    c = _asm_case(golden, "asm_eq")
+    good = O.lowrank_delta(c["h"], c["alpha"], c["idx"], c["vectors"], c["d_A"], c["d_B"], c["r"])
+    d_A, d_B, r = c["d_A"], c["d_B"], c["r"]
+    swapped = c["vectors"].copy()
+    nU = d_B * r
+    swapped[:, :nU], swapped[:, nU:2 * nU] = c["vectors"][:, nU:2 * nU], c["vectors"][:, :nU]
+    bad = O.lowrank_delta(c["h"], c["alpha"], c["idx"], swapped, d_A, d_B, r)
+    assert np.abs(bad - good).max() > 1e-2 * np.abs(good).max()
