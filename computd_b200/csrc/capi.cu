@@ -326,6 +326,87 @@ dwa_status dwa_pool_init_normal(void* out, int64_t rows, int64_t cols, int64_t l
   return ok();
 }
 
+dwa_status dwa_peer_alloc(size_t bytes, void** out_ptr, void* out_handle) {
+  if (!out_ptr || !out_handle || bytes == 0)
+    return fail(DWA_ERR_INVALID_ARG, "dwa_peer_alloc: null output or zero size");
+  static_assert(sizeof(cudaIpcMemHandle_t) == DWA_IPC_HANDLE_BYTES, "IPC handle size");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_peer_alloc cudaMalloc");
+  e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(out_handle), p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "dwa_peer_alloc");
+  }
+  *out_ptr = p;
+  return ok();
+}
+
+dwa_status dwa_peer_open(const void* handle, void** out_ptr) {
+  if (!handle || !out_ptr) return fail(DWA_ERR_INVALID_ARG, "dwa_peer_open: null argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(out_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_peer_open cudaIpcOpenMemHandle");
+  return ok();
+}
+
+dwa_status dwa_peer_close(void* ptr) {
+  if (!ptr) return fail(DWA_ERR_INVALID_ARG, "dwa_peer_close: null pointer");
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_peer_close");
+  return ok();
+}
+
+dwa_status dwa_peer_free(void* ptr) {
+  if (!ptr) return fail(DWA_ERR_INVALID_ARG, "dwa_peer_free: null pointer");
+  cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_peer_free");
+  return ok();
+}
+
+dwa_status dwa_peer_signal(void* const* flag_bases, int32_t P, int32_t my_rank, int32_t value,
+                           dwa_stream_t stream) {
+  if (!flag_bases) return fail(DWA_ERR_INVALID_ARG, "dwa_peer_signal: null flag table");
+  if (P < 1 || P > DWA_MAX_PEERS || my_rank < 0 || my_rank >= P)
+    return fail(DWA_ERR_INVALID_ARG, "dwa_peer_signal: P=%d / rank %d", P, my_rank);
+  int32_t* bases[DWA_MAX_PEERS];
+  for (int p = 0; p < P; ++p) {
+    if (!flag_bases[p] || !aligned(flag_bases[p], 4))
+      return fail(DWA_ERR_INVALID_ARG, "dwa_peer_signal: bad flag array of rank %d", p);
+    bases[p] = static_cast<int32_t*>(flag_bases[p]);
+  }
+  cudaError_t e = dwa::launch_peer_signal(bases, P, my_rank, value, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_peer_signal launch");
+  return ok();
+}
+
+dwa_status dwa_merge_topk_peers(const void* const* packed, int32_t P, int64_t M, int32_t k,
+                                const int32_t* flags, int32_t step, float* out_vals,
+                                int32_t* out_idx, int32_t* status, dwa_stream_t stream) {
+  if (M < 0) return fail(DWA_ERR_INVALID_ARG, "dwa_merge_topk_peers: negative M");
+  if (M == 0) return ok();
+  if (!packed || !flags || !out_vals || !out_idx || !status)
+    return fail(DWA_ERR_INVALID_ARG, "dwa_merge_topk_peers: null argument");
+  if (P < 1 || P > DWA_MAX_PEERS) return fail(DWA_ERR_INVALID_ARG, "dwa_merge_topk_peers: P=%d", P);
+  if (k < 1 || k > DWA_MERGE_MAX_K)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_merge_topk_peers: k=%d outside [1, %d]", k,
+                DWA_MERGE_MAX_K);
+  if (M > (int64_t)INT32_MAX * 8) return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_merge_topk_peers: M too large");
+  const int32_t* lists[DWA_MAX_PEERS];
+  for (int p = 0; p < P; ++p) {
+    if (!packed[p] || !aligned(packed[p], 8))
+      return fail(DWA_ERR_INVALID_ARG, "dwa_merge_topk_peers: bad list pointer of rank %d", p);
+    lists[p] = static_cast<const int32_t*>(packed[p]);
+  }
+  cudaError_t e = dwa::launch_merge_topk_peers(lists, P, M, k, flags, step, out_vals, out_idx,
+                                               status, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_merge_topk_peers launch");
+  return ok();
+}
+
 dwa_status dwa_lowrank_delta(const void* h, int32_t h_is_bf16, int64_t ldh, const float* alpha,
                              const int32_t* gidx, int64_t M, int32_t k, const void* vectors,
                              int64_t row_begin, int64_t row_end, int64_t ldv, int32_t d_A,

@@ -80,6 +80,14 @@ cudaError_t launch_scatter_add_rows(const float* wts, const int32_t* idx, int64_
                                     int64_t row_end, float* grad, int64_t ldg, int d,
                                     cudaStream_t stream);
 
+// merge_topk.cu: NVLink peer exchange
+int max_peers();
+cudaError_t launch_peer_signal(int32_t* const* flag_bases, int n, int my_rank, int value,
+                               cudaStream_t stream);
+cudaError_t launch_merge_topk_peers(const int32_t* const* packed, int n, int64_t M, int k,
+                                    const int32_t* flags, int step, float* out_vals,
+                                    int32_t* out_idx, int* status, cudaStream_t stream);
+
 // assembly.cu
 size_t lowrank_delta_smem_bytes(int d_A, int k, int r);
 cudaError_t launch_lowrank_delta(const void* h, int h_bf16, int64_t ldh, const float* alpha,

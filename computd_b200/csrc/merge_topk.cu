@@ -22,6 +22,7 @@
 #include <cmath>
 
 #include "dwa_internal.h"
+#include "sm100_ptx.cuh"
 #include "topk_heap.cuh"
 
 namespace dwa {
@@ -32,9 +33,16 @@ constexpr int kWarps = 8;           // rows per block
 constexpr int kSlots = kMaxSplits / 32;  // lists per lane
 constexpr int kCache = 4;           // entries cached per list
 
+constexpr int kMaxPeers = 16;       // peer lists of the NVLink exchange
+
 struct MergeArgs {
   const float* cv;
   const int32_t* ci;
+  // peer mode: list l is peer[l] + row * stride_row, (score bits, index) pairs
+  const int32_t* peer[kMaxPeers];
+  const int32_t* flags;  // this GPU's flag words, one per peer: >= wait_step when ready
+  int wait_step;
+  int* status;
   int64_t stride_list, stride_pos, stride_row;
   int64_t M;
   int64_t idx_offset;
@@ -67,17 +75,33 @@ struct ListCursor {
   int off;   // current head = entry `off` of the cache
 };
 
+// kPeer: the lists live in other GPUs' memory and were written by their
+// kernels; plain (coherent) loads after the acquire on the flags, not the
+// read-only path.
+template <bool kPeer>
 __device__ __forceinline__ void load_block(ListCursor& L, const float* vp, const int32_t* ip,
                                            int64_t stride_pos, int k_in) {
 #pragma unroll
   for (int e = 0; e < kCache; ++e) {
     const int p = L.base + e;
     const bool in = p < k_in;
-    L.s[e] = in ? __ldg(vp + p * stride_pos) : -INFINITY;
-    L.i[e] = in ? __ldg(ip + p * stride_pos) : kSentinelIdx;
+    if constexpr (kPeer) {
+      L.s[e] = in ? vp[p * stride_pos] : -INFINITY;
+      L.i[e] = in ? ip[p * stride_pos] : kSentinelIdx;
+    } else {
+      L.s[e] = in ? __ldg(vp + p * stride_pos) : -INFINITY;
+      L.i[e] = in ? __ldg(ip + p * stride_pos) : kSentinelIdx;
+    }
   }
 }
 
+__device__ __forceinline__ int32_t ld_acquire_sys(const int32_t* p) {
+  int32_t v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <bool kPeer>
 __global__ void __launch_bounds__(kWarps * 32) merge_sorted_kernel(const MergeArgs a) {
   __shared__ float st_s[kWarps][DWA_MERGE_MAX_K];
   __shared__ int32_t st_i[kWarps][DWA_MERGE_MAX_K];
@@ -85,6 +109,27 @@ __global__ void __launch_bounds__(kWarps * 32) merge_sorted_kernel(const MergeAr
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + w;
   if (row >= a.M) return;  // warp-uniform; only warp-level synchronisation below
+  if constexpr (kPeer) {
+    // Wait (bounded) until every peer has published this step's lists.
+    bool ready = true;
+    if (lane < a.n_lists) {
+      const uint64_t t0 = globaltimer_ns();
+      while (ld_acquire_sys(a.flags + lane) < a.wait_step) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          ready = false;
+          break;
+        }
+      }
+    }
+    if (!__all_sync(0xffffffffu, ready)) {
+      if (lane == 0) atomicCAS(a.status, 0, kStatusTimeout);
+      for (int j = lane; j < a.k; j += 32) {
+        a.out_v[row * a.k + j] = -INFINITY;
+        a.out_i[row * a.k + j] = -1;
+      }
+      return;
+    }
+  }
 
   ListCursor cur[kSlots];
   const float* vbase[kSlots];
@@ -95,9 +140,14 @@ __global__ void __launch_bounds__(kWarps * 32) merge_sorted_kernel(const MergeAr
     cur[u].base = 0;
     cur[u].off = 0;
     if (l < a.n_lists) {
-      vbase[u] = a.cv + l * a.stride_list + row * a.stride_row;
-      ibase[u] = a.ci + l * a.stride_list + row * a.stride_row;
-      load_block(cur[u], vbase[u], ibase[u], a.stride_pos, a.k_in);
+      if constexpr (kPeer) {
+        ibase[u] = a.peer[l] + row * a.stride_row + 1;
+        vbase[u] = reinterpret_cast<const float*>(a.peer[l] + row * a.stride_row);
+      } else {
+        vbase[u] = a.cv + l * a.stride_list + row * a.stride_row;
+        ibase[u] = a.ci + l * a.stride_list + row * a.stride_row;
+      }
+      load_block<kPeer>(cur[u], vbase[u], ibase[u], a.stride_pos, a.k_in);
     } else {
       vbase[u] = nullptr;
       ibase[u] = nullptr;
@@ -149,7 +199,7 @@ __global__ void __launch_bounds__(kWarps * 32) merge_sorted_kernel(const MergeAr
             cur[u].off = 0;
             cur[u].base += kCache;
             if (vbase[u] != nullptr) {
-              load_block(cur[u], vbase[u], ibase[u], a.stride_pos, a.k_in);
+              load_block<kPeer>(cur[u], vbase[u], ibase[u], a.stride_pos, a.k_in);
             }
           }
         }
@@ -201,7 +251,7 @@ cudaError_t launch_merge_topk(const float* cand_vals, const int32_t* cand_idx, i
   if (M <= 0) return cudaSuccess;
   if (n_lists < 1 || n_lists > kMaxSplits || k < 1 || k > DWA_MERGE_MAX_K)
     return cudaErrorInvalidValue;
-  MergeArgs a;
+  MergeArgs a{};
   a.cv = cand_vals;
   a.ci = cand_idx;
   a.stride_list = stride_list;
@@ -220,7 +270,65 @@ cudaError_t launch_merge_topk(const float* cand_vals, const int32_t* cand_idx, i
   a.out_v = out_vals;
   a.out_i = out_idx;
   const int64_t blocks = (M + kWarps - 1) / kWarps;
-  merge_sorted_kernel<<<static_cast<unsigned>(blocks), kWarps * 32, 0, stream>>>(a);
+  merge_sorted_kernel<false><<<static_cast<unsigned>(blocks), kWarps * 32, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+namespace {
+__device__ __forceinline__ void st_release_sys(int32_t* p, int32_t v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+struct SignalArgs {
+  int32_t* flag_base[kMaxPeers];
+  int n, my_rank, value;
+};
+
+// One thread: everything this GPU's earlier kernels on the stream wrote is made
+// visible system-wide, then flag[my_rank] = value on every peer (release).
+__global__ void peer_signal_kernel(const SignalArgs a) {
+  __threadfence_system();
+  for (int p = 0; p < a.n; ++p) st_release_sys(a.flag_base[p] + a.my_rank, a.value);
+}
+}  // namespace
+
+int max_peers() { return kMaxPeers; }
+
+cudaError_t launch_peer_signal(int32_t* const* flag_bases, int n, int my_rank, int value,
+                               cudaStream_t stream) {
+  if (n < 1 || n > kMaxPeers || my_rank < 0 || my_rank >= n) return cudaErrorInvalidValue;
+  SignalArgs a{};
+  for (int p = 0; p < n; ++p) a.flag_base[p] = flag_bases[p];
+  a.n = n;
+  a.my_rank = my_rank;
+  a.value = value;
+  peer_signal_kernel<<<1, 1, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_merge_topk_peers(const int32_t* const* packed, int n, int64_t M, int k,
+                                    const int32_t* flags, int step, float* out_vals,
+                                    int32_t* out_idx, int* status, cudaStream_t stream) {
+  if (M <= 0) return cudaSuccess;
+  if (n < 1 || n > kMaxPeers || k < 1 || k > DWA_MERGE_MAX_K) return cudaErrorInvalidValue;
+  MergeArgs a{};
+  for (int p = 0; p < n; ++p) a.peer[p] = packed[p];
+  a.flags = flags;
+  a.wait_step = step;
+  a.status = status;
+  a.stride_list = 0;
+  a.stride_pos = 2;
+  a.stride_row = 2 * static_cast<int64_t>(k);
+  a.M = M;
+  a.idx_offset = 0;
+  a.n_lists = n;
+  a.k_in = k;
+  a.k = k;
+  a.transform = 0;
+  a.out_v = out_vals;
+  a.out_i = out_idx;
+  const int64_t blocks = (M + kWarps - 1) / kWarps;
+  merge_sorted_kernel<true><<<static_cast<unsigned>(blocks), kWarps * 32, 0, stream>>>(a);
   return cudaGetLastError();
 }
 

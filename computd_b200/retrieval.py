@@ -11,12 +11,17 @@ Mirrors the reference's multi-chip retrieval, ``MultiAspectRetrieval.pallas_hybr
     alpha      = fv / (sum(fv) + 1e-8)                            (326)
 
 On B200 the ``shard_map`` becomes one process per GPU (torch.distributed over
-NCCL): queries are replicated, rank r holds pool rows [r*N/P, (r+1)*N/P) in
-HBM, the candidate exchange is one NCCL all-gather per array over NVLink, and
-the merge runs on the device.  The value side (assembly.py:104-128) sums only
-owned rows per rank and adds the partial sums with one all-reduce.
+NCCL): queries are replicated and rank r holds pool rows [r*N/P, (r+1)*N/P) in
+HBM.  The candidate exchange and merge run as one kernel that reads the
+other GPUs' lists over NVLink (``PeerExchange``: CUDA IPC buffers, a
+system-scope release flag per rank and step, a bounded wait in the merge);
+an NCCL all-gather + device merge remains selectable.  The value side
+(assembly.py:104-128) sums only owned rows per rank and adds the partial sums
+with one all-reduce.
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -32,6 +37,113 @@ def _group_rank_world(group) -> tuple[int, int]:
     if group is None and not (dist.is_available() and dist.is_initialized()):
         return 0, 1
     return dist.get_rank(group), dist.get_world_size(group)
+
+
+class _DeviceBuffer:
+    """A raw device range seen by torch as a tensor (``__cuda_array_interface__``, no copy)."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 3, "strides": None}
+
+
+class PeerExchange:
+    """Cross-shard candidate exchange + merge over NVLink peer memory.
+
+    The reference's all_gather of every chip's [M, k] candidates followed by the
+    top_k merge (src/model/retrieval.py:295-302) becomes: each rank writes its
+    packed (score bits, global index) lists into its own CUDA-IPC buffer and
+    raises flag[rank] = step on every rank (``dwa_peer_signal``: system fence +
+    release stores); then every rank's merge kernel (``dwa_merge_topk_peers``)
+    waits for all flags of this step (bounded: 2 s, then DWA_ERR_TIMEOUT in the
+    status word) and merges the P lists straight from the other GPUs' memory.
+
+    Buffers alternate by step parity.  A rank rewrites the buffer of step s at
+    step s + 2 only after its own merge of step s + 1, which waited for every
+    rank's step-(s + 1) flag, raised after that rank's merge of step s: so no
+    list is overwritten while a peer still reads it.  Construction is
+    collective over ``group`` (all ranks, same order).
+    """
+
+    _HDR = 256            # bytes: int32 flag words [0, P), status word at byte 192
+    _STATUS_OFF = 192
+
+    def __init__(self, M: int, k: int, group, device: torch.device):
+        self.rank, self.world = _group_rank_world(group)
+        if self.world > 16:
+            raise _lib.DWAArgumentError(_lib.DWA_ERR_UNSUPPORTED_SHAPE, "PeerExchange",
+                                        "more than 16 ranks")
+        self.M, self.k, self.group, self.device = int(M), int(k), group, device
+        self._list_bytes = self.M * self.k * 8
+        nbytes = self._HDR + 2 * self._list_bytes
+        lib = _lib.load()
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_char * 64)()
+        with torch.cuda.device(device):
+            _lib.check(lib.dwa_peer_alloc(nbytes, ctypes.byref(own), handle), "dwa_peer_alloc")
+        self._own = own.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self._opened = []
+        bases = []
+        with torch.cuda.device(device):
+            for p in range(self.world):
+                if p == self.rank:
+                    bases.append(self._own)
+                    continue
+                q = ctypes.c_void_p()
+                _lib.check(lib.dwa_peer_open(handles[p], ctypes.byref(q)), "dwa_peer_open")
+                self._opened.append(q.value)
+                bases.append(q.value)
+        self._bases = bases
+        self._flag_table = (ctypes.c_void_p * self.world)(*bases)
+        self._list_tables = [(ctypes.c_void_p * self.world)(
+            *[b + self._HDR + par * self._list_bytes for b in bases]) for par in range(2)]
+        self._packed = [torch.as_tensor(_DeviceBuffer(self._own + self._HDR + par * self._list_bytes,
+                                                      (self.M, self.k, 2), "<i4"), device=device)
+                        for par in range(2)]
+        self._hdr = torch.as_tensor(_DeviceBuffer(self._own, (self._HDR // 4,), "<i4"), device=device)
+        self.step = 0
+        dist.barrier(group=group, device_ids=[device.index])
+
+    def publish(self, local_vals: torch.Tensor, local_idx: torch.Tensor) -> None:
+        """Pack this rank's [M, k] lists into its buffer and raise its flag on every rank."""
+        self.step += 1
+        buf = self._packed[self.step & 1]
+        buf[..., 0].copy_(local_vals.view(torch.int32))
+        buf[..., 1].copy_(local_idx)
+        lib = _lib.load()
+        with torch.cuda.device(self.device):
+            st = lib.dwa_peer_signal(self._flag_table, self.world, self.rank, self.step,
+                                     _stream_handle(self.device))
+        _lib.check(st, "dwa_peer_signal")
+
+    def merge(self, out_vals: torch.Tensor, out_idx: torch.Tensor) -> None:
+        """Global top-k of this step's lists of all ranks, read over NVLink."""
+        lib = _lib.load()
+        with torch.cuda.device(self.device):
+            st = lib.dwa_merge_topk_peers(self._list_tables[self.step & 1], self.world, self.M,
+                                          self.k, self._own, self.step, out_vals.data_ptr(),
+                                          out_idx.data_ptr(), self._own + self._STATUS_OFF,
+                                          _stream_handle(self.device))
+        _lib.check(st, "dwa_merge_topk_peers")
+
+    def status(self) -> int:
+        """Device status word of the peer merge (0 or DWA_ERR_TIMEOUT); syncs the device."""
+        torch.cuda.synchronize(self.device)
+        return int(self._hdr[self._STATUS_OFF // 4].item())
+
+    def close(self) -> None:
+        """Collective: unmap the peers' buffers and free this rank's."""
+        if self._own is None:
+            return
+        dist.barrier(group=self.group, device_ids=[self.device.index])
+        lib = _lib.load()
+        with torch.cuda.device(self.device):
+            for q in self._opened:
+                lib.dwa_peer_close(q)
+            lib.dwa_peer_free(self._own)
+        self._opened, self._own = [], None
 
 
 def exchange_candidates(local_vals: torch.Tensor, local_idx: torch.Tensor, group=None,
@@ -104,7 +216,7 @@ class Retriever:
 
     def __init__(self, keys_local: torch.Tensor, values_local: torch.Tensor, M: int, k: int, *,
                  lambda_sharp: float = 1.0, tau: float = 0.0, T: float = 1.0,
-                 use_sigmoid: bool = False, group=None):
+                 use_sigmoid: bool = False, group=None, exchange: str = "auto"):
         self.keys = _as_bf16_rows(keys_local, "keys_local")
         self.values = _check_values(values_local)
         if self.values.shape[0] != self.keys.shape[0]:
@@ -124,8 +236,6 @@ class Retriever:
         self.local_vals = torch.empty((self.M, self.k), dtype=f32, device=dev)
         self.local_idx = torch.empty((self.M, self.k), dtype=i32, device=dev)
         if self.world > 1:
-            self._packed_local = torch.empty((self.M, self.k, 2), dtype=i32, device=dev)
-            self._packed_all = torch.empty((self.world, self.M, self.k, 2), dtype=i32, device=dev)
             self.top_vals = torch.empty((self.M, self.k), dtype=f32, device=dev)
             self.top_idx = torch.empty((self.M, self.k), dtype=i32, device=dev)
         else:
@@ -137,13 +247,25 @@ class Retriever:
             raise _lib.DWAArgumentError(_lib.DWA_ERR_UNSUPPORTED_SHAPE, "Retriever",
                                         "no workspace plan for this shape")
         self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        # cross-shard exchange: "nvlink" (PeerExchange), "nccl" (all-gather +
+        # merge) or "auto" (nvlink for an NCCL group of more than one rank)
+        if exchange not in ("auto", "nvlink", "nccl"):
+            raise ValueError("exchange must be 'auto', 'nvlink' or 'nccl'")
+        use_peer = self.world > 1 and (exchange == "nvlink" or (
+            exchange == "auto" and dist.get_backend(self.group) == "nccl"))
+        self.peer = PeerExchange(self.M, self.k, self.group, dev) if use_peer else None
+        if self.world > 1 and self.peer is None:
+            self._packed_local = torch.empty((self.M, self.k, 2), dtype=i32, device=dev)
+            self._packed_all = torch.empty((self.world, self.M, self.k, 2), dtype=i32, device=dev)
 
     @property
     def kernels_per_call(self) -> int:
         """Kernels of this library one full call launches (NCCL and torch copy kernels
         not counted): bound reset, fused score + top-k, split merge,
-        [cross-shard merge,] weighted gather."""
-        return 4 if self.world == 1 else 5
+        [peer signal,] [cross-shard merge,] weighted gather."""
+        if self.world == 1:
+            return 4
+        return 6 if self.peer is not None else 5
 
     def topk_local(self, queries: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         """This rank's shard only: fused score + top-k and the split merge
@@ -163,6 +285,9 @@ class Retriever:
         """
         if self.world == 1:
             return
+        if self.peer is not None:
+            self.peer.publish(self.local_vals, self.local_idx)
+            return
         self._packed_local[..., 0].copy_(self.local_vals.view(torch.int32))
         self._packed_local[..., 1].copy_(self.local_idx)
         if dist.get_backend(self.group) == "nccl":
@@ -173,6 +298,9 @@ class Retriever:
     def merge(self) -> None:
         """Global top-k of the gathered [P, M, k] lists (retrieval.py:299-302), on the device."""
         if self.world == 1:
+            return
+        if self.peer is not None:
+            self.peer.merge(self.top_vals, self.top_idx)
             return
         lib = _lib.load()
         with torch.cuda.device(self.device):
@@ -223,7 +351,8 @@ class Retriever:
             st = lib.dwa_workspace_status(self.workspace.data_ptr(), _stream_handle(self.device),
                                           ctypes.byref(v))
         _lib.check(st, "dwa_workspace_status")
-        return int(v.value)
+        peer = self.peer.status() if self.peer is not None else 0
+        return int(v.value) or peer
 
 
 class HostPipeline:

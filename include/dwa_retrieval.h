@@ -221,6 +221,46 @@ DWA_API dwa_status dwa_pool_init_normal(void* out, int64_t rows, int64_t cols, i
                                 dwa_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Cross-shard exchange over NVLink peer memory: the all-gather + merge of
+ * _chip_topk (src/model/retrieval.py:295-302) as one kernel that reads the
+ * other GPUs' candidate lists directly, instead of a collective followed by
+ * a merge.  Each rank of a group owns one exchange buffer made by
+ * dwa_peer_alloc (set-up time, not per call) and opens the others' with
+ * dwa_peer_open; handles travel between processes as DWA_IPC_HANDLE_BYTES
+ * opaque bytes (CUDA IPC).
+ * ------------------------------------------------------------------------ */
+#define DWA_IPC_HANDLE_BYTES 64
+#define DWA_MAX_PEERS 16
+
+/* cudaMalloc(bytes), zero-filled, and its IPC handle (out_handle: 64 bytes). */
+DWA_API dwa_status dwa_peer_alloc(size_t bytes, void** out_ptr, void* out_handle);
+/* Maps another process's dwa_peer_alloc buffer (peer access enabled). */
+DWA_API dwa_status dwa_peer_open(const void* handle, void** out_ptr);
+DWA_API dwa_status dwa_peer_close(void* ptr);  /* unmaps a dwa_peer_open mapping */
+DWA_API dwa_status dwa_peer_free(void* ptr);   /* frees a dwa_peer_alloc buffer */
+
+/*
+ * After this stream's earlier work: makes it visible system-wide, then writes
+ * `value` to flag word my_rank of every rank's flag array (flag_bases[p] =
+ * rank p's flag array as mapped on this GPU; P ranks, P <= DWA_MAX_PEERS).
+ */
+DWA_API dwa_status dwa_peer_signal(void* const* flag_bases, int32_t P, int32_t my_rank,
+                           int32_t value, dwa_stream_t stream);
+
+/*
+ * Global top-k of P ranks' candidate lists read over NVLink: packed[p] is
+ * rank p's int32 [M, k, 2] list (fused score bits, global index), sorted
+ * best first, as mapped on this GPU.  Each warp first waits until
+ * flags[p] >= step for every p (this GPU's flag array, written by the
+ * ranks' dwa_peer_signal); a wait longer than 2 s records DWA_ERR_TIMEOUT in
+ * *status, writes -inf / -1 for that row and returns.  out_vals f32 /
+ * out_idx i32 [M, k] (ties: lower global index first, as lax.top_k).
+ */
+DWA_API dwa_status dwa_merge_topk_peers(const void* const* packed, int32_t P, int64_t M, int32_t k,
+                                const int32_t* flags, int32_t step, float* out_vals,
+                                int32_t* out_idx, int32_t* status, dwa_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Low-rank weight assembly: the consumer of the retrieved rows in a DWA
  * block, WeightAssembler.__call__ with per-position idx
  * (src/model/assembly.py:75-128).  Pool row layout (assembly.py:10-14):

@@ -99,6 +99,27 @@ def _worker(rank, world, port, q):
                     msg = "backward: dK rows differ"
                 elif not close(vg.grad, full_v.grad[:spec.n_local]):
                     msg = "backward: dV rows differ"
+        # NVLink peer exchange vs the NCCL all-gather path: identical results over
+        # three steps (both parity buffers, step flags reused).  Every rank runs the
+        # same collective sequence whatever its own checks found.
+        rp = cb.Retriever(keys, values, M, k, lambda_sharp=3.0, tau=0.5, T=0.8,
+                          use_sigmoid=True, exchange="nvlink")
+        rn = cb.Retriever(keys, values, M, k, lambda_sharp=3.0, tau=0.5, T=0.8,
+                          use_sigmoid=True, exchange="nccl")
+        same = rp.peer is not None and rn.peer is None
+        for step in range(3):
+            qs = cb.new_normal(M, d, seed=50 + step, device=dev)
+            op, ap, vp, ip = (t.clone() for t in rp(qs))
+            on, an, vn, in_ = rn(qs)
+            torch.cuda.synchronize()
+            same = same and torch.equal(ip, in_) and torch.equal(vp, vn) and torch.equal(op, on)
+        st_p = rp.status()
+        rp.peer.close()
+        if msg == "ok" and not same:
+            msg = "nvlink exchange differs from the NCCL path"
+        if msg == "ok" and st_p != 0:
+            msg = f"nvlink exchange status {st_p}"
+
         q.put((rank, same_chip, msg, r.status()))
         dist.barrier(device_ids=[rank])
     finally:
