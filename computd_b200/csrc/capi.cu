@@ -391,13 +391,13 @@ dwa_status dwa_merge_topk_peers(const void* const* packed, int32_t P, int64_t M,
   if (!packed || !flags || !out_vals || !out_idx || !status)
     return fail(DWA_ERR_INVALID_ARG, "dwa_merge_topk_peers: null argument");
   if (P < 1 || P > DWA_MAX_PEERS) return fail(DWA_ERR_INVALID_ARG, "dwa_merge_topk_peers: P=%d", P);
-  if (k < 1 || k > DWA_MERGE_MAX_K)
-    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_merge_topk_peers: k=%d outside [1, %d]", k,
+  if (k < 2 || k > DWA_MERGE_MAX_K || k % 2 != 0)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_merge_topk_peers: k=%d must be even in [2, %d]", k,
                 DWA_MERGE_MAX_K);
   if (M > (int64_t)INT32_MAX * 8) return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_merge_topk_peers: M too large");
   const int32_t* lists[DWA_MAX_PEERS];
   for (int p = 0; p < P; ++p) {
-    if (!packed[p] || !aligned(packed[p], 8))
+    if (!packed[p] || !aligned(packed[p], 16))
       return fail(DWA_ERR_INVALID_ARG, "dwa_merge_topk_peers: bad list pointer of rank %d", p);
     lists[p] = static_cast<const int32_t*>(packed[p]);
   }

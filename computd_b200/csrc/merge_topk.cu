@@ -130,6 +130,22 @@ __global__ void __launch_bounds__(kWarps * 32) merge_sorted_kernel(const MergeAr
       return;
     }
   }
+  // Peer mode: pull this row's P lists (k (score, index) pairs each, 8k bytes
+  // contiguous per list) into this warp's shared memory with 16-byte loads
+  // all in flight together, so NVLink latency is paid once per row instead of
+  // once per cached block of every list.
+  extern __shared__ uint4 peer_stage[];
+  const int32_t* stage = nullptr;
+  if constexpr (kPeer) {
+    const int words = a.k >> 1;  // 16-byte words per list row (k even)
+    uint4* dst = peer_stage + static_cast<size_t>(w) * a.n_lists * words;
+    for (int t = lane; t < a.n_lists * words; t += 32) {
+      const int l = t / words, c = t - l * words;
+      dst[t] = *reinterpret_cast<const uint4*>(a.peer[l] + row * a.stride_row + 4 * c);
+    }
+    __syncwarp();
+    stage = reinterpret_cast<const int32_t*>(dst);
+  }
 
   ListCursor cur[kSlots];
   const float* vbase[kSlots];
@@ -141,8 +157,8 @@ __global__ void __launch_bounds__(kWarps * 32) merge_sorted_kernel(const MergeAr
     cur[u].off = 0;
     if (l < a.n_lists) {
       if constexpr (kPeer) {
-        ibase[u] = a.peer[l] + row * a.stride_row + 1;
-        vbase[u] = reinterpret_cast<const float*>(a.peer[l] + row * a.stride_row);
+        ibase[u] = stage + static_cast<int64_t>(l) * 2 * a.k + 1;
+        vbase[u] = reinterpret_cast<const float*>(stage + static_cast<int64_t>(l) * 2 * a.k);
       } else {
         vbase[u] = a.cv + l * a.stride_list + row * a.stride_row;
         ibase[u] = a.ci + l * a.stride_list + row * a.stride_row;
@@ -327,8 +343,16 @@ cudaError_t launch_merge_topk_peers(const int32_t* const* packed, int n, int64_t
   a.transform = 0;
   a.out_v = out_vals;
   a.out_i = out_idx;
+  if (k % 2 != 0) return cudaErrorInvalidValue;  // 16-byte staging words
   const int64_t blocks = (M + kWarps - 1) / kWarps;
-  merge_sorted_kernel<true><<<static_cast<unsigned>(blocks), kWarps * 32, 0, stream>>>(a);
+  const size_t smem = static_cast<size_t>(kWarps) * n * k * 8;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(merge_sorted_kernel<true>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
+  merge_sorted_kernel<true><<<static_cast<unsigned>(blocks), kWarps * 32, smem, stream>>>(a);
   return cudaGetLastError();
 }
 

@@ -251,8 +251,10 @@ class Retriever:
         # merge) or "auto" (nvlink for an NCCL group of more than one rank)
         if exchange not in ("auto", "nvlink", "nccl"):
             raise ValueError("exchange must be 'auto', 'nvlink' or 'nccl'")
+        if exchange == "nvlink" and self.k % 2:
+            raise ValueError("exchange='nvlink' needs an even k (16-byte list staging)")
         use_peer = self.world > 1 and (exchange == "nvlink" or (
-            exchange == "auto" and dist.get_backend(self.group) == "nccl"))
+            exchange == "auto" and self.k % 2 == 0 and dist.get_backend(self.group) == "nccl"))
         self.peer = PeerExchange(self.M, self.k, self.group, dev) if use_peer else None
         if self.world > 1 and self.peer is None:
             self._packed_local = torch.empty((self.M, self.k, 2), dtype=i32, device=dev)

@@ -255,6 +255,8 @@ DWA_API dwa_status dwa_peer_signal(void* const* flag_bases, int32_t P, int32_t m
  * ranks' dwa_peer_signal); a wait longer than 2 s records DWA_ERR_TIMEOUT in
  * *status, writes -inf / -1 for that row and returns.  out_vals f32 /
  * out_idx i32 [M, k] (ties: lower global index first, as lax.top_k).
+ * k must be even and the lists 16-byte aligned (each row is staged in
+ * shared memory with 16-byte loads).
  */
 DWA_API dwa_status dwa_merge_topk_peers(const void* const* packed, int32_t P, int64_t M, int32_t k,
                                 const int32_t* flags, int32_t step, float* out_vals,
