@@ -21,9 +21,11 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 
 #include "dwa_internal.h"
+#include "sm100_ptx.cuh"
 
 namespace dwa {
 
@@ -166,6 +168,233 @@ __global__ void __launch_bounds__(kAsmThreads) lowrank_delta_kernel(const LowRan
   }
 }
 
+// ---------------------------------------------------------------------------
+// Staged variant: two persistent CTAs per SM; a producer warp bulk-copies each
+// selected row's V block, then its U and b blocks, into a ring of shared-memory
+// stages with cp.async.bulk (completion counted on mbarriers), so many
+// kilobytes per SM are in flight from HBM at once; eight consumer warps
+// compute from shared memory.  All waits are bounded; a wait that runs out
+// raises a CTA abort flag and every role leaves its loop.
+constexpr int kStgConsumers = 256;
+constexpr int kStgWarps = kStgConsumers / 32;
+constexpr int kStgThreads = kStgConsumers + 32;
+constexpr int kStgMaxOut = 16;      // outputs per consumer thread: d_B <= 4096
+constexpr int kStgMaxStages = 4;
+constexpr int kStgCtasPerSm = 2;  // a second CTA overlaps each CTA's per-row barrier bubbles
+
+struct StagedArgs {
+  LowRankArgs a;
+  int stages;
+  uint32_t stage_bytes, v_bytes, u_bytes, b_bytes, h_bytes, h_slot_bytes;
+  uint32_t meta_off, bar_off;  // byte offsets in shared memory
+};
+
+template <bool kHBf16>
+__global__ void __launch_bounds__(kStgThreads, kStgCtasPerSm) lowrank_delta_staged_kernel(const StagedArgs sa) {
+  const LowRankArgs& a = sa.a;
+  extern __shared__ __align__(128) uint8_t sm[];
+  const int S = sa.stages;
+  const int k = a.k, r = a.r;
+  uint8_t* hslot0 = sm + static_cast<size_t>(S) * sa.stage_bytes;
+  int32_t* meta_j = reinterpret_cast<int32_t*>(sm + sa.meta_off);  // [2][k]
+  float* meta_a = reinterpret_cast<float*>(meta_j + 2 * k);          // [2][k]
+  int* meta_n = reinterpret_cast<int*>(meta_a + 2 * k);              // [2]
+  float* hv = reinterpret_cast<float*>(meta_n + 4);                  // [2][r]
+  const uint32_t bar0 = smem_u32(sm + sa.bar_off);
+  auto full = [&](int st) { return bar0 + 8u * st; };
+  auto empty = [&](int st) { return bar0 + 8u * (S + st); };
+  auto hfull = [&](int sl) { return bar0 + 8u * (2 * S + sl); };
+  auto hempty = [&](int sl) { return bar0 + 8u * (2 * S + 2 + sl); };
+  auto hvbar = [&](int sl) { return bar0 + 8u * (2 * S + 4 + sl); };
+  int* ctl = reinterpret_cast<int*>(sm + sa.bar_off + 8 * (2 * S + 6));
+  volatile int* abort_flag = ctl;
+  int* n_issued = ctl + 1;
+  int* n_consumed = ctl + 2;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < S; ++st) {
+      mbar_init(full(st), 1);
+      mbar_init(empty(st), kStgWarps);
+    }
+    for (int sl = 0; sl < 2; ++sl) {
+      mbar_init(hfull(sl), 1);
+      mbar_init(hempty(sl), kStgWarps);
+      mbar_init(hvbar(sl), kStgWarps);
+    }
+    *abort_flag = 0;
+    *n_issued = 0;
+    *n_consumed = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  const int64_t off_b = static_cast<int64_t>(a.d_B) * r + static_cast<int64_t>(r) * a.d_A;
+  const int h_elem = kHBf16 ? 2 : 4;
+  if (warp == kStgWarps) {
+    // ------------------------------------------------------------ producer
+    int it = 0, tk = 0;
+    bool ok = true;
+    for (int64_t m = blockIdx.x; m < a.M && ok; m += gridDim.x, ++tk) {
+      const int slot = tk & 1;
+      const uint32_t use = static_cast<uint32_t>(tk >> 1);
+      bool got = true;
+      if (lane == 0) got = mbar_wait(hempty(slot), (use & 1u) ^ 1u, nullptr, abort_flag);
+      if (!__shfl_sync(0xffffffffu, got, 0)) break;
+      int cnt = 0;  // owned entries of token m, in entry order
+      for (int base = 0; base < k; base += 32) {
+        const int e = base + lane;
+        int32_t g = 0;
+        float al = 0.f;
+        bool own = false;
+        if (e < k) {
+          g = a.gidx[m * k + e];
+          al = a.alpha[m * k + e];
+          own = g >= a.row_begin && g < a.row_end;
+        }
+        const uint32_t bal = __ballot_sync(0xffffffffu, own);
+        if (own) {
+          const int pos = cnt + __popc(bal & ((1u << lane) - 1u));
+          meta_j[slot * k + pos] = static_cast<int32_t>(g - a.row_begin);
+          meta_a[slot * k + pos] = al;
+        }
+        cnt += __popc(bal);
+      }
+      if (lane == 0) meta_n[slot] = cnt;
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive_expect_tx(hfull(slot), sa.h_bytes);
+        bulk_load(smem_u32(hslot0 + slot * sa.h_slot_bytes),
+                  static_cast<const uint8_t*>(a.h) + m * a.ldh * h_elem, sa.h_bytes, hfull(slot));
+        for (int jj = 0; jj < cnt && ok; ++jj) {
+          const __nv_bfloat16* row = a.vectors + static_cast<int64_t>(meta_j[slot * k + jj]) * a.ldv;
+          for (int piece = 0; piece < 2; ++piece, ++it) {
+            const int st = it % S;
+            const uint32_t rr = static_cast<uint32_t>(it / S);
+            if (!mbar_wait(empty(st), (rr & 1u) ^ 1u, nullptr, abort_flag)) {
+              ok = false;
+              break;
+            }
+            const uint32_t dst = smem_u32(sm + static_cast<size_t>(st) * sa.stage_bytes);
+            if (piece == 0) {
+              mbar_arrive_expect_tx(full(st), sa.v_bytes);
+              bulk_load(dst, row + static_cast<int64_t>(a.d_B) * r, sa.v_bytes, full(st));
+            } else {
+              mbar_arrive_expect_tx(full(st), sa.u_bytes + sa.b_bytes);
+              bulk_load(dst, row, sa.u_bytes, full(st));
+              bulk_load(dst + sa.u_bytes, row + off_b, sa.b_bytes, full(st));
+            }
+          }
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+    }
+    if (lane == 0) *n_issued = it;
+  } else {
+    // ------------------------------------------------------------ consumers
+    const int tid = threadIdx.x;
+    int it = 0, tk = 0, jg = 0;
+    bool ok = true;
+    for (int64_t m = blockIdx.x; m < a.M; m += gridDim.x, ++tk) {
+      const int slot = tk & 1;
+      const uint32_t use = static_cast<uint32_t>(tk >> 1);
+      ok = mbar_wait(hfull(slot), use & 1u, nullptr, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) {
+        ok = false;
+        break;
+      }
+      const int n = meta_n[slot];
+      const float* oa = meta_a + slot * k;
+      const uint8_t* hs = hslot0 + slot * sa.h_slot_bytes;
+      float acc[kStgMaxOut];
+#pragma unroll
+      for (int u = 0; u < kStgMaxOut; ++u) acc[u] = 0.f;
+      for (int jj = 0; jj < n && ok; ++jj, ++jg) {
+        // V_j . h: one warp per rank row
+        int st = it % S;
+        ok = mbar_wait(full(st), static_cast<uint32_t>(it / S) & 1u, nullptr, abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+        const uint4* V = reinterpret_cast<const uint4*>(sm + static_cast<size_t>(st) * sa.stage_bytes);
+        const int words = a.d_A >> 3;
+        float* hvj = hv + (jg & 1) * r;
+        for (int ri = warp; ri < r; ri += kStgWarps) {
+          float sacc = 0.f;
+          for (int c = lane; c < words; c += 32) {
+            const uint4 w = V[ri * words + c];
+            if constexpr (kHBf16) {
+              const uint4 hw = reinterpret_cast<const uint4*>(hs)[c];
+              sacc = fmaf(bf16_lo(w.x), bf16_lo(hw.x), sacc);
+              sacc = fmaf(bf16_hi(w.x), bf16_hi(hw.x), sacc);
+              sacc = fmaf(bf16_lo(w.y), bf16_lo(hw.y), sacc);
+              sacc = fmaf(bf16_hi(w.y), bf16_hi(hw.y), sacc);
+              sacc = fmaf(bf16_lo(w.z), bf16_lo(hw.z), sacc);
+              sacc = fmaf(bf16_hi(w.z), bf16_hi(hw.z), sacc);
+              sacc = fmaf(bf16_lo(w.w), bf16_lo(hw.w), sacc);
+              sacc = fmaf(bf16_hi(w.w), bf16_hi(hw.w), sacc);
+            } else {
+              sacc += dot8(w, reinterpret_cast<const float*>(hs) + 8 * c);
+            }
+          }
+#pragma unroll
+          for (int o = 16; o; o >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, o);
+          if (lane == 0) hvj[ri] = oa[jj] * sacc;
+        }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(empty(st));
+          mbar_arrive(hvbar(jg & 1));  // this warp's rows of alpha_j hV_j are written
+        }
+        ++it;
+        ok = mbar_wait(hvbar(jg & 1), static_cast<uint32_t>(jg >> 1) & 1u, nullptr, abort_flag);
+        // alpha_j (U_j hV_j + b_j) for this thread's outputs
+        st = it % S;
+        ok = ok && mbar_wait(full(st), static_cast<uint32_t>(it / S) & 1u, nullptr, abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* ub = sm + static_cast<size_t>(st) * sa.stage_bytes;
+        const uint4* U = reinterpret_cast<const uint4*>(ub);
+        const __nv_bfloat16* bv = reinterpret_cast<const __nv_bfloat16*>(ub + sa.u_bytes);
+        const float aj = oa[jj];
+        const int uw = r >> 3;  // 16-byte words per U row
+#pragma unroll
+        for (int u = 0; u < kStgMaxOut; ++u) {
+          const int i = tid + u * kStgConsumers;
+          if (i < a.d_B) {
+            float t = aj * __bfloat162float(bv[i]);
+            for (int c = 0; c < uw; ++c) t += dot8(U[i * uw + c], hvj + 8 * c);
+            acc[u] += t;
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty(st));
+        ++it;
+      }
+      if (!ok) break;
+#pragma unroll
+      for (int u = 0; u < kStgMaxOut; ++u) {
+        const int i = tid + u * kStgConsumers;
+        if (i < a.d_B) a.delta[m * a.d_B + i] = acc[u];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(hempty(slot));
+    }
+    if (!ok) *abort_flag = 1;
+    if (tid == 0) *n_consumed = it;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // copies issued but never consumed (only after an abort) must land before exit
+    for (int i = *n_consumed; i < *n_issued; ++i)
+      mbar_wait(full(i % S), static_cast<uint32_t>(i / S) & 1u, nullptr, nullptr);
+  }
+  __syncthreads();
+}
+
 struct FinishArgs {
   const void* residual;
   int res_bf16;
@@ -244,6 +473,48 @@ cudaError_t launch_lowrank_delta(const void* h, int h_bf16, int64_t ldh, const f
                                  int r, float* delta, cudaStream_t stream) {
   LowRankArgs a{h, h_bf16, ldh, alpha, gidx, M, k, static_cast<const __nv_bfloat16*>(vectors),
                 row_begin, row_end, ldv, d_A, d_B, r, delta};
+  // Staged path: U rows of whole 16-byte words, outputs fit the consumers'
+  // registers, h rows 16-byte aligned, and at least two stages fit.
+  if (r % 8 == 0 && d_B <= kStgMaxOut * kStgConsumers && row_end > row_begin &&
+      (ldh * (h_bf16 ? 2 : 4)) % 16 == 0 && (reinterpret_cast<uintptr_t>(h) % 16) == 0) {
+    StagedArgs sa{};
+    sa.a = a;
+    sa.v_bytes = static_cast<uint32_t>(r) * d_A * 2;
+    sa.u_bytes = static_cast<uint32_t>(d_B) * r * 2;
+    sa.b_bytes = static_cast<uint32_t>(d_B) * 2;
+    sa.h_bytes = static_cast<uint32_t>(d_A) * (h_bf16 ? 2 : 4);
+    auto up128 = [](uint32_t x) { return (x + 127u) & ~127u; };
+    sa.stage_bytes = up128(std::max(sa.v_bytes, sa.u_bytes + sa.b_bytes));
+    sa.h_slot_bytes = up128(sa.h_bytes);
+    const uint32_t meta_bytes = up128(static_cast<uint32_t>(4 * k * 4 + 16 + 2 * r * 4));
+    const uint32_t bar_bytes = 8u * (2 * kStgMaxStages + 6) + 16u;
+    // per CTA: half of an SM's shared memory; 128 more for the barrier area's alignment
+    const uint32_t budget = 110u * 1024u - 2u * sa.h_slot_bytes - meta_bytes - bar_bytes - 128u;
+    const int stages = static_cast<int>(std::min<uint32_t>(kStgMaxStages, budget / sa.stage_bytes));
+    if (stages >= 2) {
+      sa.stages = stages;
+      sa.meta_off = static_cast<uint32_t>(stages) * sa.stage_bytes + 2u * sa.h_slot_bytes;
+      sa.bar_off = up128(sa.meta_off + meta_bytes);
+      const size_t smem = sa.bar_off + bar_bytes;
+      int dev = 0, sms = 148;
+      if (cudaGetDevice(&dev) == cudaSuccess)
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      const unsigned grid = static_cast<unsigned>(std::min<int64_t>(M, kStgCtasPerSm * sms));
+      cudaError_t e;
+      if (h_bf16) {
+        e = cudaFuncSetAttribute(lowrank_delta_staged_kernel<true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        lowrank_delta_staged_kernel<true><<<grid, kStgThreads, smem, stream>>>(sa);
+      } else {
+        e = cudaFuncSetAttribute(lowrank_delta_staged_kernel<false>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        lowrank_delta_staged_kernel<false><<<grid, kStgThreads, smem, stream>>>(sa);
+      }
+      return cudaGetLastError();
+    }
+  }
   const size_t smem = lowrank_delta_smem_bytes(d_A, k, r);
   const bool vec_u = (r % 8) == 0;
   cudaError_t e;
