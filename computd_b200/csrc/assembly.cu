@@ -199,14 +199,14 @@ __global__ void __launch_bounds__(kStgThreads, kStgCtasPerSm) lowrank_delta_stag
   int32_t* meta_j = reinterpret_cast<int32_t*>(sm + sa.meta_off);  // [2][k]
   float* meta_a = reinterpret_cast<float*>(meta_j + 2 * k);          // [2][k]
   int* meta_n = reinterpret_cast<int*>(meta_a + 2 * k);              // [2]
-  float* hv = reinterpret_cast<float*>(meta_n + 4);                  // [2][r]
+  float* hv = reinterpret_cast<float*>(meta_n + 4);                  // [4][r]
   const uint32_t bar0 = smem_u32(sm + sa.bar_off);
   auto full = [&](int st) { return bar0 + 8u * st; };
   auto empty = [&](int st) { return bar0 + 8u * (S + st); };
   auto hfull = [&](int sl) { return bar0 + 8u * (2 * S + sl); };
   auto hempty = [&](int sl) { return bar0 + 8u * (2 * S + 2 + sl); };
-  auto hvbar = [&](int sl) { return bar0 + 8u * (2 * S + 4 + sl); };
-  int* ctl = reinterpret_cast<int*>(sm + sa.bar_off + 8 * (2 * S + 6));
+  auto hvbar = [&](int sl) { return bar0 + 8u * (2 * S + 4 + sl); };  // 4 of them
+  int* ctl = reinterpret_cast<int*>(sm + sa.bar_off + 8 * (2 * S + 8));
   volatile int* abort_flag = ctl;
   int* n_issued = ctl + 1;
   int* n_consumed = ctl + 2;
@@ -220,8 +220,8 @@ __global__ void __launch_bounds__(kStgThreads, kStgCtasPerSm) lowrank_delta_stag
     for (int sl = 0; sl < 2; ++sl) {
       mbar_init(hfull(sl), 1);
       mbar_init(hempty(sl), kStgWarps);
-      mbar_init(hvbar(sl), kStgWarps);
     }
+    for (int sl = 0; sl < 4; ++sl) mbar_init(hvbar(sl), kStgWarps);
     *abort_flag = 0;
     *n_issued = 0;
     *n_consumed = 0;
@@ -292,9 +292,53 @@ __global__ void __launch_bounds__(kStgThreads, kStgCtasPerSm) lowrank_delta_stag
     if (lane == 0) *n_issued = it;
   } else {
     // ------------------------------------------------------------ consumers
+    // Per token: pieces it0 + 2j (V_j) and it0 + 2j + 1 (U_j | b_j).  A warp
+    // computes its rows of alpha_j V_j h for row j + 1 before it waits for the
+    // other warps' rows of row j and accumulates row j, so no warp idles at
+    // the per-row barrier.  alpha_j hV_j lives in buffer g % 4 (g counts rows
+    // over all tokens): a warp writing buffer g + 2 has passed barrier g,
+    // which every warp reached only after finishing row g - 2.
     const int tid = threadIdx.x;
-    int it = 0, tk = 0, jg = 0;
+    const int words = a.d_A >> 3;
+    const int uw = r >> 3;  // 16-byte words per U row
+    int it0 = 0, tk = 0, g0 = 0;
     bool ok = true;
+    auto v_phase = [&](int j, int g, const float* oa, const uint8_t* hs) -> bool {
+      const int piece = it0 + 2 * j;
+      const int st = piece % S;
+      bool got = mbar_wait(full(st), static_cast<uint32_t>(piece / S) & 1u, nullptr, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) return false;
+      const uint4* V = reinterpret_cast<const uint4*>(sm + static_cast<size_t>(st) * sa.stage_bytes);
+      float* hvj = hv + (g & 3) * r;
+      for (int ri = warp; ri < r; ri += kStgWarps) {
+        float sacc = 0.f;
+        for (int c = lane; c < words; c += 32) {
+          const uint4 w = V[ri * words + c];
+          if constexpr (kHBf16) {
+            const uint4 hw = reinterpret_cast<const uint4*>(hs)[c];
+            sacc = fmaf(bf16_lo(w.x), bf16_lo(hw.x), sacc);
+            sacc = fmaf(bf16_hi(w.x), bf16_hi(hw.x), sacc);
+            sacc = fmaf(bf16_lo(w.y), bf16_lo(hw.y), sacc);
+            sacc = fmaf(bf16_hi(w.y), bf16_hi(hw.y), sacc);
+            sacc = fmaf(bf16_lo(w.z), bf16_lo(hw.z), sacc);
+            sacc = fmaf(bf16_hi(w.z), bf16_hi(hw.z), sacc);
+            sacc = fmaf(bf16_lo(w.w), bf16_lo(hw.w), sacc);
+            sacc = fmaf(bf16_hi(w.w), bf16_hi(hw.w), sacc);
+          } else {
+            sacc += dot8(w, reinterpret_cast<const float*>(hs) + 8 * c);
+          }
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, o);
+        if (lane == 0) hvj[ri] = oa[j] * sacc;
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(empty(st));
+        mbar_arrive(hvbar(g & 3));  // this warp's rows of alpha_j hV_j are written
+      }
+      return true;
+    };
     for (int64_t m = blockIdx.x; m < a.M; m += gridDim.x, ++tk) {
       const int slot = tk & 1;
       const uint32_t use = static_cast<uint32_t>(tk >> 1);
@@ -309,58 +353,24 @@ __global__ void __launch_bounds__(kStgThreads, kStgCtasPerSm) lowrank_delta_stag
       float acc[kStgMaxOut];
 #pragma unroll
       for (int u = 0; u < kStgMaxOut; ++u) acc[u] = 0.f;
-      for (int jj = 0; jj < n && ok; ++jj, ++jg) {
-        // V_j . h: one warp per rank row
-        int st = it % S;
-        ok = mbar_wait(full(st), static_cast<uint32_t>(it / S) & 1u, nullptr, abort_flag);
-        if (!__all_sync(0xffffffffu, ok)) {
-          ok = false;
-          break;
-        }
-        const uint4* V = reinterpret_cast<const uint4*>(sm + static_cast<size_t>(st) * sa.stage_bytes);
-        const int words = a.d_A >> 3;
-        float* hvj = hv + (jg & 1) * r;
-        for (int ri = warp; ri < r; ri += kStgWarps) {
-          float sacc = 0.f;
-          for (int c = lane; c < words; c += 32) {
-            const uint4 w = V[ri * words + c];
-            if constexpr (kHBf16) {
-              const uint4 hw = reinterpret_cast<const uint4*>(hs)[c];
-              sacc = fmaf(bf16_lo(w.x), bf16_lo(hw.x), sacc);
-              sacc = fmaf(bf16_hi(w.x), bf16_hi(hw.x), sacc);
-              sacc = fmaf(bf16_lo(w.y), bf16_lo(hw.y), sacc);
-              sacc = fmaf(bf16_hi(w.y), bf16_hi(hw.y), sacc);
-              sacc = fmaf(bf16_lo(w.z), bf16_lo(hw.z), sacc);
-              sacc = fmaf(bf16_hi(w.z), bf16_hi(hw.z), sacc);
-              sacc = fmaf(bf16_lo(w.w), bf16_lo(hw.w), sacc);
-              sacc = fmaf(bf16_hi(w.w), bf16_hi(hw.w), sacc);
-            } else {
-              sacc += dot8(w, reinterpret_cast<const float*>(hs) + 8 * c);
-            }
-          }
-#pragma unroll
-          for (int o = 16; o; o >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, o);
-          if (lane == 0) hvj[ri] = oa[jj] * sacc;
-        }
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(empty(st));
-          mbar_arrive(hvbar(jg & 1));  // this warp's rows of alpha_j hV_j are written
-        }
-        ++it;
-        ok = mbar_wait(hvbar(jg & 1), static_cast<uint32_t>(jg >> 1) & 1u, nullptr, abort_flag);
-        // alpha_j (U_j hV_j + b_j) for this thread's outputs
-        st = it % S;
-        ok = ok && mbar_wait(full(st), static_cast<uint32_t>(it / S) & 1u, nullptr, abort_flag);
-        if (!__all_sync(0xffffffffu, ok)) {
+      if (n > 0) ok = v_phase(0, g0, oa, hs);
+      for (int jj = 0; jj < n && ok; ++jj) {
+        const int g = g0 + jj;
+        if (jj + 1 < n) ok = v_phase(jj + 1, g + 1, oa, hs);
+        if (!ok) break;
+        bool got = mbar_wait(hvbar(g & 3), static_cast<uint32_t>(g >> 2) & 1u, nullptr, abort_flag);
+        const int piece = it0 + 2 * jj + 1;
+        const int st = piece % S;
+        got = got && mbar_wait(full(st), static_cast<uint32_t>(piece / S) & 1u, nullptr, abort_flag);
+        if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
         }
         const uint8_t* ub = sm + static_cast<size_t>(st) * sa.stage_bytes;
         const uint4* U = reinterpret_cast<const uint4*>(ub);
         const __nv_bfloat16* bv = reinterpret_cast<const __nv_bfloat16*>(ub + sa.u_bytes);
+        const float* hvj = hv + (g & 3) * r;
         const float aj = oa[jj];
-        const int uw = r >> 3;  // 16-byte words per U row
 #pragma unroll
         for (int u = 0; u < kStgMaxOut; ++u) {
           const int i = tid + u * kStgConsumers;
@@ -372,9 +382,10 @@ __global__ void __launch_bounds__(kStgThreads, kStgCtasPerSm) lowrank_delta_stag
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty(st));
-        ++it;
       }
       if (!ok) break;
+      it0 += 2 * n;
+      g0 += n;
 #pragma unroll
       for (int u = 0; u < kStgMaxOut; ++u) {
         const int i = tid + u * kStgConsumers;
@@ -384,7 +395,7 @@ __global__ void __launch_bounds__(kStgThreads, kStgCtasPerSm) lowrank_delta_stag
       if (lane == 0) mbar_arrive(hempty(slot));
     }
     if (!ok) *abort_flag = 1;
-    if (tid == 0) *n_consumed = it;
+    if (tid == 0) *n_consumed = it0;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -486,8 +497,8 @@ cudaError_t launch_lowrank_delta(const void* h, int h_bf16, int64_t ldh, const f
     auto up128 = [](uint32_t x) { return (x + 127u) & ~127u; };
     sa.stage_bytes = up128(std::max(sa.v_bytes, sa.u_bytes + sa.b_bytes));
     sa.h_slot_bytes = up128(sa.h_bytes);
-    const uint32_t meta_bytes = up128(static_cast<uint32_t>(4 * k * 4 + 16 + 2 * r * 4));
-    const uint32_t bar_bytes = 8u * (2 * kStgMaxStages + 6) + 16u;
+    const uint32_t meta_bytes = up128(static_cast<uint32_t>(4 * k * 4 + 16 + 4 * r * 4));
+    const uint32_t bar_bytes = 8u * (2 * kStgMaxStages + 8) + 16u;
     // per CTA: half of an SM's shared memory; 128 more for the barrier area's alignment
     const uint32_t budget = 110u * 1024u - 2u * sa.h_slot_bytes - meta_bytes - bar_bytes - 128u;
     const int stages = static_cast<int>(std::min<uint32_t>(kStgMaxStages, budget / sa.stage_bytes));

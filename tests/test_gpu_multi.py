@@ -115,6 +115,27 @@ def _worker(rank, world, port, q):
             same = same and torch.equal(ip, in_) and torch.equal(vp, vn) and torch.equal(op, on)
         st_p = rp.status()
         rp.peer.close()
+        # sharded WeightAssembler (owner-computes delta + all-reduce + LayerNorm)
+        # against the unsharded one on rank 0; every rank runs the same collectives
+        d_A = d_B = 64
+        r_lr = 8
+        D = d_B * r_lr + r_lr * d_A + d_B
+        vec_l = cb.new_normal(spec.n_local, D, seed=61, stddev=0.2, row_offset=spec.row_begin,
+                              device=dev)
+        h = cb.new_normal(M, d_A, seed=62, device=dev)
+        asm = cb.WeightAssembler(d_A, d_B, r_lr, device=dev)
+        asm.W_base = cb.new_normal(d_B, d_A, seed=63, stddev=d_A ** -0.5, device=dev)
+        asm.gamma = 0.8
+        hm = asm(h, alpha, ti, vec_l)
+        if rank == 0 and msg == "ok":
+            vec_full = cb.new_normal(N, D, seed=61, stddev=0.2, device=dev)
+            asm1 = cb.WeightAssembler(d_A, d_B, r_lr, device=dev)
+            asm1.W_base, asm1.gamma = asm.W_base, asm.gamma
+            h1 = asm1(h, alpha, ti, vec_full, group=g0)
+            torch.cuda.synchronize()
+            err = float((hm - h1).abs().max()) / max(float(h1.abs().max()), 1e-12)
+            if err > 1e-3:
+                msg = f"sharded WeightAssembler differs from the single-GPU one (rel {err:.2e})"
         if msg == "ok" and not same:
             msg = "nvlink exchange differs from the NCCL path"
         if msg == "ok" and st_p != 0:
