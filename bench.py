@@ -362,6 +362,7 @@ def run_ours(args, wl):
         torch.cuda.empty_cache()
     if not args.no_assembly:
         line["assembly"] = measure_assembly(world, rank, local_rank, group)
+        line["key_projection"] = measure_key_projection(world, rank, local_rank)
     if args.lm:
         names = [n for n in args.lm.split(",") if n and (n != "small_char" or world == 1)]
         line["lm"] = [measure_lm(n, world, rank, local_rank) for n in names]
@@ -439,6 +440,48 @@ def measure_assembly(world, rank, local_rank, group, warmup=3, steps=10):
                          "unit": "GB/s", "frac": bytes_delta / (ms_delta * 1e-3) / 1e9 / hbm,
                          "algorithmic_bytes_per_launch": bytes_delta},
             "data": "synthetic: uniform distinct indices per token, random weights"}
+
+
+def measure_key_projection(world, rank, local_rank, warmup=2, steps=5):
+    """Pool keys (projection + L2 normalisation + aspect collapse, retrieval.py:241-262)
+    on the reference's 7B layout: S = 16 aspects, d_k = 128, D = 69632, a pool of
+    32768 rows sharded over the ranks; one fused tcgen05 launch per step."""
+    import torch
+    import torch.distributed as dist
+
+    import computd_b200 as cb
+
+    S, d_k, D, N = 16, 128, 69632, 32768
+    dev = torch.device("cuda", local_rank)
+    spec = cb.ShardSpec(N, rank, world)
+    vectors = cb.new_normal(spec.n_local, D, seed=71, stddev=0.02, row_offset=spec.row_begin,
+                            device=dev)
+    wk = cb.new_normal(S * d_k, D, seed=72, stddev=D ** -0.5, device=dev).view(S, d_k, D)
+    w = torch.softmax(torch.linspace(-1.0, 1.0, S, device=dev), 0)
+    out = torch.empty((spec.n_local, d_k), dtype=torch.bfloat16, device=dev)
+    for _ in range(warmup):
+        cb.project_keys(vectors, wk, w, out=out)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        cb.project_keys(vectors, wk, w, out=out)
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t[0])
+    flops = 2.0 * spec.n_local * D * S * d_k
+    burst = _peaks()[0]
+    del vectors, wk, out
+    torch.cuda.empty_cache()
+    return {"config": "reference 7B key layout (S=16, d_k=128, D=69632, N=32768)",
+            "pool_rows_per_gpu": spec.n_local, "ms_per_launch": ms,
+            "rows_per_s": N / (ms * 1e-3), "unit": "pool rows/s",
+            "roofline": {"bound": "tensor", "kernel": "key_project_kernel",
+                         "achieved": flops / (ms * 1e-3) / 1e12, "peak": burst, "unit": "TFLOP/s",
+                         "frac": flops / (ms * 1e-3) / 1e12 / burst, "flops_per_launch": flops}}
 
 
 def measure_lm(cfg_name, world, rank, local_rank, warmup=3, steps=3):

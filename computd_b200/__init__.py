@@ -12,6 +12,7 @@ from .assembler import WeightAssembler, assemble_finish, lowrank_delta, usage_em
 from .assembly import normalise_alpha, weighted_gather_into, weighted_value_sum
 from .pool import ShardSpec, init_normal, new_normal
 from .retrieval import (HostPipeline, MultiAspectRetrieval, PeerExchange, Retriever, chip_topk,
+                        project_keys,
                         exchange_candidates, reduce_partials)
 from .tiled_topk import (merge_topk, score_topk_into, tiled_topk_fallback, tiled_topk_fused,
                          workspace_bytes)
@@ -21,6 +22,6 @@ __all__ = [
     "WeightAssembler", "assemble_finish", "lowrank_delta", "usage_ema_update",
     "normalise_alpha", "weighted_gather_into", "weighted_value_sum", "MultiAspectRetrieval",
     "ShardSpec", "init_normal", "new_normal",
-    "HostPipeline", "PeerExchange", "Retriever", "chip_topk", "exchange_candidates", "reduce_partials",
+    "HostPipeline", "PeerExchange", "Retriever", "chip_topk", "project_keys", "exchange_candidates", "reduce_partials",
     "merge_topk", "score_topk_into", "tiled_topk_fallback", "tiled_topk_fused", "workspace_bytes",
 ]

@@ -326,6 +326,32 @@ dwa_status dwa_pool_init_normal(void* out, int64_t rows, int64_t cols, int64_t l
   return ok();
 }
 
+dwa_status dwa_project_keys(const void* vectors, int64_t N, int64_t ldv, int32_t D, const void* w_k,
+                            int64_t ldw, int32_t S, int32_t d_k, const float* aspect_w,
+                            void* keys_out, int64_t ldo, int32_t* status, dwa_stream_t stream) {
+  if (N < 0) return fail(DWA_ERR_INVALID_ARG, "dwa_project_keys: negative N");
+  if (N == 0) return ok();
+  if (!vectors || !w_k || !aspect_w || !keys_out)
+    return fail(DWA_ERR_INVALID_ARG, "dwa_project_keys: null argument");
+  if (d_k != 32 && d_k != 64 && d_k != 128)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_project_keys: d_k=%d must be 32, 64 or 128", d_k);
+  if (S < 1 || static_cast<int64_t>(S) * d_k > (1 << 20))
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_project_keys: S=%d outside [1, 2^20 / d_k]", S);
+  if (D < 8 || D % 8 != 0)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_project_keys: D=%d must be a positive multiple of 8", D);
+  if (N > INT32_MAX - 256) return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_project_keys: N too large");
+  if (ldv < D || ldw < D || ldo < d_k)
+    return fail(DWA_ERR_INVALID_ARG, "dwa_project_keys: a row stride is below its row length");
+  if (ldv % 8 || ldw % 8 || ldo % 8 || !aligned(vectors, 16) || !aligned(w_k, 16) ||
+      !aligned(keys_out, 16))
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE,
+                "dwa_project_keys: 16-byte aligned bases and strides (multiples of 8) required");
+  cudaError_t e = dwa::launch_project_keys(vectors, N, ldv, D, w_k, ldw, S, d_k, aspect_w, keys_out,
+                                           ldo, status, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_project_keys launch");
+  return ok();
+}
+
 dwa_status dwa_peer_alloc(size_t bytes, void** out_ptr, void* out_handle) {
   if (!out_ptr || !out_handle || bytes == 0)
     return fail(DWA_ERR_INVALID_ARG, "dwa_peer_alloc: null output or zero size");

@@ -4,6 +4,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace dwa {
@@ -79,6 +80,15 @@ cudaError_t launch_scatter_add_rows(const float* wts, const int32_t* idx, int64_
                                     const void* a, int a_bf16, int64_t lda, int64_t row_begin,
                                     int64_t row_end, float* grad, int64_t ldg, int d,
                                     cudaStream_t stream);
+
+// score_topk.cu: 2-D bf16 tensor map, 128-byte swizzle, box (box_inner x box_rows)
+bool make_bf16_tile_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t rows,
+                        uint64_t ld_elems, uint32_t box_inner, uint32_t box_rows);
+
+// key_projection.cu
+cudaError_t launch_project_keys(const void* vectors, int64_t N, int64_t ldv, int D, const void* w_k,
+                                int64_t ldw, int S, int d_k, const float* aspect_w, void* keys_out,
+                                int64_t ldo, int* status, cudaStream_t stream);
 
 // merge_topk.cu: NVLink peer exchange
 int max_peers();

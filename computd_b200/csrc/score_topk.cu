@@ -553,6 +553,35 @@ __global__ void fill_i32_kernel(int32_t* p, int64_t n, int32_t v) {
 }
 
 // ---------------------------------------------------------------- host side
+template <int KCAP, int NWG>
+cudaError_t configure_once() {
+  static std::atomic<uint64_t> done_mask{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done_mask.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(score_topk_kernel<KCAP, NWG>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           TopkCfg<KCAP, NWG>::kSmemBytes);
+  if (e == cudaSuccess) done_mask.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
+
+template <int KCAP, int NWG>
+cudaError_t launch_variant(const ScoreTopkPlan& p, const CUtensorMap& mq, const CUtensorMap& mk,
+                           const TopkKernelArgs& args, cudaStream_t stream) {
+  cudaError_t e = configure_once<KCAP, NWG>();
+  if (e != cudaSuccess) return e;
+  const unsigned grid = 2u * static_cast<unsigned>(p.n_qt) * static_cast<unsigned>(p.n_split);
+  score_topk_kernel<KCAP, NWG><<<grid, threads_for(NWG), TopkCfg<KCAP, NWG>::kSmemBytes, stream>>>(
+      mq, mk, args);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+// Shared with key_projection.cu (declared in dwa_internal.h).
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static std::once_flag once;
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -581,34 +610,6 @@ bool make_bf16_tile_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint6
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
-
-template <int KCAP, int NWG>
-cudaError_t configure_once() {
-  static std::atomic<uint64_t> done_mask{0};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  const uint64_t bit = 1ull << (dev & 63);
-  if (done_mask.load(std::memory_order_acquire) & bit) return cudaSuccess;
-  e = cudaFuncSetAttribute(score_topk_kernel<KCAP, NWG>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           TopkCfg<KCAP, NWG>::kSmemBytes);
-  if (e == cudaSuccess) done_mask.fetch_or(bit, std::memory_order_acq_rel);
-  return e;
-}
-
-template <int KCAP, int NWG>
-cudaError_t launch_variant(const ScoreTopkPlan& p, const CUtensorMap& mq, const CUtensorMap& mk,
-                           const TopkKernelArgs& args, cudaStream_t stream) {
-  cudaError_t e = configure_once<KCAP, NWG>();
-  if (e != cudaSuccess) return e;
-  const unsigned grid = 2u * static_cast<unsigned>(p.n_qt) * static_cast<unsigned>(p.n_split);
-  score_topk_kernel<KCAP, NWG><<<grid, threads_for(NWG), TopkCfg<KCAP, NWG>::kSmemBytes, stream>>>(
-      mq, mk, args);
-  return cudaGetLastError();
-}
-
-}  // namespace
 
 cudaError_t launch_plan(const ScoreTopkPlan& p, const CUtensorMap& mq, const CUtensorMap& mk,
                         const TopkKernelArgs& args, cudaStream_t stream);

@@ -442,6 +442,33 @@ class HostPipeline:
         return max(r.status() for r in self.ret)
 
 
+def project_keys(vectors: torch.Tensor, W_K: torch.Tensor, w: torch.Tensor,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """keys_w [N, d_k] bf16 = sum_s w[s] k_s / (|k_s| + 1e-8), k_s = W_K[s] @ v, for the
+    pool rows ``vectors`` [N, D] (retrieval.py:241-242, 253, 261) in one tcgen05 GEMM
+    with the normalisation and aspect collapse in its epilogue (``dwa_project_keys``).
+
+    W_K [S, d_k, D] (converted to bf16), w [S] aspect weights (softmax of the
+    aspect logits).  d_k in {32, 64, 128}, D % 8 == 0.
+    """
+    v = _as_bf16_rows(vectors, "vectors")
+    S, d_k, D = W_K.shape
+    if v.shape[1] != D:
+        raise ValueError(f"vectors must be [N, {D}]")
+    wk = W_K.to(device=v.device, dtype=torch.bfloat16).reshape(S * d_k, D).contiguous()
+    wv = w.to(device=v.device, dtype=torch.float32).contiguous()
+    N = v.shape[0]
+    if out is None:
+        out = torch.empty((N, d_k), dtype=torch.bfloat16, device=v.device)
+    lib = _lib.load()
+    with torch.cuda.device(v.device):
+        st = lib.dwa_project_keys(v.data_ptr(), N, v.stride(0), D, wk.data_ptr(), wk.stride(0), S,
+                                  d_k, wv.data_ptr(), out.data_ptr(), out.stride(0), None,
+                                  _stream_handle(v.device))
+    _lib.check(st, "dwa_project_keys")
+    return out
+
+
 class MultiAspectRetrieval:
     """Parameters and ``pallas_hybrid_forward`` of the reference's retrieval
     module (src/model/retrieval.py:7-46, 204-343) on B200.
@@ -472,9 +499,17 @@ class MultiAspectRetrieval:
 
     def project_keys(self, vectors: torch.Tensor, w: torch.Tensor, chunk_rows: int = 1 << 18
                      ) -> torch.Tensor:
-        """keys_w = sum_s w_s normalize(W_K[s] v) for every pool row (retrieval.py:241-242,261),
-        chunked over rows so the (S, N, d_k) tensor is never materialised."""
-        N = vectors.shape[0]
+        """keys_w = sum_s w_s W_K[s] v / (|W_K[s] v| + 1e-8) for every pool row
+        (retrieval.py:241-242, 261).  With bf16 W_K (the default) one fused tcgen05
+        kernel (``dwa_project_keys``: bf16 operands, fp32 accumulation,
+        normalisation and collapse in its epilogue) when d_k is 32, 64 or 128 and
+        D % 8 == 0; with fp32 W_K, fp32 cuBLAS GEMMs chunked over rows, so the
+        projection keeps the parameters' precision.  The (S, N, d_k) tensor is
+        never materialised."""
+        N, D = vectors.shape
+        if (self.W_K.dtype == torch.bfloat16 and self.d_k in (32, 64, 128) and D % 8 == 0
+                and vectors.is_cuda):
+            return project_keys(vectors, self.W_K, w)
         out = torch.empty((N, self.d_k), dtype=torch.bfloat16, device=vectors.device)
         WK = self.W_K.float()
         for r0 in range(0, N, chunk_rows):

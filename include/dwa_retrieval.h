@@ -220,6 +220,23 @@ DWA_API dwa_status dwa_pool_init_normal(void* out, int64_t rows, int64_t cols, i
                                 int64_t row_offset, uint64_t seed, float stddev,
                                 dwa_stream_t stream);
 
+/*
+ * Pool keys of the retrieval: keys_w[n] = sum_s w[s] k_s / (|k_s| + 1e-8),
+ * k_s = W_K[s] vectors[n] (src/model/retrieval.py:241-242, 253, 261: the
+ * per-aspect projection, its L2 normalisation and the aspect collapse, one
+ * tcgen05 GEMM with the normalisation and collapse in its epilogue; the
+ * (S, N, d_k) projection is never materialised).
+ * vectors: bf16 [N, ldv] (D used); w_k: bf16 [S * d_k, ldw] (W_K[s, kk, :] at
+ * row s * d_k + kk); aspect_w: f32 [S] on the device (softmax of the aspect
+ * logits); keys_out: bf16 [N, ldo].  d_k in {32, 64, 128}, D % 8 == 0,
+ * 16-byte aligned bases, strides multiples of 8.  status (a device int32,
+ * may be NULL) receives DWA_ERR_TIMEOUT if a bounded wait runs out.
+ */
+DWA_API dwa_status dwa_project_keys(const void* vectors, int64_t N, int64_t ldv, int32_t D,
+                            const void* w_k, int64_t ldw, int32_t S, int32_t d_k,
+                            const float* aspect_w, void* keys_out, int64_t ldo,
+                            int32_t* status, dwa_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Cross-shard exchange over NVLink peer memory: the all-gather + merge of
  * _chip_topk (src/model/retrieval.py:295-302) as one kernel that reads the

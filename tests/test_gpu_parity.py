@@ -341,3 +341,26 @@ def test_host_pipeline_matches_retriever(lib):
         assert torch.equal(ih, iw)
         assert torch.equal(ah, aw)
         assert torch.equal(oh, ow)
+
+
+@pytest.mark.parametrize("N,D,S,d_k", [
+    (1000, 88, 2, 32),      # the reference-run fixture's shape (one padded projection tile)
+    (5000, 1024, 16, 64),   # four full projection tiles
+    (700, 520, 3, 128),     # d_k = 128, D tail of 8 columns, padded tile
+    (300, 4096, 8, 128),
+])
+def test_project_keys_vs_fp32(lib, N, D, S, d_k):
+    """dwa_project_keys (fused projection + L2 normalisation + aspect collapse)
+    against a plain fp32 PyTorch restatement on the same bf16 inputs."""
+    dev = _dev()
+    g = torch.Generator(device=dev)
+    g.manual_seed(N + D)
+    v = torch.randn((N, D), device=dev, generator=g).to(torch.bfloat16)
+    wk = (torch.randn((S, d_k, D), device=dev, generator=g) * D ** -0.5).to(torch.bfloat16)
+    w = torch.softmax(torch.randn(S, device=dev, generator=g), 0)
+    got = lib.project_keys(v, wk, w).float()
+    ks = torch.einsum("skd,nd->snk", wk.float(), v.float())
+    ks = ks / (ks.norm(dim=-1, keepdim=True) + 1e-8)
+    want = torch.einsum("s,snk->nk", w, ks)
+    err = float((got - want).abs().max())
+    assert err <= RTOL * float(want.abs().max()), f"max abs err {err}"
