@@ -54,6 +54,13 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                     _i64, _c_void_p, _i64, _i32, _c_void_p]),
     "dwa_pool_init_normal": (_i32, [_c_void_p, _i64, _i64, _i64, _i64, ctypes.c_uint64, _f32,
                                     _c_void_p]),
+    "dwa_weighted_gather_peers": (_i32, [_c_void_p, _c_void_p, _i64, _i32, _c_void_p, _i64, _i64,
+                                         _i64, _i32, ctypes.POINTER(_c_void_p), _i32, _i32, _i64,
+                                         _c_void_p, _c_void_p]),
+    "dwa_reduce_broadcast_peers": (_i32, [_c_void_p, _i32, _i32, _i64, _i64, _i32,
+                                          ctypes.POINTER(_c_void_p), _c_void_p, _i32, _c_void_p,
+                                          _c_void_p]),
+    "dwa_peer_wait": (_i32, [_c_void_p, _i32, _i32, _c_void_p, _c_void_p]),
     "dwa_project_keys": (_i32, [_c_void_p, _i64, _i64, _i32, _c_void_p, _i64, _i32, _i32, _c_void_p,
                                 _c_void_p, _i64, _c_void_p, _c_void_p]),
     "dwa_peer_alloc": (_i32, [ctypes.c_size_t, ctypes.POINTER(_c_void_p), _c_void_p]),

@@ -326,6 +326,71 @@ dwa_status dwa_pool_init_normal(void* out, int64_t rows, int64_t cols, int64_t l
   return ok();
 }
 
+dwa_status dwa_weighted_gather_peers(const float* vals, const int32_t* gidx, int64_t M, int32_t k,
+                                     const void* values, int64_t row_begin, int64_t row_end,
+                                     int64_t ldv, int32_t d, void* const* inboxes, int32_t P,
+                                     int32_t rank, int64_t block_rows, float* alpha_out,
+                                     dwa_stream_t stream) {
+  if (M < 0) return fail(DWA_ERR_INVALID_ARG, "dwa_weighted_gather_peers: negative M");
+  if (M == 0) return ok();
+  if (!vals || !gidx || !inboxes) return fail(DWA_ERR_INVALID_ARG, "dwa_weighted_gather_peers: null argument");
+  if (P < 1 || P > DWA_MAX_PEERS || rank < 0 || rank >= P)
+    return fail(DWA_ERR_INVALID_ARG, "dwa_weighted_gather_peers: P=%d rank=%d", P, rank);
+  if (block_rows < 1 || block_rows * P < M)
+    return fail(DWA_ERR_INVALID_ARG, "dwa_weighted_gather_peers: P * block_rows must cover M");
+  if (k < 1 || k > DWA_MAX_K)
+    return fail(k < 1 ? DWA_ERR_INVALID_ARG : DWA_ERR_UNSUPPORTED_SHAPE, "dwa_weighted_gather_peers: k=%d", k);
+  if (d < 8 || d % 8 != 0)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_weighted_gather_peers: d=%d must be a positive multiple of 8", d);
+  if (row_begin < 0 || row_end < row_begin || row_end > INT32_MAX)
+    return fail(DWA_ERR_INVALID_ARG, "dwa_weighted_gather_peers: bad owned row range");
+  if (row_end > row_begin && (!values || ldv < d || ldv % 8 != 0 || !aligned(values, 16)))
+    return fail(DWA_ERR_INVALID_ARG, "dwa_weighted_gather_peers: values need 16-byte aligned rows");
+  float* boxes[DWA_MAX_PEERS];
+  for (int p = 0; p < P; ++p) {
+    if (!inboxes[p] || !aligned(inboxes[p], 16))
+      return fail(DWA_ERR_INVALID_ARG, "dwa_weighted_gather_peers: bad inbox of rank %d", p);
+    boxes[p] = static_cast<float*>(inboxes[p]);
+  }
+  cudaError_t e = dwa::launch_weighted_gather_peers(vals, gidx, M, k, values, row_begin, row_end, ldv,
+                                                    d, boxes, P, rank, block_rows, alpha_out,
+                                                    static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_weighted_gather_peers launch");
+  return ok();
+}
+
+dwa_status dwa_reduce_broadcast_peers(const float* inbox, int32_t P, int32_t rank, int64_t block_rows,
+                                      int64_t M, int32_t d, void* const* outs, const int32_t* flags,
+                                      int32_t step, int32_t* status, dwa_stream_t stream) {
+  if (!inbox || !outs || !flags || !status)
+    return fail(DWA_ERR_INVALID_ARG, "dwa_reduce_broadcast_peers: null argument");
+  if (P < 1 || P > DWA_MAX_PEERS || rank < 0 || rank >= P)
+    return fail(DWA_ERR_INVALID_ARG, "dwa_reduce_broadcast_peers: P=%d rank=%d", P, rank);
+  if (M < 0 || block_rows < 1 || block_rows * P < M)
+    return fail(DWA_ERR_INVALID_ARG, "dwa_reduce_broadcast_peers: P * block_rows must cover M");
+  if (d < 8 || d % 8 != 0 || !aligned(inbox, 16))
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_reduce_broadcast_peers: d %% 8 and 16-byte inbox required");
+  float* o[DWA_MAX_PEERS];
+  for (int p = 0; p < P; ++p) {
+    if (!outs[p] || !aligned(outs[p], 16))
+      return fail(DWA_ERR_INVALID_ARG, "dwa_reduce_broadcast_peers: bad output of rank %d", p);
+    o[p] = static_cast<float*>(outs[p]);
+  }
+  cudaError_t e = dwa::launch_reduce_broadcast_peers(inbox, P, rank, block_rows, M, d, o, flags, step,
+                                                     status, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_reduce_broadcast_peers launch");
+  return ok();
+}
+
+dwa_status dwa_peer_wait(const int32_t* flags, int32_t P, int32_t step, int32_t* status,
+                         dwa_stream_t stream) {
+  if (!flags || !status) return fail(DWA_ERR_INVALID_ARG, "dwa_peer_wait: null argument");
+  if (P < 1 || P > DWA_MAX_PEERS) return fail(DWA_ERR_INVALID_ARG, "dwa_peer_wait: P=%d", P);
+  cudaError_t e = dwa::launch_peer_wait(flags, P, step, status, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_peer_wait launch");
+  return ok();
+}
+
 dwa_status dwa_project_keys(const void* vectors, int64_t N, int64_t ldv, int32_t D, const void* w_k,
                             int64_t ldw, int32_t S, int32_t d_k, const float* aspect_w,
                             void* keys_out, int64_t ldo, int32_t* status, dwa_stream_t stream) {

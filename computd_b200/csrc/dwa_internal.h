@@ -85,6 +85,16 @@ cudaError_t launch_scatter_add_rows(const float* wts, const int32_t* idx, int64_
 bool make_bf16_tile_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t rows,
                         uint64_t ld_elems, uint32_t box_inner, uint32_t box_rows);
 
+// weighted_gather.cu: NVLink owner-computes reduction
+cudaError_t launch_weighted_gather_peers(const float* vals, const int32_t* gidx, int64_t M, int k,
+                                         const void* values, int64_t row_begin, int64_t row_end,
+                                         int64_t ldv, int d, float* const* inboxes, int P, int rank,
+                                         int64_t block_rows, float* alpha_out, cudaStream_t stream);
+cudaError_t launch_reduce_broadcast_peers(const float* inbox, int P, int rank, int64_t block_rows,
+                                          int64_t M, int d, float* const* outs, const int32_t* flags,
+                                          int step, int* status, cudaStream_t stream);
+cudaError_t launch_peer_wait(const int32_t* flags, int P, int step, int* status, cudaStream_t stream);
+
 // key_projection.cu
 cudaError_t launch_project_keys(const void* vectors, int64_t N, int64_t ldv, int D, const void* w_k,
                                 int64_t ldw, int S, int d_k, const float* aspect_w, void* keys_out,

@@ -13,6 +13,7 @@
 #include <cstdint>
 
 #include "dwa_internal.h"
+#include "sm100_ptx.cuh"
 
 namespace dwa {
 
@@ -20,6 +21,7 @@ namespace {
 
 constexpr int kWarps = 8;
 constexpr int kMaxGatherK = 128;
+constexpr int kMaxPeerRanks = 16;
 
 struct GatherArgs {
   const float* vals;
@@ -29,6 +31,11 @@ struct GatherArgs {
   int k, d;
   float* out;
   float* alpha_out;
+  // NVLink mode (n_peers > 0): row m's partial sum goes to the inbox of the
+  // rank owning row block m / block_rows, in this rank's slot
+  float* inbox[kMaxPeerRanks];
+  int n_peers, rank;
+  int64_t block_rows;
 };
 
 __device__ __forceinline__ void bf16x8_to_f32(const uint4 x, float (&f)[8]) {
@@ -81,9 +88,13 @@ __global__ void __launch_bounds__(kWarps * 32) weighted_gather_kernel(const Gath
     n_own += __popc(mask);
   }
   __syncwarp();
-  if (a.out == nullptr) return;  // alpha only
+  if (a.out == nullptr && a.n_peers == 0) return;  // alpha only
 
   float* orow = a.out + m * a.d;
+  if (a.n_peers > 0) {
+    const int64_t o = m / a.block_rows;
+    orow = a.inbox[o] + (static_cast<int64_t>(a.rank) * a.block_rows + (m - o * a.block_rows)) * a.d;
+  }
   for (int c0 = 0; c0 < a.d; c0 += 256) {
     const int col = c0 + lane * 8;
     if (col >= a.d) continue;  // d % 8 == 0: a lane's 8 columns are all in range or all out
@@ -127,7 +138,7 @@ cudaError_t launch_weighted_gather(const float* vals, const int32_t* gidx, int64
                                    cudaStream_t stream) {
   if (M <= 0) return cudaSuccess;
   if (k > kMaxGatherK) return cudaErrorInvalidValue;
-  GatherArgs a;
+  GatherArgs a{};
   a.vals = vals;
   a.gidx = gidx;
   a.values = static_cast<const uint16_t*>(values);
@@ -141,6 +152,123 @@ cudaError_t launch_weighted_gather(const float* vals, const int32_t* gidx, int64
   a.alpha_out = alpha_out;
   const int64_t blocks = (M + kWarps - 1) / kWarps;
   weighted_gather_kernel<<<static_cast<unsigned>(blocks), kWarps * 32, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+namespace {
+
+struct ReduceArgs {
+  const float* inbox;  // this rank's [P][block_rows][d] partials
+  float* outs[kMaxPeerRanks];
+  const int32_t* flags;  // "partials ready" flag word of each rank, on this GPU
+  int* status;
+  int64_t block_rows, M;
+  int P, rank, d, step;
+};
+
+__device__ __forceinline__ int32_t ld_acquire_sys_i32(const int32_t* p) {
+  int32_t v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait of one thread for flags[0..P) >= step.
+__device__ bool wait_flags(const int32_t* flags, int P, int step) {
+  const uint64_t t0 = globaltimer_ns();
+  for (int p = 0; p < P; ++p) {
+    while (ld_acquire_sys_i32(flags + p) < step) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    }
+  }
+  return true;
+}
+
+// One thread per 4 columns of one row of this rank's block: the sum of the P
+// partials, written to every rank's output (NVLink stores for the others).
+__global__ void __launch_bounds__(256) reduce_broadcast_kernel(const ReduceArgs a) {
+  __shared__ int ready;
+  if (threadIdx.x == 0) {
+    ready = wait_flags(a.flags, a.P, a.step) ? 1 : 0;
+    if (!ready) atomicCAS(a.status, 0, kStatusTimeout);
+  }
+  __syncthreads();
+  if (!ready) return;
+  const int c4 = a.d >> 2;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t row = t / c4;
+  const int col = static_cast<int>(t - row * c4) * 4;
+  const int64_t grow = static_cast<int64_t>(a.rank) * a.block_rows + row;
+  if (row >= a.block_rows || grow >= a.M) return;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int r = 0; r < a.P; ++r) {
+    const float4 x = *reinterpret_cast<const float4*>(
+        a.inbox + (static_cast<int64_t>(r) * a.block_rows + row) * a.d + col);
+    acc.x += x.x;
+    acc.y += x.y;
+    acc.z += x.z;
+    acc.w += x.w;
+  }
+  for (int p = 0; p < a.P; ++p)
+    *reinterpret_cast<float4*>(a.outs[p] + grow * a.d + col) = acc;
+}
+
+__global__ void peer_wait_kernel(const int32_t* flags, int P, int step, int* status) {
+  if (threadIdx.x == 0 && !wait_flags(flags, P, step)) atomicCAS(status, 0, kStatusTimeout);
+}
+
+}  // namespace
+
+cudaError_t launch_weighted_gather_peers(const float* vals, const int32_t* gidx, int64_t M, int k,
+                                         const void* values, int64_t row_begin, int64_t row_end,
+                                         int64_t ldv, int d, float* const* inboxes, int P, int rank,
+                                         int64_t block_rows, float* alpha_out, cudaStream_t stream) {
+  if (M <= 0) return cudaSuccess;
+  if (k > kMaxGatherK || P < 1 || P > kMaxPeerRanks || block_rows < 1) return cudaErrorInvalidValue;
+  GatherArgs a{};
+  a.vals = vals;
+  a.gidx = gidx;
+  a.values = static_cast<const uint16_t*>(values);
+  a.M = M;
+  a.row_begin = row_begin;
+  a.row_end = row_end;
+  a.ldv = ldv;
+  a.k = k;
+  a.d = d;
+  a.out = nullptr;
+  a.alpha_out = alpha_out;
+  for (int p = 0; p < P; ++p) a.inbox[p] = inboxes[p];
+  a.n_peers = P;
+  a.rank = rank;
+  a.block_rows = block_rows;
+  const int64_t blocks = (M + kWarps - 1) / kWarps;
+  weighted_gather_kernel<<<static_cast<unsigned>(blocks), kWarps * 32, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_reduce_broadcast_peers(const float* inbox, int P, int rank, int64_t block_rows,
+                                          int64_t M, int d, float* const* outs, const int32_t* flags,
+                                          int step, int* status, cudaStream_t stream) {
+  if (P < 1 || P > kMaxPeerRanks || block_rows < 1 || d % 4 != 0) return cudaErrorInvalidValue;
+  ReduceArgs a{};
+  a.inbox = inbox;
+  for (int p = 0; p < P; ++p) a.outs[p] = outs[p];
+  a.flags = flags;
+  a.status = status;
+  a.block_rows = block_rows;
+  a.M = M;
+  a.P = P;
+  a.rank = rank;
+  a.d = d;
+  a.step = step;
+  const int64_t threads = block_rows * (d / 4);
+  const int64_t blocks = (threads + 255) / 256;
+  reduce_broadcast_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_peer_wait(const int32_t* flags, int P, int step, int* status, cudaStream_t stream) {
+  if (P < 1 || P > kMaxPeerRanks) return cudaErrorInvalidValue;
+  peer_wait_kernel<<<1, 32, 0, stream>>>(flags, P, step, status);
   return cudaGetLastError();
 }
 

@@ -63,19 +63,31 @@ class PeerExchange:
     rank's step-(s + 1) flag, raised after that rank's merge of step s: so no
     list is overwritten while a peer still reads it.  Construction is
     collective over ``group`` (all ranks, same order).
+
+    With ``d`` the buffer also carries the value side (owner-computes sum over
+    NVLink): an inbox [P][block_rows][d] f32 receiving every rank's partial
+    sums of this rank's row block, and the replicated output [M, d] f32 that
+    the block owners write into.  A rank's partials of step s + 1 reach an
+    inbox only after its wait for every block of step s, raised after the
+    owner finished reading that inbox.
     """
 
-    _HDR = 256            # bytes: int32 flag words [0, P), status word at byte 192
-    _STATUS_OFF = 192
+    _HDR = 256            # bytes: int32 flag words: [0, 16) lists, [16, 32) partials,
+    _STATUS_OFF = 192     # [32, 48) blocks done; status word at byte 192
 
-    def __init__(self, M: int, k: int, group, device: torch.device):
+    def __init__(self, M: int, k: int, group, device: torch.device, d: int | None = None):
         self.rank, self.world = _group_rank_world(group)
         if self.world > 16:
             raise _lib.DWAArgumentError(_lib.DWA_ERR_UNSUPPORTED_SHAPE, "PeerExchange",
                                         "more than 16 ranks")
         self.M, self.k, self.group, self.device = int(M), int(k), group, device
         self._list_bytes = self.M * self.k * 8
-        nbytes = self._HDR + 2 * self._list_bytes
+        self.d = int(d) if d is not None else 0
+        self.block_rows = -(-self.M // self.world)
+        self._inbox_off = self._HDR + 2 * self._list_bytes
+        self._inbox_bytes = self.world * self.block_rows * self.d * 4
+        self._out_off = self._inbox_off + self._inbox_bytes
+        nbytes = self._out_off + self.M * self.d * 4
         lib = _lib.load()
         own = ctypes.c_void_p()
         handle = (ctypes.c_char * 64)()
@@ -103,6 +115,13 @@ class PeerExchange:
                                                       (self.M, self.k, 2), "<i4"), device=device)
                         for par in range(2)]
         self._hdr = torch.as_tensor(_DeviceBuffer(self._own, (self._HDR // 4,), "<i4"), device=device)
+        if self.d:
+            self._part_flags = (ctypes.c_void_p * self.world)(*[b + 64 for b in bases])
+            self._done_flags = (ctypes.c_void_p * self.world)(*[b + 128 for b in bases])
+            self._inboxes = (ctypes.c_void_p * self.world)(*[b + self._inbox_off for b in bases])
+            self._outs = (ctypes.c_void_p * self.world)(*[b + self._out_off for b in bases])
+            self.out = torch.as_tensor(_DeviceBuffer(self._own + self._out_off, (self.M, self.d), "<f4"),
+                                       device=device)
         self.step = 0
         dist.barrier(group=group, device_ids=[device.index])
 
@@ -127,6 +146,38 @@ class PeerExchange:
                                           out_idx.data_ptr(), self._own + self._STATUS_OFF,
                                           _stream_handle(self.device))
         _lib.check(st, "dwa_merge_topk_peers")
+
+    def gather_partials(self, top_vals: torch.Tensor, top_idx: torch.Tensor, values: torch.Tensor,
+                        row_begin: int, row_end: int, alpha_out: torch.Tensor) -> None:
+        """alpha (all rows) and this shard's partial sums, stored into the owners' inboxes
+        over NVLink; then this rank's "partials ready" flag on every rank."""
+        lib = _lib.load()
+        sh = _stream_handle(self.device)
+        with torch.cuda.device(self.device):
+            st = lib.dwa_weighted_gather_peers(top_vals.data_ptr(), top_idx.data_ptr(), self.M, self.k,
+                                               values.data_ptr(), int(row_begin), int(row_end),
+                                               values.stride(0), self.d, self._inboxes, self.world,
+                                               self.rank, self.block_rows, alpha_out.data_ptr(), sh)
+            _lib.check(st, "dwa_weighted_gather_peers")
+            st = lib.dwa_peer_signal(self._part_flags, self.world, self.rank, self.step, sh)
+        _lib.check(st, "dwa_peer_signal")
+
+    def reduce_broadcast(self) -> torch.Tensor:
+        """Sum of this rank's row block over the P inboxes, written into every rank's
+        output; then wait until every block of this step has arrived here."""
+        lib = _lib.load()
+        sh = _stream_handle(self.device)
+        status = self._own + self._STATUS_OFF
+        with torch.cuda.device(self.device):
+            st = lib.dwa_reduce_broadcast_peers(self._own + self._inbox_off, self.world, self.rank,
+                                                self.block_rows, self.M, self.d, self._outs,
+                                                self._own + 64, self.step, status, sh)
+            _lib.check(st, "dwa_reduce_broadcast_peers")
+            st = lib.dwa_peer_signal(self._done_flags, self.world, self.rank, self.step, sh)
+            _lib.check(st, "dwa_peer_signal")
+            st = lib.dwa_peer_wait(self._own + 128, self.world, self.step, status, sh)
+        _lib.check(st, "dwa_peer_wait")
+        return self.out
 
     def status(self) -> int:
         """Device status word of the peer merge (0 or DWA_ERR_TIMEOUT); syncs the device."""
@@ -255,7 +306,10 @@ class Retriever:
             raise ValueError("exchange='nvlink' needs an even k (16-byte list staging)")
         use_peer = self.world > 1 and (exchange == "nvlink" or (
             exchange == "auto" and self.k % 2 == 0 and dist.get_backend(self.group) == "nccl"))
-        self.peer = PeerExchange(self.M, self.k, self.group, dev) if use_peer else None
+        self.peer = (PeerExchange(self.M, self.k, self.group, dev, d=self.d_v)
+                     if use_peer and self.d_v % 8 == 0 else None)
+        if self.peer is not None:
+            self.out = self.peer.out  # the owners write the summed blocks straight into it
         if self.world > 1 and self.peer is None:
             self._packed_local = torch.empty((self.M, self.k, 2), dtype=i32, device=dev)
             self._packed_all = torch.empty((self.world, self.M, self.k, 2), dtype=i32, device=dev)
@@ -263,11 +317,13 @@ class Retriever:
     @property
     def kernels_per_call(self) -> int:
         """Kernels of this library one full call launches (NCCL and torch copy kernels
-        not counted): bound reset, fused score + top-k, split merge,
-        [peer signal,] [cross-shard merge,] weighted gather."""
+        not counted).  One GPU: bound reset, fused score + top-k, split merge,
+        weighted gather.  NVLink path: those four, plus the list signal, peer merge,
+        partials signal, reduce-broadcast, blocks-done signal and wait.  NCCL path:
+        the four plus the cross-shard merge."""
         if self.world == 1:
             return 4
-        return 6 if self.peer is not None else 5
+        return 10 if self.peer is not None else 5
 
     def topk_local(self, queries: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         """This rank's shard only: fused score + top-k and the split merge
@@ -318,10 +374,17 @@ class Retriever:
 
     def gather(self) -> None:
         """Owner-computes alpha-weighted sum over this rank's pool rows."""
+        if self.peer is not None:
+            self.peer.gather_partials(self.top_vals, self.top_idx, self.values, self.shard.row_begin,
+                                      self.shard.row_end, self.alpha)
+            return
         weighted_gather_into(self.top_vals, self.top_idx, self.values, self.out, self.alpha,
                              self.shard.row_begin, self.shard.row_end)
 
     def reduce(self) -> None:
+        if self.peer is not None:
+            self.peer.reduce_broadcast()
+            return
         reduce_partials(self.out, self.group)
 
     def topk(self, queries: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:

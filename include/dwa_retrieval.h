@@ -279,6 +279,35 @@ DWA_API dwa_status dwa_merge_topk_peers(const void* const* packed, int32_t P, in
                                 const int32_t* flags, int32_t step, float* out_vals,
                                 int32_t* out_idx, int32_t* status, dwa_stream_t stream);
 
+/*
+ * Owner-computes value sum with the cross-rank sum over NVLink (the
+ * reference's gather + einsum, assembly.py:104-127, on a row-sharded pool,
+ * where the partial sums of the shards must be added).  Row block o of the
+ * output, rows [o * block_rows, (o + 1) * block_rows), belongs to rank o.
+ *  1. dwa_weighted_gather_peers: alpha (all rows, local) and this shard's
+ *     partial sum of every row m, stored into the inbox of the rank owning m,
+ *     at inboxes[o] + ((rank * block_rows) + m - o * block_rows) * d (f32);
+ *     then dwa_peer_signal on the "partials ready" flag arrays.
+ *  2. dwa_reduce_broadcast_peers: waits (bounded) until every rank's partials
+ *     flag >= step, sums its block's P partials (inbox [P][block_rows][d])
+ *     and writes the sums into every rank's output (outs[p]: f32 [M, d]);
+ *     then dwa_peer_signal on the "block done" flag arrays.
+ *  3. dwa_peer_wait on the "block done" flags before the output is read.
+ * d % 8 == 0; P <= DWA_MAX_PEERS.  Timeouts (2 s) record DWA_ERR_TIMEOUT in
+ * *status.
+ */
+DWA_API dwa_status dwa_weighted_gather_peers(const float* vals, const int32_t* gidx, int64_t M,
+                                     int32_t k, const void* values, int64_t row_begin,
+                                     int64_t row_end, int64_t ldv, int32_t d,
+                                     void* const* inboxes, int32_t P, int32_t rank,
+                                     int64_t block_rows, float* alpha_out, dwa_stream_t stream);
+DWA_API dwa_status dwa_reduce_broadcast_peers(const float* inbox, int32_t P, int32_t rank,
+                                      int64_t block_rows, int64_t M, int32_t d,
+                                      void* const* outs, const int32_t* flags, int32_t step,
+                                      int32_t* status, dwa_stream_t stream);
+DWA_API dwa_status dwa_peer_wait(const int32_t* flags, int32_t P, int32_t step, int32_t* status,
+                         dwa_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Low-rank weight assembly: the consumer of the retrieved rows in a DWA
  * block, WeightAssembler.__call__ with per-position idx

@@ -112,7 +112,10 @@ def _worker(rank, world, port, q):
             op, ap, vp, ip = (t.clone() for t in rp(qs))
             on, an, vn, in_ = rn(qs)
             torch.cuda.synchronize()
-            same = same and torch.equal(ip, in_) and torch.equal(vp, vn) and torch.equal(op, on)
+            # selections and scores bit for bit; the fp32 sums of P partials may be added
+            # in another order than NCCL's ring (equal only up to rounding)
+            same = (same and torch.equal(ip, in_) and torch.equal(vp, vn)
+                    and torch.allclose(op, on, rtol=1e-5, atol=1e-5))
         st_p = rp.status()
         rp.peer.close()
         # sharded WeightAssembler (owner-computes delta + all-reduce + LayerNorm)
