@@ -121,6 +121,11 @@ def status_name(status: int) -> str:
     return load().dwa_status_string(status).decode()
 
 
+def last_error() -> str:
+    """Detail of the last failed C-ABI call on this thread."""
+    return load().dwa_last_error().decode(errors="replace")
+
+
 def check(status: int, func: str) -> None:
     if status == DWA_OK:
         return

@@ -91,22 +91,47 @@ class PeerExchange:
         lib = _lib.load()
         own = ctypes.c_void_p()
         handle = (ctypes.c_char * 64)()
+        # Set-up failures are collective: every rank takes part in the same
+        # exchanges, and all of them raise together if any rank could not
+        # allocate or map (a rank raising alone would leave the others waiting
+        # in the next collective).
+        err = ""
         with torch.cuda.device(device):
-            _lib.check(lib.dwa_peer_alloc(nbytes, ctypes.byref(own), handle), "dwa_peer_alloc")
-        self._own = own.value
+            st = lib.dwa_peer_alloc(nbytes, ctypes.byref(own), handle)
+        if st != 0:
+            err = f"dwa_peer_alloc: {_lib.last_error()}"
+        self._own = own.value if st == 0 else None
         handles = [None] * self.world
-        dist.all_gather_object(handles, bytes(handle), group=group)
+        dist.all_gather_object(handles, bytes(handle) if st == 0 else b"", group=group)
         self._opened = []
         bases = []
         with torch.cuda.device(device):
             for p in range(self.world):
+                if err:
+                    break
                 if p == self.rank:
                     bases.append(self._own)
                     continue
+                if not handles[p]:
+                    err = f"rank {p} has no exchange buffer"
+                    break
                 q = ctypes.c_void_p()
-                _lib.check(lib.dwa_peer_open(handles[p], ctypes.byref(q)), "dwa_peer_open")
+                if lib.dwa_peer_open(handles[p], ctypes.byref(q)) != 0:
+                    err = f"dwa_peer_open of rank {p}: {_lib.last_error()}"
+                    break
                 self._opened.append(q.value)
                 bases.append(q.value)
+        ok = torch.tensor([0 if err else 1], dtype=torch.int32, device=device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if int(ok.item()) == 0:
+            with torch.cuda.device(device):
+                for q in self._opened:
+                    lib.dwa_peer_close(q)
+                if self._own is not None:
+                    lib.dwa_peer_free(self._own)
+            self._opened, self._own = [], None
+            raise _lib.DWAError(_lib.DWA_ERR_CUDA, "PeerExchange",
+                                err or "a peer rank could not set up its exchange buffer")
         self._bases = bases
         self._flag_table = (ctypes.c_void_p * self.world)(*bases)
         self._list_tables = [(ctypes.c_void_p * self.world)(
@@ -306,8 +331,14 @@ class Retriever:
             raise ValueError("exchange='nvlink' needs an even k (16-byte list staging)")
         use_peer = self.world > 1 and (exchange == "nvlink" or (
             exchange == "auto" and self.k % 2 == 0 and dist.get_backend(self.group) == "nccl"))
-        self.peer = (PeerExchange(self.M, self.k, self.group, dev, d=self.d_v)
-                     if use_peer and self.d_v % 8 == 0 else None)
+        self.peer = None
+        if use_peer and self.d_v % 8 == 0:
+            try:
+                self.peer = PeerExchange(self.M, self.k, self.group, dev, d=self.d_v)
+            except _lib.DWAError:
+                # raised on every rank together; "auto" falls back to NCCL everywhere
+                if exchange == "nvlink":
+                    raise
         if self.peer is not None:
             self.out = self.peer.out  # the owners write the summed blocks straight into it
         if self.world > 1 and self.peer is None:
@@ -419,6 +450,13 @@ class Retriever:
         peer = self.peer.status() if self.peer is not None else 0
         return int(v.value) or peer
 
+    def close(self) -> None:
+        """Collective on a sharded pool: releases the NVLink exchange buffers (every
+        rank calls it, after its last call).  The retriever is unusable afterwards."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
+
 
 class HostPipeline:
     """Retrieval batches streamed from pinned host memory and back, for serving.
@@ -503,6 +541,13 @@ class HostPipeline:
 
     def status(self) -> int:
         return max(r.status() for r in self.ret)
+
+    def close(self) -> None:
+        """Collective on a sharded pool: waits for the enqueued work, then releases both
+        retrievers' NVLink buffers."""
+        self.synchronize()
+        for r in self.ret:
+            r.close()
 
 
 def project_keys(vectors: torch.Tensor, W_K: torch.Tensor, w: torch.Tensor,

@@ -117,7 +117,7 @@ def _worker(rank, world, port, q):
             same = (same and torch.equal(ip, in_) and torch.equal(vp, vn)
                     and torch.allclose(op, on, rtol=1e-5, atol=1e-5))
         st_p = rp.status()
-        rp.peer.close()
+        rp.close()
         # sharded WeightAssembler (owner-computes delta + all-reduce + LayerNorm)
         # against the unsharded one on rank 0; every rank runs the same collectives
         d_A = d_B = 64
