@@ -123,3 +123,55 @@ def test_python_api_refuses_cpu_tensors():
     q = torch.zeros(4, 16, dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="CUDA"):
         tiled_topk_fused(q, q, 2, 1.0, 0.0, 1.0, False)
+
+
+def _ptrs(*vals):
+    return (ctypes.c_void_p * len(vals))(*vals)
+
+
+def test_nvlink_and_projection_entry_points_validate_before_launch():
+    """The NVLink exchange / value-sum, key projection, assembly and EMA entry points
+    reject bad arguments on the host, before any CUDA call (runs without a GPU)."""
+    lib = _lib.load()
+    nul = ctypes.c_void_p()
+    # peer buffers and signals
+    assert lib.dwa_peer_alloc(0, ctypes.byref(nul), FAKE) == 1
+    assert lib.dwa_peer_open(None, ctypes.byref(nul)) == 1
+    assert lib.dwa_peer_signal(_ptrs(FAKE, FAKE), 0, 0, 1, None) == 1
+    assert lib.dwa_peer_signal(_ptrs(FAKE, FAKE), 2, 2, 1, None) == 1          # rank >= P
+    assert lib.dwa_peer_signal(_ptrs(FAKE, FAKE), 17, 0, 1, None) == 1         # P > 16
+    # peer merge: odd k (16-byte staging), P range, list alignment
+    out_v, out_i, st = FAKE + 4096, FAKE + 8192, FAKE + 12288
+    assert lib.dwa_merge_topk_peers(_ptrs(FAKE, FAKE), 2, 8, 5, FAKE, 1, out_v, out_i, st, None) == 2
+    assert lib.dwa_merge_topk_peers(_ptrs(FAKE), 0, 8, 4, FAKE, 1, out_v, out_i, st, None) == 1
+    assert lib.dwa_merge_topk_peers(_ptrs(FAKE + 8, FAKE), 2, 8, 4, FAKE, 1, out_v, out_i, st, None) == 1
+    # peer value sum: blocks must cover M, d % 8
+    assert lib.dwa_weighted_gather_peers(FAKE, FAKE, 100, 4, FAKE, 0, 10, 64, 64, _ptrs(FAKE, FAKE),
+                                         2, 0, 40, None, None) == 1
+    assert lib.dwa_weighted_gather_peers(FAKE, FAKE, 100, 4, FAKE, 0, 10, 64, 60, _ptrs(FAKE, FAKE),
+                                         2, 0, 50, None, None) == 2
+    assert lib.dwa_weighted_gather_peers(FAKE, FAKE, 100, 4, FAKE, 0, 10, 64, 64, _ptrs(FAKE, FAKE),
+                                         2, 2, 50, None, None) == 1
+    assert lib.dwa_reduce_broadcast_peers(FAKE, 2, 0, 40, 100, 64, _ptrs(FAKE, FAKE), FAKE, 1, st,
+                                          None) == 1
+    assert lib.dwa_reduce_broadcast_peers(FAKE, 2, 0, 50, 100, 60, _ptrs(FAKE, FAKE), FAKE, 1, st,
+                                          None) == 2
+    assert lib.dwa_peer_wait(None, 2, 1, st, None) == 1
+    assert lib.dwa_peer_wait(FAKE, 0, 1, st, None) == 1
+    # key projection: d_k, D, S, strides
+    assert lib.dwa_project_keys(FAKE, 10, 64, 64, FAKE, 64, 2, 48, FAKE, FAKE, 64, None, None) == 2
+    assert lib.dwa_project_keys(FAKE, 10, 64, 12, FAKE, 64, 2, 32, FAKE, FAKE, 64, None, None) == 2
+    assert lib.dwa_project_keys(FAKE, 10, 64, 64, FAKE, 64, 0, 32, FAKE, FAKE, 64, None, None) == 2
+    assert lib.dwa_project_keys(None, 10, 64, 64, FAKE, 64, 2, 32, FAKE, FAKE, 64, None, None) == 1
+    assert lib.dwa_project_keys(FAKE, 10, 60, 64, FAKE, 64, 2, 32, FAKE, FAKE, 64, None, None) == 1
+    assert lib.dwa_project_keys(FAKE, 10, 68, 64, FAKE, 64, 2, 32, FAKE, FAKE, 64, None, None) == 2
+    # low-rank assembly and EMA
+    assert lib.dwa_lowrank_delta(FAKE, 1, 64, FAKE, FAKE, 4, 2, FAKE, 0, 10, 2048, 12, 16, 8, FAKE,
+                                 None) == 2
+    assert lib.dwa_lowrank_delta(FAKE, 1, 64, FAKE, FAKE, 4, 2, FAKE, 0, 10, 2048, 64, 16, 0, FAKE,
+                                 None) == 2
+    assert lib.dwa_lowrank_delta(FAKE, 1, 64, FAKE, FAKE, 4, 2, FAKE, 0, 10, 100, 64, 16, 8, FAKE,
+                                 None) == 1
+    assert lib.dwa_assemble_finish(None, 0, 0, None, None, 4, 16, 1.0, None, None, 1e-6, FAKE,
+                                   None) == 1
+    assert lib.dwa_usage_ema(FAKE, FAKE, -1, 0, 10, 0.01, 0.99, FAKE, None) == 1
