@@ -53,6 +53,10 @@ WORKLOADS = {
     "lm7b_shard8": dict(M=16384, N=2097152, d=4096, k=128, use_sigmoid=False,
                         desc="7B-scale DWA LM, one layer's retrieval on one GPU of 8: 4x4096 "
                              "tokens against a 2,097,152x4096 shard (16,777,216 rows / 8), top-k 128"),
+    "op_16m": dict(M=16384, N=1 << 24, d=4096, k=128, use_sigmoid=False,
+                   desc="the 16M-entry pool of the 7B layout: queries [16384,4096] bf16; pool "
+                        "16,777,216x4096 bf16 keys ~N(0,1/4096), values ~N(0,1) (256 GiB in all: "
+                        "2 or more GPUs); top-k 128; softmax-weighted value sum"),
     "c1_op": dict(M=2048, N=16384, d=128, k=16, use_sigmoid=False,
                   desc="queries [2048,128]; pool [16384,128]; top-k 16; softmax-weighted sum"),
 }
@@ -341,7 +345,8 @@ def run_ours(args, wl):
         "config": {"workload": args.workload, "M": M, "N": N, "d": d, "k": k,
                    "n_local": n_local, "desc": wl["desc"],
                    "parallelism": f"pool rows sharded x{world}" if world > 1 else "single GPU",
-                   "l2": "inputs larger than L2 (2 GiB keys + 2 GiB values)"},
+                   "l2": (f"inputs larger than L2 ({n_local * d * 2 / 2**30:.2f} GiB keys + "
+                          f"{n_local * d * 2 / 2**30:.2f} GiB values per GPU)")},
         "e2e": {"value": M / (e2e_ms * 1e-3), "unit": "queries/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
                 "path": ("pinned host -> rank 0 -> NCCL broadcast; result read back at rank 0;"
