@@ -27,6 +27,7 @@ struct ScoreTopkPlan {
   int n_qt = 0;        // pair query tiles = ceil(M / 256)
   int64_t n_kt = 0;    // key tiles    = ceil(N / 256)
   int n_split = 0;     // key-range splits per query tile
+  int group = 0;       // query tiles per unit group (0: plain split-major order)
   int num_kb = 0;      // k-blocks of 64 along d
   int kcap = 0;        // heap capacity variant (16, 32, 64, 128)
   int nwg = 1;         // epilogue warpgroups (1 or 2), one partial list each per unit

@@ -30,7 +30,9 @@
 // Work unit = (pair query tile, contiguous range of key tiles).  Units are
 // ordered split-major so the pairs resident at one time sweep the same few
 // key ranges: each key tile is fetched from HBM about once and re-served
-// from L2 to every query tile.  Each unit leaves one sorted partial top-k list
+// from L2 to every query tile.  When the queries are too large for L2 the
+// units go in groups of a few query tiles x all splits instead, so that the
+// resident query tiles stay in L2 as well.  Each unit leaves one sorted partial top-k list
 // per row in the workspace; merge_topk.cu merges the splits, applies the
 // gate/exp and adds the global index offset.
 #include <cuda.h>
@@ -199,6 +201,7 @@ struct TopkKernelArgs {
   int k;             // kept per row
   int n_qt;          // 256-row pair query tiles
   int n_split;       // key-range splits
+  int group;         // query tiles per unit group, 0 = split-major over all query tiles
   int32_t* row_bound;  // [m_pad][kBoundSlots] shared admission bounds per query row (ordered_int images)
   float* ws_vals;    // [n_split * NWG][m_pad][k] raw scores, sorted best first
   int32_t* ws_idx;   // [n_split * NWG][m_pad][k] local key indices
@@ -239,8 +242,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
   const bool leader = cta == 0;
 
   const int pair = blockIdx.x >> 1;
-  const int qt = pair % a.n_qt;
-  const int split = pair / a.n_qt;
+  int qt, split;
+  if (a.group > 0) {
+    // groups of `group` query tiles, each group split-major over all splits
+    const int per_group = a.group * a.n_split;
+    const int g = pair / per_group;
+    const int r = pair - g * per_group;
+    const int q0 = g * a.group;
+    const int gsize = min(a.group, a.n_qt - q0);
+    split = r / gsize;
+    qt = q0 + (r - split * gsize);
+  } else {
+    qt = pair % a.n_qt;
+    split = pair / a.n_qt;
+  }
   const int64_t kt_begin = static_cast<int64_t>(split) * a.n_kt / a.n_split;
   const int64_t kt_end = static_cast<int64_t>(split + 1) * a.n_kt / a.n_split;
   const int n_tiles = static_cast<int>(kt_end - kt_begin);
@@ -667,6 +682,19 @@ bool plan_score_topk(int64_t M, int64_t N, int d, int k, int num_sms, ScoreTopkP
     }
   }
   p.n_split = best_s;
+  // Unit order.  Split-major over all query tiles keeps the resident pairs on
+  // a few key ranges, so each key tile is read from HBM about once; that
+  // needs the whole query set to stay in L2.  Once the queries exceed half
+  // of L2, every key tile would re-read its pair's query tile from HBM, so
+  // units go in groups of G query tiles x all splits (G * n_split about the
+  // resident pair count): G query tiles stay in L2 and each key tile is
+  // read once per group.
+  const int64_t query_bytes = p.m_pad * static_cast<int64_t>(p.num_kb) * kTileK * 2;
+  p.group = 0;
+  if (query_bytes > (64ll << 20)) {
+    const int64_t g = std::max<int64_t>(1, pairs / p.n_split);
+    if (g < n_qt) p.group = static_cast<int>(g);
+  }
   p.ws_bytes = kStatusBytes + static_cast<size_t>(p.m_pad) * kBoundSlots * 4u +
                static_cast<size_t>(p.n_split) * p.nwg * static_cast<size_t>(k) *
                    static_cast<size_t>(p.m_pad) * 8u;
@@ -695,6 +723,7 @@ cudaError_t launch_score_topk(const ScoreTopkPlan& p, const void* q, int64_t ldq
   args.k = p.k;
   args.n_qt = p.n_qt;
   args.n_split = p.n_split;
+  args.group = p.group;
   args.status = reinterpret_cast<int*>(wsb);
   const size_t list_elems = static_cast<size_t>(p.n_split) * p.nwg * p.k * p.m_pad;
   const size_t bound_bytes = static_cast<size_t>(p.m_pad) * kBoundSlots * 4u;
