@@ -279,6 +279,32 @@ def test_exact_ties_across_key_splits(lib, M, N, d, k):
     np.testing.assert_allclose(v.cpu().numpy(), rv, rtol=1e-6)
 
 
+@pytest.mark.parametrize("k", [32, 64, 128])
+def test_exact_ties_grouped_unit_order(lib, k):
+    """Queries larger than half of L2 (9651 x 4096 bf16, 79 MB) switch the
+    score kernel to query-tile groups: here 38 query tiles x 3 key splits, in
+    groups of 24 and 14 query tiles (a ragged last group, ragged M and N).
+    Integer inputs keep every score exact (|s| <= 4 * 4096 < 2^24), and
+    duplicated key rows tie across splits and groups; indices must equal the
+    oracle's top_k on exactly recomputed scores, lower index first on ties."""
+    dev = _dev()
+    M, N, d = 9651, 8205, 4096
+    g = torch.Generator(device=dev).manual_seed(k)
+    q = torch.randint(-2, 3, (M, d), generator=g, device=dev).to(torch.bfloat16)
+    base = torch.randint(-2, 3, (N // 8, d), generator=g, device=dev).to(torch.bfloat16)
+    keys = base[torch.randint(0, N // 8, (N,), generator=g, device=dev)].contiguous()
+    T = 64.0  # s / T is exact and exp(s / T) stays finite and strictly ordered
+    v, i = lib.tiled_topk_fused(q, keys, k, 1.0, 0.0, T, False)
+    torch.cuda.synchronize()
+    got_v, got_i = v.cpu().numpy(), i.cpu().numpy()
+    kf = keys.float()
+    for r0 in range(0, M, 1024):
+        s = (q[r0:r0 + 1024].float() @ kf.T).double().cpu().numpy()
+        rv, ri = O.top_k(O.fused_score(s, 1.0, 0.0, T, False), k)
+        np.testing.assert_array_equal(got_i[r0:r0 + 1024], ri)
+        np.testing.assert_allclose(got_v[r0:r0 + 1024], rv, rtol=1e-5)
+
+
 def test_pallas_hybrid_forward_matches_reference(lib, golden):
     """MultiAspectRetrieval.pallas_hybrid_forward with the parameters the
     reference ran with (its own 4-chip shard_map run produced the fixture)."""
