@@ -604,12 +604,24 @@ def main(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-assembly", action="store_true",
                     help="skip the WeightAssembler (low-rank consumer) measurement")
+    ap.add_argument("--shape", default="",
+                    help="MxNxDxK: run the chosen workload's step at these sizes instead "
+                         "(profiling and sweeps; the workload is then named by its sizes)")
     ap.add_argument("--lm", default="small_char,large_1b",
                     help="DWA LM forwards to time after the op (comma list; empty to skip)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     wl = WORKLOADS[args.workload]
+    if args.shape:
+        try:
+            M, N, d, k = (int(x) for x in args.shape.lower().split("x"))
+        except ValueError:
+            ap.error("--shape must be MxNxDxK, e.g. 16384x262144x4096x64")
+        wl = dict(wl, M=M, N=N, d=d, k=k,
+                  desc=f"queries [{M},{d}] bf16 ~N(0,1); pool {N}x{d} bf16 keys ~N(0,1/{d}), "
+                       f"values ~N(0,1); top-k {k}; softmax-weighted value sum")
+        args.workload = f"shape_{M}x{N}x{d}x{k}"
     if args.impl == "reference":
         return run_reference(args, wl)
     return run_ours(args, wl)
