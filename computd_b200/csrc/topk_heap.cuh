@@ -5,9 +5,11 @@
 // root score is the admission threshold.  An entry is 8 bytes (score bits,
 // index), read and written with one 64-bit shared-memory access.  Entries of
 // all threads are interleaved ([pos][thread], stride = threads): at any heap
-// position the 32 lanes of a warp touch 32 consecutive entries, and because
-// the stride is a multiple of 32 entries, lanes at DIFFERENT positions still
-// map to distinct bank pairs, so sift-downs never conflict.
+// position the 32 lanes of a warp touch 32 consecutive entries (two
+// wavefronts).  Because the stride is a multiple of 32 entries, a lane's bank
+// pair depends only on its lane index, so lanes at different positions within
+// a half-warp never conflict; lanes 16 apart share a bank pair, and a sift in
+// which lanes have diverged can take an extra wavefront for them.
 //
 // Order ("better"): higher score first; among equal scores the LOWER index
 // first — the tie rule of jax.lax.top_k that the reference relies on
