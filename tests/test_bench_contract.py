@@ -13,9 +13,10 @@ import pytest
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def _run(*args, timeout=300):
+def _run(*args, timeout=300, env=None):
     return subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), *args], cwd=ROOT,
-                          capture_output=True, text=True, timeout=timeout)
+                          capture_output=True, text=True, timeout=timeout,
+                          env=None if env is None else {**os.environ, **env})
 
 
 def _line(res):
@@ -49,6 +50,19 @@ def test_shape_override_names_the_workload_by_its_sizes():
     cfg = d["config"]
     assert cfg["workload"] == "shape_300x5000x64x32"
     assert (cfg["M"], cfg["N"], cfg["d"], cfg["k"]) == (300, 5000, 64, 32)
+
+
+def test_reference_arm_other_ranks_exit_quietly():
+    """Under torchrun with N > 1 only rank 0 times and prints the reference arm."""
+    res = _run("--impl", "reference", "--gpus", "2", "--workload", "c1_op", "--steps", "1",
+               "--warmup", "3", "--cpu-queries", "4",
+               env={"RANK": "1", "LOCAL_RANK": "1", "WORLD_SIZE": "2"})
+    assert res.returncode == 0, res.stderr[-1000:]
+    assert not [ln for ln in res.stdout.splitlines() if ln.startswith("{")]
+    d = _line(_run("--impl", "reference", "--gpus", "2", "--workload", "c1_op", "--steps", "1",
+                   "--warmup", "3", "--cpu-queries", "4",
+                   env={"RANK": "0", "LOCAL_RANK": "0", "WORLD_SIZE": "2"}))
+    assert d["n_gpus"] == 2 and d["impl"] == "reference"
 
 
 @pytest.mark.parametrize("args", [
