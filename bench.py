@@ -62,6 +62,16 @@ WORKLOADS = {
 }
 METRIC = "fused score+top-k retrieval queries/s"
 
+# dram__bytes_read.sum + dram__bytes_write.sum of one full-size launch of the
+# fused score + top-k kernel, from a separate ncu capture of the same workload
+# (one pass, after the plain command exited 0).  External evidence, not
+# measured by the run that prints it; the profile file holds the command.
+NCU_TRAFFIC = {
+    "op_at_scale": {"bytes_per_launch": 3042590000,
+                    "source": "profiles/score_topk_op_at_scale.md (ncu, one full-size launch)",
+                    "captured": "2026-12-02"},
+}
+
 
 def _peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -332,9 +342,11 @@ def run_ours(args, wl):
                 "peak_source": f"{peak_src} bf16 dense burst (MEASURED_PEAKS.json)",
                 "kernel": "score_topk_kernel + split merge (dwa_score_topk) on this GPU's shard",
                 "flops_per_launch": flops, "ms_per_launch": topk_avg_ms,
-                "traffic": _ncu_traffic(args.workload, world),
-                "traffic_source": (f"profiles/score_topk_{args.workload}.md: ncu dram__bytes_read.sum"
-                                   " + dram__bytes_write.sum of one full-size launch"),
+                # DRAM bytes are not measurable inside a timed run: null here, and the
+                # figure of a separate ncu capture of this workload, when one exists, is
+                # reported beside it as external evidence with where it came from
+                "traffic": None,
+                "traffic_external": NCU_TRAFFIC.get(args.workload) if world == 1 else None,
                 "algorithmic_bytes_per_launch": 2.0 * n_local * d + 2.0 * M * d + 8.0 * M * k}
 
     line = {
@@ -550,19 +562,6 @@ def measure_lm(cfg_name, world, rank, local_rank, warmup=3, steps=3):
                          "peak": "bf16 burst (MEASURED_PEAKS.json)"},
             "warmup": warmup, "steps": steps, "device_status": status,
             "cuda_graph": graphed}
-
-
-def _ncu_traffic(workload, world):
-    """DRAM bytes per launch of the fused kernel from the committed ncu summary, if any."""
-    path = os.path.join(ROOT, "profiles", f"score_topk_{workload}.md")
-    try:
-        with open(path) as f:
-            for line in f:
-                if line.startswith("traffic_bytes_per_launch_full_size:") and world == 1:
-                    return float(line.split(":", 1)[1].split()[0])
-    except OSError:
-        pass
-    return None
 
 
 def _cpu_baseline(args, wl, keys_dev, values_dev, q_dev):

@@ -14,8 +14,8 @@ from .pool import ShardSpec, init_normal, new_normal
 from .retrieval import (HostPipeline, MultiAspectRetrieval, PeerExchange, Retriever, chip_topk,
                         project_keys,
                         exchange_candidates, reduce_partials)
-from .tiled_topk import (merge_topk, score_topk_into, tiled_topk_fallback, tiled_topk_fused,
-                         workspace_bytes)
+from .tiled_topk import (merge_topk, score_params, score_topk_into, seq_scores,
+                         tiled_topk_fallback, tiled_topk_fused, workspace_bytes)
 
 __all__ = [
     "DWA_MAX_K", "DWAArgumentError", "DWAError", "load_library",
@@ -23,5 +23,6 @@ __all__ = [
     "normalise_alpha", "weighted_gather_into", "weighted_value_sum", "MultiAspectRetrieval",
     "ShardSpec", "init_normal", "new_normal",
     "HostPipeline", "PeerExchange", "Retriever", "chip_topk", "project_keys", "exchange_candidates", "reduce_partials",
-    "merge_topk", "score_topk_into", "tiled_topk_fallback", "tiled_topk_fused", "workspace_bytes",
+    "merge_topk", "score_params", "score_topk_into", "seq_scores", "tiled_topk_fallback",
+    "tiled_topk_fused", "workspace_bytes",
 ]

@@ -38,6 +38,13 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dwa_score_topk_noalloc": (_i32, [_c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _i32, _i32,
                                       _f32, _f32, _f32, _i32, _i64, _c_void_p, _c_void_p,
                                       _c_void_p]),
+    "dwa_score_topk_dev": (_i32, [_c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _i32, _i32,
+                                  _c_void_p, _i32, _i64, _c_void_p, _c_void_p, _c_void_p,
+                                  ctypes.c_size_t, _c_void_p]),
+    "dwa_seq_scores": (_i32, [_c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _i32, _c_void_p,
+                              _i32, _c_void_p, _i64, _c_void_p, _i64, _c_void_p, _c_void_p]),
+    "dwa_score_backward_dev": (_i32, [_c_void_p, _c_void_p, _c_void_p, _i64, _i32, _c_void_p,
+                                      _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
     "dwa_merge_topk": (_i32, [_c_void_p, _c_void_p, _i32, _i64, _i32, _c_void_p, _c_void_p,
                               _c_void_p]),
     "dwa_merge_topk_strided": (_i32, [_c_void_p, _c_void_p, _i32, _i64, _i32, _i64, _i64, _i64,

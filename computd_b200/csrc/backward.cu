@@ -20,6 +20,7 @@
 #include <cstdint>
 
 #include "dwa_internal.h"
+#include "score_params.cuh"
 
 namespace dwa {
 
@@ -84,10 +85,24 @@ __global__ void __launch_bounds__(kWarps * 32)
 __global__ void __launch_bounds__(kWarps * 32)
     score_backward_kernel(const float* v, const float* s, const float* dalpha, int64_t M, int k,
                           float lambda_sharp, float tau, float T, int use_sigmoid, float* ds,
-                          float* dparams) {
+                          float* dparams, const float* params, int* status) {
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t m = static_cast<int64_t>(blockIdx.x) * kWarps + w;
   if (m >= M) return;
+  if (params != nullptr) {
+    // device-held {lambda_sharp, tau, T}: read here, checked here
+    const ScoreParams p = load_score_params(params, lambda_sharp, tau, T);
+    lambda_sharp = p.lambda_sharp;
+    tau = p.tau;
+    T = p.T;
+    const bool ok = T > 0.0f && isfinite(T) &&
+                    (!use_sigmoid || (isfinite(lambda_sharp) && isfinite(tau)));
+    if (!ok) {
+      if (lane == 0) record_status(status, kStatusDeviceCheck);
+      for (int j = lane; j < k; j += 32) ds[m * k + j] = NAN;
+      return;
+    }
+  }
   float sv = 0.f, sdv = 0.f;
   for (int j = lane; j < k; j += 32) {
     const float vj = v[m * k + j];
@@ -206,10 +221,11 @@ cudaError_t launch_gather_dot(const void* a, int a_bf16, int64_t lda, const int3
 
 cudaError_t launch_score_backward(const float* v, const float* s, const float* dalpha, int64_t M,
                                   int k, float lambda_sharp, float tau, float T, int use_sigmoid,
-                                  float* ds, float* dparams, cudaStream_t stream) {
+                                  float* ds, float* dparams, cudaStream_t stream,
+                                  const float* params, int* status) {
   if (M <= 0) return cudaSuccess;
   score_backward_kernel<<<blocks_for(M), kWarps * 32, 0, stream>>>(
-      v, s, dalpha, M, k, lambda_sharp, tau, T, use_sigmoid, ds, dparams);
+      v, s, dalpha, M, k, lambda_sharp, tau, T, use_sigmoid, ds, dparams, params, status);
   return cudaGetLastError();
 }
 

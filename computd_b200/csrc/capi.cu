@@ -78,13 +78,19 @@ size_t dwa_score_topk_workspace(int64_t M, int64_t N_local, int32_t d, int32_t k
   return plan.ws_bytes;
 }
 
-dwa_status dwa_score_topk(const void* q, int64_t M, int64_t ldq, const void* keys,
-                          int64_t N_local, int64_t ldk, int32_t d, int32_t k, float lambda_sharp,
-                          float tau, float T, int32_t use_sigmoid, int64_t idx_offset,
-                          float* out_vals, int32_t* out_idx, void* ws, size_t ws_bytes,
-                          dwa_stream_t stream) {
-  if (M < 0 || N_local < 0) return fail(DWA_ERR_INVALID_ARG, "negative size (M=%lld, N=%lld)",
-                                        (long long)M, (long long)N_local);
+}  // extern "C"
+
+namespace {
+// dwa_score_topk with the runtime scalars either as host values (params ==
+// nullptr, checked here) or as a device array {lambda_sharp, tau, T}
+// (checked by the merge kernel, which records DWA_ERR_DEVICE_CHECK).
+dwa_status score_topk_impl(const char* fn, const void* q, int64_t M, int64_t ldq,
+                           const void* keys, int64_t N_local, int64_t ldk, int32_t d, int32_t k,
+                           float lambda_sharp, float tau, float T, const float* params,
+                           int32_t use_sigmoid, int64_t idx_offset, float* out_vals,
+                           int32_t* out_idx, void* ws, size_t ws_bytes, dwa_stream_t stream) {
+  if (M < 0 || N_local < 0) return fail(DWA_ERR_INVALID_ARG, "%s: negative size (M=%lld, N=%lld)",
+                                        fn, (long long)M, (long long)N_local);
   if (M == 0) return ok();
   if (!q || !keys || !out_vals || !out_idx)
     return fail(DWA_ERR_INVALID_ARG, "null queries/keys/output pointer");
@@ -108,13 +114,17 @@ dwa_status dwa_score_topk(const void* q, int64_t M, int64_t ldq, const void* key
   if (idx_offset < 0 || N_local + idx_offset > INT32_MAX)
     return fail(DWA_ERR_INVALID_ARG, "idx_offset=%lld out of the int32 index range",
                 (long long)idx_offset);
-  if (!(T > 0.f) || !std::isfinite(T))
-    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "temperature T must be finite and > 0");
-  if (use_sigmoid && (!(lambda_sharp >= 0.f) || !std::isfinite(lambda_sharp) ||
-                      !std::isfinite(tau)))
-    return fail(DWA_ERR_UNSUPPORTED_SHAPE,
-                "the gate needs finite lambda_sharp >= 0 and finite tau (selection on raw "
-                "scores requires a monotone gate)");
+  if (params != nullptr) {
+    if (!aligned(params, 4)) return fail(DWA_ERR_INVALID_ARG, "%s: params must be 4-byte aligned", fn);
+  } else {
+    if (!(T > 0.f) || !std::isfinite(T))
+      return fail(DWA_ERR_UNSUPPORTED_SHAPE, "temperature T must be finite and > 0");
+    if (use_sigmoid && (!(lambda_sharp >= 0.f) || !std::isfinite(lambda_sharp) ||
+                        !std::isfinite(tau)))
+      return fail(DWA_ERR_UNSUPPORTED_SHAPE,
+                  "the gate needs finite lambda_sharp >= 0 and finite tau (selection on raw "
+                  "scores requires a monotone gate)");
+  }
   dwa::ScoreTopkPlan plan;
   if (!dwa::plan_score_topk(M, N_local, d, k, dwa::device_sm_count(), &plan))
     return fail(DWA_ERR_UNSUPPORTED_SHAPE, "no launch plan for this shape");
@@ -126,8 +136,58 @@ dwa_status dwa_score_topk(const void* q, int64_t M, int64_t ldq, const void* key
   const char* detail = nullptr;
   cudaError_t e = dwa::launch_score_topk(plan, q, ldq, keys, ldk, lambda_sharp, tau, T,
                                          use_sigmoid ? 1 : 0, idx_offset, out_vals, out_idx, ws,
-                                         static_cast<cudaStream_t>(stream), &detail);
-  if (e != cudaSuccess) return cuda_fail(e, "dwa_score_topk launch", detail);
+                                         static_cast<cudaStream_t>(stream), &detail, params);
+  if (e != cudaSuccess) return cuda_fail(e, fn, detail);
+  return ok();
+}
+}  // namespace
+
+extern "C" {
+
+dwa_status dwa_score_topk(const void* q, int64_t M, int64_t ldq, const void* keys,
+                          int64_t N_local, int64_t ldk, int32_t d, int32_t k, float lambda_sharp,
+                          float tau, float T, int32_t use_sigmoid, int64_t idx_offset,
+                          float* out_vals, int32_t* out_idx, void* ws, size_t ws_bytes,
+                          dwa_stream_t stream) {
+  return score_topk_impl("dwa_score_topk", q, M, ldq, keys, N_local, ldk, d, k, lambda_sharp, tau,
+                         T, nullptr, use_sigmoid, idx_offset, out_vals, out_idx, ws, ws_bytes,
+                         stream);
+}
+
+dwa_status dwa_score_topk_dev(const void* q, int64_t M, int64_t ldq, const void* keys,
+                              int64_t N_local, int64_t ldk, int32_t d, int32_t k,
+                              const float* params, int32_t use_sigmoid, int64_t idx_offset,
+                              float* out_vals, int32_t* out_idx, void* ws, size_t ws_bytes,
+                              dwa_stream_t stream) {
+  if (M > 0 && !params) return fail(DWA_ERR_INVALID_ARG, "dwa_score_topk_dev: null params");
+  return score_topk_impl("dwa_score_topk_dev", q, M, ldq, keys, N_local, ldk, d, k, 0.f, 0.f, 1.f,
+                         params, use_sigmoid, idx_offset, out_vals, out_idx, ws, ws_bytes, stream);
+}
+
+dwa_status dwa_seq_scores(const float* q, int64_t B, int64_t ldq, const void* keys, int64_t N,
+                          int64_t ldk, int32_t d, const float* params, int32_t use_sigmoid,
+                          float* sims, int64_t lds, float* fused, int64_t ldf, int32_t* status,
+                          dwa_stream_t stream) {
+  if (B < 0 || N < 0) return fail(DWA_ERR_INVALID_ARG, "dwa_seq_scores: negative size");
+  if (B == 0 || N == 0) return ok();
+  if (!q || !keys || !sims) return fail(DWA_ERR_INVALID_ARG, "dwa_seq_scores: null q/keys/sims");
+  if (fused && !params)
+    return fail(DWA_ERR_INVALID_ARG, "dwa_seq_scores: the fused scores need the params array");
+  if (d < 8 || d % 8 != 0 || d > dwa::seq_scores_max_d())
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_seq_scores: d=%d must be a multiple of 8 in [8, %d]",
+                d, dwa::seq_scores_max_d());
+  if (ldq < d || ldk < d || lds < N || (fused && ldf < N))
+    return fail(DWA_ERR_INVALID_ARG, "dwa_seq_scores: a row stride is below its row length");
+  if (ldk % 8 != 0 || !aligned(keys, 16))
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_seq_scores: keys need 16-byte aligned rows");
+  if (!aligned(q, 4) || !aligned(sims, 4) || (fused && !aligned(fused, 4)) ||
+      (params && !aligned(params, 4)))
+    return fail(DWA_ERR_INVALID_ARG, "dwa_seq_scores: f32 arrays must be 4-byte aligned");
+  if (N > INT32_MAX) return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_seq_scores: N too large");
+  cudaError_t e = dwa::launch_seq_scores(q, B, ldq, keys, N, ldk, d, params, use_sigmoid ? 1 : 0,
+                                         sims, lds, fused, ldf, status,
+                                         static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_seq_scores launch");
   return ok();
 }
 
@@ -273,6 +333,23 @@ dwa_status dwa_score_backward(const float* vals, const float* scores, const floa
                                              use_sigmoid ? 1 : 0, dscores, dparams,
                                              static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "dwa_score_backward launch");
+  return ok();
+}
+
+dwa_status dwa_score_backward_dev(const float* vals, const float* scores, const float* dalpha,
+                                  int64_t M, int32_t k, const float* params, int32_t use_sigmoid,
+                                  float* dscores, float* dparams, int32_t* status,
+                                  dwa_stream_t stream) {
+  if (M < 0) return fail(DWA_ERR_INVALID_ARG, "negative M");
+  if (M == 0) return ok();
+  if (!vals || !scores || !dalpha || !dscores || !params)
+    return fail(DWA_ERR_INVALID_ARG, "dwa_score_backward_dev: null pointer");
+  if (!aligned(params, 4)) return fail(DWA_ERR_INVALID_ARG, "dwa_score_backward_dev: params misaligned");
+  if (k < 1) return fail(DWA_ERR_INVALID_ARG, "k=%d must be >= 1", k);
+  cudaError_t e = dwa::launch_score_backward(vals, scores, dalpha, M, k, 0.f, 0.f, 1.f,
+                                             use_sigmoid ? 1 : 0, dscores, dparams,
+                                             static_cast<cudaStream_t>(stream), params, status);
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_score_backward_dev launch");
   return ok();
 }
 

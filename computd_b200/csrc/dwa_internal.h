@@ -45,23 +45,27 @@ bool plan_score_topk(int64_t M, int64_t N, int d, int k, int num_sms, ScoreTopkP
 int device_sm_count();
 
 // Launches the fused kernel + split merge.  Arguments were validated by the caller.
+// `params` (device {lambda, tau, T}, may be null) overrides the host scalars.
 cudaError_t launch_score_topk(const ScoreTopkPlan& plan, const void* q, int64_t ldq,
                               const void* keys, int64_t ldk, float lambda_sharp, float tau,
                               float T, int use_sigmoid, int64_t idx_offset, float* out_vals,
                               int32_t* out_idx, void* ws, cudaStream_t stream,
-                              const char** err_detail);
+                              const char** err_detail, const float* params = nullptr);
 
 // Generic candidate merge.  Candidate (list l, position p, row r) lives at
 // offset l*stride_list + p*stride_pos + r*stride_row.  When `transform` is
 // set, candidate scores are raw dot products s and the output holds
 // v(s) = [sigmoid(lambda (s - tau))] * exp(s / T); otherwise the scores are
-// copied.  Indices get `idx_offset` added.
+// copied.  Indices get `idx_offset` added.  `params` (device {lambda, tau,
+// T}, may be null) overrides the host scalars; scalars that fail the device
+// check record DWA_ERR_DEVICE_CHECK in `status` (may be null).
 cudaError_t launch_merge_topk(const float* cand_vals, const int32_t* cand_idx, int n_lists,
                               int k_in, int64_t stride_list, int64_t stride_pos,
                               int64_t stride_row, int64_t M, int k, int transform,
                               float lambda_sharp, float tau, float T, int use_sigmoid,
                               int64_t idx_offset, float* out_vals, int32_t* out_idx,
-                              cudaStream_t stream);
+                              cudaStream_t stream, const float* params = nullptr,
+                              int* status = nullptr);
 
 cudaError_t launch_weighted_gather(const float* vals, const int32_t* gidx, int64_t M, int k,
                                    const void* values, int64_t row_begin, int64_t row_end,
@@ -73,7 +77,17 @@ cudaError_t launch_gather_dot(const void* a, int a_bf16, int64_t lda, const int3
                               int64_t ldr, int d, float* out, cudaStream_t stream);
 cudaError_t launch_score_backward(const float* v, const float* s, const float* dalpha, int64_t M,
                                   int k, float lambda_sharp, float tau, float T, int use_sigmoid,
-                                  float* ds, float* dparams, cudaStream_t stream);
+                                  float* ds, float* dparams, cudaStream_t stream,
+                                  const float* params = nullptr, int* status = nullptr);
+
+// seq_scores.cu: sims[b, n] = <q[b], keys[n]> (f32 x bf16, fp32 accumulate)
+// and fused[b, n] = v(sims[b, n]) for a few (<= 64) query rows against a
+// whole key shard.  Arguments validated by the caller.
+cudaError_t launch_seq_scores(const float* q, int64_t B, int64_t ldq, const void* keys, int64_t N,
+                              int64_t ldk, int d, const float* params, int use_sigmoid,
+                              float* sims, int64_t lds, float* fused, int64_t ldf, int* status,
+                              cudaStream_t stream);
+int seq_scores_max_d();  // largest d launch_seq_scores accepts
 cudaError_t launch_gather_rows(const float* wts, const int32_t* idx, int64_t M, int k,
                                const void* rows, int64_t row_begin, int64_t row_end, int64_t ldr,
                                int d, float* out, int accumulate, cudaStream_t stream);

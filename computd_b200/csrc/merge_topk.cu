@@ -22,6 +22,7 @@
 #include <cmath>
 
 #include "dwa_internal.h"
+#include "score_params.cuh"
 #include "sm100_ptx.cuh"
 #include "topk_heap.cuh"
 
@@ -49,6 +50,7 @@ struct MergeArgs {
   int n_lists, k_in, k;
   int transform, use_sigmoid;
   float lambda_sharp, tau, T;
+  const float* params;  // device {lambda_sharp, tau, T} overriding the values above, or null
   float* out_v;
   int32_t* out_i;
 };
@@ -109,6 +111,19 @@ __global__ void __launch_bounds__(kWarps * 32) merge_sorted_kernel(const MergeAr
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + w;
   if (row >= a.M) return;  // warp-uniform; only warp-level synchronisation below
+  ScoreParams sp{a.lambda_sharp, a.tau, a.T};
+  if (a.transform) {
+    sp = load_score_params(a.params, a.lambda_sharp, a.tau, a.T);
+    if (!score_params_ok(sp, a.use_sigmoid)) {
+      // device-held scalars the selection cannot honour: no top-k is defined
+      if (lane == 0) record_status(a.status, kStatusDeviceCheck);
+      for (int j = lane; j < a.k; j += 32) {
+        a.out_v[row * a.k + j] = NAN;
+        a.out_i[row * a.k + j] = -1;
+      }
+      return;
+    }
+  }
   if constexpr (kPeer) {
     // Wait (bounded) until every peer has published this step's lists.
     bool ready = true;
@@ -226,7 +241,7 @@ __global__ void __launch_bounds__(kWarps * 32) merge_sorted_kernel(const MergeAr
 
   if (a.transform) {
     for (int j = lane; j < a.k; j += 32)
-      st_s[w][j] = fused_score(st_s[w][j], a.use_sigmoid, a.lambda_sharp, a.tau, a.T);
+      st_s[w][j] = fused_score(st_s[w][j], a.use_sigmoid, sp.lambda_sharp, sp.tau, sp.T);
     __syncwarp();
     // v is non-decreasing in s, so the list is ordered by v already; entries
     // whose v became equal must still be ordered by lower index first.
@@ -263,7 +278,7 @@ cudaError_t launch_merge_topk(const float* cand_vals, const int32_t* cand_idx, i
                               int64_t stride_row, int64_t M, int k, int transform,
                               float lambda_sharp, float tau, float T, int use_sigmoid,
                               int64_t idx_offset, float* out_vals, int32_t* out_idx,
-                              cudaStream_t stream) {
+                              cudaStream_t stream, const float* params, int* status) {
   if (M <= 0) return cudaSuccess;
   if (n_lists < 1 || n_lists > kMaxSplits || k < 1 || k > DWA_MERGE_MAX_K)
     return cudaErrorInvalidValue;
@@ -283,6 +298,8 @@ cudaError_t launch_merge_topk(const float* cand_vals, const int32_t* cand_idx, i
   a.lambda_sharp = lambda_sharp;
   a.tau = tau;
   a.T = T;
+  a.params = params;
+  a.status = status;
   a.out_v = out_vals;
   a.out_i = out_idx;
   const int64_t blocks = (M + kWarps - 1) / kWarps;

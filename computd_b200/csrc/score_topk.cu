@@ -705,7 +705,7 @@ bool plan_score_topk(int64_t M, int64_t N, int d, int k, int num_sms, ScoreTopkP
 cudaError_t launch_score_topk(const ScoreTopkPlan& p, const void* q, int64_t ldq, const void* keys,
                               int64_t ldk, float lambda_sharp, float tau, float T, int use_sigmoid,
                               int64_t idx_offset, float* out_vals, int32_t* out_idx, void* ws,
-                              cudaStream_t stream, const char** err_detail) {
+                              cudaStream_t stream, const char** err_detail, const float* params) {
   CUtensorMap mq, mk;
   if (!make_bf16_tile_map(&mq, q, static_cast<uint64_t>(p.d), static_cast<uint64_t>(p.M),
                           static_cast<uint64_t>(ldq), kTileK, kTileM) ||
@@ -745,7 +745,7 @@ cudaError_t launch_score_topk(const ScoreTopkPlan& p, const void* q, int64_t ldq
   return launch_merge_topk(args.ws_vals, args.ws_idx, p.n_split * p.nwg, p.k,
                            static_cast<int64_t>(p.k) * p.m_pad, 1, p.k, p.M, p.k,
                            /*transform=*/1, lambda_sharp, tau, T, use_sigmoid, idx_offset, out_vals,
-                           out_idx, stream);
+                           out_idx, stream, params, args.status);
 }
 
 cudaError_t launch_plan(const ScoreTopkPlan& p, const CUtensorMap& mq, const CUtensorMap& mk,

@@ -21,6 +21,12 @@
 // admission bounds are re-initialised by every call (stream-ordered), and the
 // partial lists are fully overwritten, but two calls whose kernels overlap on
 // the GPU (different streams without ordering) race on the scratch.
+//
+// The scratch used is the current device's, so the stream must belong to the
+// current device (a stream of another GPU is refused with
+// DWA_ERR_INVALID_ARG).  Only a successful address lookup is remembered: a
+// lookup that failed (for example because the first call ran inside a stream
+// capture) is tried again by the next call.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -38,11 +44,24 @@ constexpr int kMaxDevices = 64;
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
 struct DeviceScratch {
-  std::once_flag once;
-  void* ptr = nullptr;
-  cudaError_t err = cudaSuccess;
+  std::mutex mu;
+  void* ptr = nullptr;  // set once a lookup has succeeded
 };
 DeviceScratch g_scratch[kMaxDevices];
+
+// Address of this device's scratch array (dev must be current).
+cudaError_t scratch_address(int dev, void** out) {
+  DeviceScratch& s = g_scratch[dev];
+  std::lock_guard<std::mutex> lock(s.mu);
+  if (s.ptr == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) return e != cudaSuccess ? e : cudaErrorInvalidSymbol;
+    s.ptr = p;
+  }
+  *out = s.ptr;
+  return cudaSuccess;
+}
 
 }  // namespace
 
@@ -72,22 +91,41 @@ DWA_API dwa_status dwa_score_topk_noalloc(const void* q, int64_t M, int64_t ldq,
              cudaGetErrorString(e));
     return dwa::record_error(DWA_ERR_CUDA, msg);
   }
-  DeviceScratch& s = g_scratch[dev];
-  std::call_once(s.once, [&s] {
-    s.err = cudaGetSymbolAddress(&s.ptr, g_noalloc_scratch);
-    if (s.err != cudaSuccess) s.ptr = nullptr;
-  });
-  if (s.err != cudaSuccess || s.ptr == nullptr) {
+  if (M <= 0) {
+    // nothing to launch: the workspace entry point validates and returns
+    return dwa_score_topk(q, M, ldq, keys, N_local, ldk, d, k, lambda_sharp, tau, T, use_sigmoid,
+                          idx_offset, out_vals, out_idx, nullptr, 0, stream);
+  }
+  int stream_dev = dev;
+  e = cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &stream_dev);
+  if (e != cudaSuccess) {
+    char msg[256];
+    snprintf(msg, sizeof(msg), "dwa_score_topk_noalloc: cudaStreamGetDevice failed (%s)",
+             cudaGetErrorString(e));
+    return dwa::record_error(DWA_ERR_CUDA, msg);
+  }
+  if (stream_dev != dev) {
     char msg[256];
     snprintf(msg, sizeof(msg),
-             "dwa_score_topk_noalloc: cudaGetSymbolAddress of the built-in scratch failed (%s)",
-             cudaGetErrorString(s.err));
+             "dwa_score_topk_noalloc: the stream belongs to device %d but device %d is current; "
+             "the built-in scratch used is the current device's",
+             stream_dev, dev);
+    return dwa::record_error(DWA_ERR_INVALID_ARG, msg);
+  }
+  void* scratch = nullptr;
+  e = scratch_address(dev, &scratch);
+  if (e != cudaSuccess) {
+    char msg[256];
+    snprintf(msg, sizeof(msg),
+             "dwa_score_topk_noalloc: cudaGetSymbolAddress of the built-in scratch failed (%s); "
+             "the next call tries again",
+             cudaGetErrorString(e));
     return dwa::record_error(DWA_ERR_CUDA, msg);
   }
   // Same validation, kernels and results as dwa_score_topk; only the
   // workspace comes from the built-in array.
   return dwa_score_topk(q, M, ldq, keys, N_local, ldk, d, k, lambda_sharp, tau, T, use_sigmoid,
-                        idx_offset, out_vals, out_idx, s.ptr, kNoAllocScratchBytes, stream);
+                        idx_offset, out_vals, out_idx, scratch, kNoAllocScratchBytes, stream);
 }
 
 }  // extern "C"

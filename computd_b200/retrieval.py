@@ -22,6 +22,7 @@ with one all-reduce.
 from __future__ import annotations
 
 import ctypes
+from typing import NamedTuple
 
 import torch
 import torch.distributed as dist
@@ -29,7 +30,7 @@ import torch.distributed as dist
 from . import _lib
 from .assembly import _check_values, normalise_alpha, weighted_gather_into
 from .pool import ShardSpec
-from .tiled_topk import (_as_bf16_rows, _stream_handle, merge_topk, score_topk_into,
+from .tiled_topk import (_as_bf16_rows, _stream_handle, merge_topk, score_topk_into, seq_scores,
                          tiled_topk_fused, workspace_bytes)
 
 
@@ -550,6 +551,18 @@ class HostPipeline:
             r.close()
 
 
+class HybridParts(NamedTuple):
+    """Outputs and intermediates of one ``pallas_hybrid_forward`` call."""
+    alpha: torch.Tensor           # f32 [B, seq, k]
+    top_idx: torch.Tensor         # i32 [B, seq, k] global pool rows
+    sims_seq: torch.Tensor        # f32 [B, N_local]
+    alpha_raw_seq: torch.Tensor   # f32 [B, N_local]
+    queries_flat: torch.Tensor    # bf16 [B * seq, d_k]: the queries the score kernel saw
+    keys_w: torch.Tensor          # bf16 [N_local, d_k]: the keys the score kernel saw
+    tau: torch.Tensor             # f32 0-d, device: w . tau (0 without the gate)
+    top_vals: torch.Tensor        # f32 [B * seq, k]: fused scores of the global top-k
+
+
 def project_keys(vectors: torch.Tensor, W_K: torch.Tensor, w: torch.Tensor,
                  out: torch.Tensor | None = None) -> torch.Tensor:
     """keys_w [N, d_k] bf16 = sum_s w[s] k_s / (|k_s| + 1e-8), k_s = W_K[s] @ v, for the
@@ -586,8 +599,9 @@ class MultiAspectRetrieval:
     the alpha normalisation (280-326) run on this library's kernels.  ``mesh``
     takes a torch.distributed process group (the reference's ``Mesh``); with
     ``tp_axis`` None or no group the single-chip path is used, as in the
-    reference (314-319).  ``tau`` is read to the host once per call (the C ABI
-    takes it as a scalar).
+    reference (314-319).  The collapsed ``tau = w . tau`` stays on the device:
+    the kernels read it there (``dwa_score_topk_dev``, ``dwa_seq_scores``), as
+    the reference passes it to its kernel as an operand.
     """
 
     def __init__(self, D: int, d_A: int, S: int, d_k: int, N: int, device=None,
@@ -628,14 +642,17 @@ class MultiAspectRetrieval:
             out[r0:r0 + chunk_rows] = acc.to(torch.bfloat16)
         return out
 
-    def pallas_hybrid_forward(self, z: torch.Tensor, vectors: torch.Tensor, k_max: int,
-                              T: float = 1.0, lambda_sharp: float = 1.0, use_sigmoid: bool = True,
-                              tp_axis: str | None = "tp", mesh=None):
-        """Returns (alpha [B, seq, k], top_idx [B, seq, k], sims_seq [B, N_local],
-        alpha_raw_seq [B, N_local]) like retrieval.py:204-343."""
+    def pallas_hybrid_parts(self, z: torch.Tensor, vectors: torch.Tensor, k_max: int,
+                            T: float = 1.0, lambda_sharp: float = 1.0, use_sigmoid: bool = True,
+                            tp_axis: str | None = "tp", mesh=None) -> "HybridParts":
+        """``pallas_hybrid_forward`` with its intermediates: the collapsed bf16
+        queries and pool keys the score kernel saw, the collapsed tau and the
+        global top-k's fused scores (what a parity check recomputes against)."""
         B, seq, d_A = z.shape
         w = torch.softmax(self.aspect_logits.float(), dim=0)                     # 253
-        tau = float(torch.dot(w, self.tau.float())) if use_sigmoid else 0.0    # 254
+        # 254: stays on the device; the kernels read it there (no host sync)
+        tau = (torch.dot(w, self.tau.float()) if use_sigmoid
+               else torch.zeros((), dtype=torch.float32, device=w.device))
         keys_w = self.project_keys(vectors, w)                                  # 241-242, 261
         zf = z.float()
         queries_s = self._normalize(torch.einsum("skd,btd->sbtk", self.W_Q.float(), zf))  # 247-248
@@ -649,9 +666,16 @@ class MultiAspectRetrieval:
         z_mean = zf.mean(dim=1)                                                 # 332-336
         q_mean_s = self._normalize(torch.einsum("skd,bd->sbk", self.W_Q.float(), z_mean))
         q_mean_w = torch.einsum("s,sbk->bk", w, q_mean_s)
-        sims_seq = q_mean_w @ keys_w.float().T
-        if use_sigmoid:                                                         # 338-341
-            alpha_raw_seq = torch.sigmoid(lambda_sharp * (sims_seq - tau)) * torch.exp(sims_seq / T)
-        else:
-            alpha_raw_seq = torch.exp(sims_seq / T)
-        return alpha, top_idx, sims_seq, alpha_raw_seq
+        sims_seq, alpha_raw_seq = seq_scores(q_mean_w, keys_w, lambda_sharp, tau, T,
+                                             use_sigmoid)                       # 336-341
+        return HybridParts(alpha, top_idx, sims_seq, alpha_raw_seq, queries_flat, keys_w, tau,
+                           final_v)
+
+    def pallas_hybrid_forward(self, z: torch.Tensor, vectors: torch.Tensor, k_max: int,
+                              T: float = 1.0, lambda_sharp: float = 1.0, use_sigmoid: bool = True,
+                              tp_axis: str | None = "tp", mesh=None):
+        """Returns (alpha [B, seq, k], top_idx [B, seq, k], sims_seq [B, N_local],
+        alpha_raw_seq [B, N_local]) like retrieval.py:204-343."""
+        p = self.pallas_hybrid_parts(z, vectors, k_max, T, lambda_sharp, use_sigmoid, tp_axis,
+                                     mesh)
+        return p.alpha, p.top_idx, p.sims_seq, p.alpha_raw_seq

@@ -13,8 +13,8 @@ Both run the same sm_100a kernel through the C ABI (``dwa_score_topk``):
 (or ``exp(s / T)``), sorted descending with lower index first among equal
 values, exactly the ``jax.lax.top_k`` contract; ``top_idx`` index the shard's
 rows (plus ``idx_offset``).  ``tile_bt``/``tile_n`` are accepted for
-signature compatibility and ignored: the B200 kernel has a fixed 128 x 256
-tile.  There is no CPU or PyTorch fallback; invalid arguments raise
+signature compatibility and ignored: the B200 kernel has fixed 256 x 256
+tiles (a CTA pair of 128 query rows each against 256 keys).  There is no CPU or PyTorch fallback; invalid arguments raise
 ``DWAArgumentError`` (a ``ValueError``) before anything is launched.
 """
 from __future__ import annotations
@@ -54,6 +54,25 @@ def _scalar(v) -> float:
     return float(v)
 
 
+def score_params(lambda_sharp, tau, T, device) -> torch.Tensor:
+    """Device array {lambda_sharp, tau, T} (f32 [3]) for the entry points that read
+    the runtime scalars on the device (``dwa_score_topk_dev``, ``dwa_seq_scores``,
+    ``dwa_score_backward_dev``).  Tensor arguments stay on the device and Python
+    numbers are written by a fill kernel, so building it never waits for the GPU
+    (the reference's (1,)-operand convention, tiled_topk.py:26-29, 112-115)."""
+    parts = []
+    for v in (lambda_sharp, tau, T):
+        if isinstance(v, torch.Tensor):
+            parts.append(v.detach().to(device=device, dtype=torch.float32).reshape(()))
+        else:
+            parts.append(torch.full((), float(v), dtype=torch.float32, device=device))
+    return torch.stack(parts)
+
+
+def _any_tensor(*xs) -> bool:
+    return any(isinstance(x, torch.Tensor) for x in xs)
+
+
 def workspace_bytes(M: int, N_local: int, d: int, k: int, device=None) -> int:
     """Device workspace ``dwa_score_topk`` needs for this shape on ``device``."""
     lib = _lib.load()
@@ -63,12 +82,25 @@ def workspace_bytes(M: int, N_local: int, d: int, k: int, device=None) -> int:
 
 def score_topk_into(queries: torch.Tensor, keys: torch.Tensor, k_max: int, lambda_sharp, tau, T,
                     use_sigmoid: bool, out_vals: torch.Tensor, out_idx: torch.Tensor,
-                    workspace: torch.Tensor, idx_offset: int = 0) -> None:
-    """Launch ``dwa_score_topk`` into caller-owned outputs and workspace (no allocation)."""
+                    workspace: torch.Tensor, idx_offset: int = 0,
+                    params: torch.Tensor | None = None) -> None:
+    """Launch ``dwa_score_topk`` into caller-owned outputs and workspace (no allocation).
+
+    With ``params`` (device f32 [3] from ``score_params``) the kernels read
+    lambda_sharp, tau and T from it (``dwa_score_topk_dev``) and the scalar
+    arguments are ignored: nothing waits for the host."""
     lib = _lib.load()
     M, d = queries.shape
     N = keys.shape[0]
     with torch.cuda.device(queries.device):
+        if params is not None:
+            st = lib.dwa_score_topk_dev(
+                queries.data_ptr(), M, queries.stride(0), keys.data_ptr(), N, keys.stride(0), d,
+                int(k_max), params.data_ptr(), int(bool(use_sigmoid)), int(idx_offset),
+                out_vals.data_ptr(), out_idx.data_ptr(), workspace.data_ptr(),
+                workspace.numel() * workspace.element_size(), _stream_handle(queries.device))
+            _lib.check(st, "dwa_score_topk_dev")
+            return
         st = lib.dwa_score_topk(
             queries.data_ptr(), M, queries.stride(0), keys.data_ptr(), N, keys.stride(0), d,
             int(k_max), _scalar(lambda_sharp), _scalar(tau), _scalar(T), int(bool(use_sigmoid)),
@@ -85,8 +117,11 @@ def tiled_topk_fused(queries: torch.Tensor, keys: torch.Tensor, k_max: int, lamb
 
     queries: [BT, d_k], keys: [N_local, d_k] on the same CUDA device.
     Returns (top_vals f32 [BT, k_max], top_idx i32 [BT, k_max]).
+    ``lambda_sharp``, ``tau`` and ``T`` may be Python numbers or 0-d/(1,) tensors,
+    as in the reference; when any is a tensor the kernels read all three from
+    the device (no host read of a learned tau).
     """
-    del tile_bt, tile_n  # fixed 128 x 256 tiles on B200
+    del tile_bt, tile_n  # fixed 256 x 256 CTA-pair tiles on B200
     queries = _as_bf16_rows(queries, "queries")
     keys = _as_bf16_rows(keys, "keys")
     if keys.device != queries.device:
@@ -104,9 +139,44 @@ def tiled_topk_fused(queries: torch.Tensor, keys: torch.Tensor, k_max: int, lamb
     if workspace is None:
         nbytes = workspace_bytes(M, N, d, k, dev)
         workspace = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
+    params = (score_params(lambda_sharp, tau, T, dev) if _any_tensor(lambda_sharp, tau, T)
+              else None)
     score_topk_into(queries, keys, k, lambda_sharp, tau, T, use_sigmoid, out_vals, out_idx,
-                    workspace, idx_offset)
+                    workspace, idx_offset, params=params)
     return out_vals, out_idx
+
+
+def seq_scores(q: torch.Tensor, keys: torch.Tensor, lambda_sharp, tau, T, use_sigmoid: bool,
+               sims: torch.Tensor | None = None, fused: torch.Tensor | None = None,
+               status: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Sequence-mean auxiliary scores (reference retrieval.py:332-341) on one key shard:
+    ``sims = q @ keys.T`` (q f32 [B, d], keys bf16 [N, d], fp32 accumulation) and the
+    fused scores ``sigmoid(lambda (sims - tau)) * exp(sims / T)`` (or ``exp(sims / T)``),
+    both f32 [B, N], by the HBM-bound ``dwa_seq_scores`` kernel (keys read once
+    per 8 query rows).  Scalars may be tensors (read on the device)."""
+    keys = _as_bf16_rows(keys, "keys")
+    dev = keys.device
+    q = q.to(device=dev, dtype=torch.float32)
+    if q.dim() != 2 or q.shape[1] != keys.shape[1]:
+        raise ValueError(f"q must be [B, {keys.shape[1]}], got {tuple(q.shape)}")
+    if q.stride(1) != 1:
+        q = q.contiguous()
+    B, d = q.shape
+    N = keys.shape[0]
+    if sims is None:
+        sims = torch.empty((B, N), dtype=torch.float32, device=dev)
+    if fused is None:
+        fused = torch.empty((B, N), dtype=torch.float32, device=dev)
+    params = score_params(lambda_sharp, tau, T, dev)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        st = lib.dwa_seq_scores(q.data_ptr(), B, q.stride(0), keys.data_ptr(), N, keys.stride(0), d,
+                                params.data_ptr(), int(bool(use_sigmoid)), sims.data_ptr(),
+                                sims.stride(0), fused.data_ptr(), fused.stride(0),
+                                status.data_ptr() if status is not None else None,
+                                _stream_handle(dev))
+    _lib.check(st, "dwa_seq_scores")
+    return sims, fused
 
 
 def tiled_topk_fallback(queries: torch.Tensor, keys: torch.Tensor, k_max: int, lambda_sharp, tau, T,

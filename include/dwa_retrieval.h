@@ -50,7 +50,7 @@ enum {
 /* Largest top-k the fused score kernel keeps per query (its per-row heap
  * lives in shared memory: 128 rows x k x 8 bytes). */
 #define DWA_MAX_K 128
-#define DWA_ABI_VERSION 1
+#define DWA_ABI_VERSION 2
 
 DWA_API int32_t dwa_abi_version(void);
 
@@ -106,9 +106,11 @@ DWA_API dwa_status dwa_score_topk(const void* q, int64_t M, int64_t ldq,
  * memory by every GPU this entry point runs on until the process exits.
  * Shapes needing more than that return DWA_ERR_UNSUPPORTED_SHAPE (nothing
  * launched).  The first call on a device looks up the scratch address with
- * that device current; make it before any stream capture.  Every call on a
- * device shares the scratch: calls must be stream-ordered, overlapping calls
- * race.  Allocates nothing.
+ * that device current; make it before any stream capture (a lookup that
+ * fails is retried by the next call).  The scratch used is the current
+ * device's, so `stream` must belong to the current device (otherwise
+ * DWA_ERR_INVALID_ARG).  Every call on a device shares the scratch: calls
+ * must be stream-ordered, overlapping calls race.  Allocates nothing.
  */
 DWA_API dwa_status dwa_score_topk_noalloc(const void* q, int64_t M, int64_t ldq,
                           const void* keys, int64_t N_local, int64_t ldk,
@@ -116,6 +118,45 @@ DWA_API dwa_status dwa_score_topk_noalloc(const void* q, int64_t M, int64_t ldq,
                           float lambda_sharp, float tau, float T, int32_t use_sigmoid,
                           int64_t idx_offset,
                           float* out_vals, int32_t* out_idx, dwa_stream_t stream);
+
+/*
+ * dwa_score_topk with lambda_sharp, tau and T read by the kernels from device
+ * memory: params points at three device floats {lambda_sharp, tau, T}.  The
+ * reference passes these as (1,)-shaped f32 operands so a learned tau never
+ * forces a recompile or a host read (src/kernels/tiled_topk.py:26-29,
+ * 112-115); with this form a caller whose scalars live on the device (an XLA
+ * FFI handler, a training step computing tau = w . tau_s) enqueues the call
+ * without waiting for the host.  Same shapes, workspace and results as
+ * dwa_score_topk.  The checks dwa_score_topk makes on the host scalars
+ * (T > 0, finite lambda_sharp >= 0 and tau with the gate) run on the device:
+ * values that fail them give NaN scores and -1 indices and record
+ * DWA_ERR_DEVICE_CHECK in the workspace status word (dwa_workspace_status).
+ */
+DWA_API dwa_status dwa_score_topk_dev(const void* q, int64_t M, int64_t ldq,
+                          const void* keys, int64_t N_local, int64_t ldk,
+                          int32_t d, int32_t k, const float* params, int32_t use_sigmoid,
+                          int64_t idx_offset, float* out_vals, int32_t* out_idx,
+                          void* ws, size_t ws_bytes, dwa_stream_t stream);
+
+/*
+ * Sequence-mean auxiliary scores of the retrieval (src/model/retrieval.py:
+ * 332-341): for a few query rows q (f32 [B, ldq]; the per-sequence mean
+ * queries q_mean_w) against every key of the shard (bf16 [N, ldk]):
+ *   sims[b, n]  = <q[b, :d], keys[n, :d]>        (f32 x bf16, fp32 accumulate)
+ *   fused[b, n] = sigmoid(lambda_sharp (sims - tau)) * exp(sims / T)   if use_sigmoid
+ *               = exp(sims / T)                                        otherwise
+ * sims f32 [B, lds], fused f32 [B, ldf] (may be NULL; then params may be
+ * NULL too); params: device {lambda_sharp, tau, T}.  HBM-bound: the keys are
+ * read once per 8 query rows.  d % 8 == 0 and d <= 12800, keys 16-byte
+ * aligned, ldk % 8 == 0.  status (device int32, may be NULL) receives
+ * DWA_ERR_DEVICE_CHECK when the params fail the checks of dwa_score_topk_dev
+ * (fused is then NaN).
+ */
+DWA_API dwa_status dwa_seq_scores(const float* q, int64_t B, int64_t ldq,
+                          const void* keys, int64_t N, int64_t ldk, int32_t d,
+                          const float* params, int32_t use_sigmoid,
+                          float* sims, int64_t lds, float* fused, int64_t ldf,
+                          int32_t* status, dwa_stream_t stream);
 
 /*
  * Merge P per-shard candidate lists into the global top-k.
@@ -195,6 +236,14 @@ DWA_API dwa_status dwa_score_backward(const float* vals, const float* scores, co
                           int64_t M, int32_t k,
                           float lambda_sharp, float tau, float T, int32_t use_sigmoid,
                           float* dscores, float* dparams, dwa_stream_t stream);
+
+/* dwa_score_backward with {lambda_sharp, tau, T} read from the device array
+ * params (see dwa_score_topk_dev).  A non-positive or non-finite T, or a
+ * non-finite lambda_sharp / tau with the gate on, gives NaN dscores and
+ * records DWA_ERR_DEVICE_CHECK in *status (device int32, may be NULL). */
+DWA_API dwa_status dwa_score_backward_dev(const float* vals, const float* scores, const float* dalpha,
+                          int64_t M, int32_t k, const float* params, int32_t use_sigmoid,
+                          float* dscores, float* dparams, int32_t* status, dwa_stream_t stream);
 
 /* out[m, :] (= or +=) sum_j w[m, j] rows[gidx[m, j] - row_begin, :] over owned rows. */
 DWA_API dwa_status dwa_gather_rows(const float* weights, const int32_t* gidx, int64_t M, int32_t k,

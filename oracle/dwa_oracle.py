@@ -262,6 +262,32 @@ def compare_topk(got_v, got_i, ref_v, ref_i, q, keys, lambda_sharp=1.0, tau=0.0,
       `ref` within rtol of got's k-th value.
     Returns a list of failure messages (empty = pass).
     """
+    M = np.asarray(got_v).shape[0]
+    rows = np.arange(M) if row_ids is None else np.asarray(row_ids)
+
+    def true_of(r, idx):  # r: row positions in the compared arrays, idx: key indices
+        return true_fused(q, keys, rows[r], idx, lambda_sharp, tau, T, use_sigmoid)
+
+    return _compare_core(got_v, got_i, ref_v, ref_i, true_of, rtol)
+
+
+def compare_topk_from_scores(got_v, got_i, ref_v, ref_i, s, lambda_sharp=1.0, tau=0.0, T=1.0,
+                             use_sigmoid=False, rtol=1e-2) -> list[str]:
+    """``compare_topk`` with the raw scores given: row r of ``s`` (f64 [R, N]) holds
+    q[row] . keys[n] for every key n of the compared rows, so a pool too large to
+    convert to f64 on the host can still be checked on sampled rows."""
+    s = np.asarray(s, np.float64)
+
+    def true_of(r, idx):
+        idx = np.asarray(idx)
+        safe = np.where(idx >= 0, idx, 0)
+        v = fused_score(s[np.broadcast_to(r, safe.shape), safe], lambda_sharp, tau, T, use_sigmoid)
+        return np.where(idx >= 0, v, -np.inf)
+
+    return _compare_core(got_v, got_i, ref_v, ref_i, true_of, rtol)
+
+
+def _compare_core(got_v, got_i, ref_v, ref_i, true_of, rtol) -> list[str]:
     got_v = np.asarray(got_v, np.float64)
     ref_v = np.asarray(ref_v, np.float64)
     got_i = np.asarray(got_i)
@@ -270,7 +296,6 @@ def compare_topk(got_v, got_i, ref_v, ref_i, q, keys, lambda_sharp=1.0, tau=0.0,
     if got_v.shape != ref_v.shape or got_i.shape != ref_i.shape:
         return [f"shape mismatch {got_v.shape} vs {ref_v.shape}"]
     M, k = got_v.shape
-    rows = np.arange(M) if row_ids is None else np.asarray(row_ids)
     scale = np.maximum(np.abs(ref_v), 1e-30)
     bad = np.abs(got_v - ref_v) > rtol * scale
     if bad.any():
@@ -284,7 +309,7 @@ def compare_topk(got_v, got_i, ref_v, ref_i, q, keys, lambda_sharp=1.0, tau=0.0,
         errs.append("duplicate indices in a row")
     if (got_i < 0).any():
         errs.append("negative (sentinel) index returned")
-    tv = true_fused(q, keys, rows[:, None], got_i, lambda_sharp, tau, T, use_sigmoid)
+    tv = true_of(np.arange(M)[:, None], got_i)
     inc = np.abs(tv - got_v) > rtol * np.maximum(np.abs(tv), 1e-30)
     if inc.any():
         r, c = np.argwhere(inc)[0]
@@ -297,10 +322,8 @@ def compare_topk(got_v, got_i, ref_v, ref_i, q, keys, lambda_sharp=1.0, tau=0.0,
             continue
         only_g = np.array(sorted(gs - rs), dtype=np.int64)
         only_r = np.array(sorted(rs - gs), dtype=np.int64)
-        vg = true_fused(q, keys, np.full(only_g.shape, rows[r]), only_g, lambda_sharp, tau, T,
-                        use_sigmoid)
-        vr = true_fused(q, keys, np.full(only_r.shape, rows[r]), only_r, lambda_sharp, tau, T,
-                        use_sigmoid)
+        vg = true_of(np.full(only_g.shape, r), only_g)
+        vr = true_of(np.full(only_r.shape, r), only_r)
         if (vg < ref_v[r, -1] - rtol * abs(ref_v[r, -1])).any() or \
            (vr > got_v[r, -1] + rtol * abs(got_v[r, -1])).any():
             n_extra += 1

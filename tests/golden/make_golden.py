@@ -14,13 +14,15 @@ all_gather, shard_map, ...).  What runs is the reference's own source:
 
 Inputs are float32 arrays holding bf16-representable values (the B200 kernel
 takes bf16, so both sides see identical inputs).  Run from the repository
-root:  ``python tests/golden/make_golden.py [--reference PATH]``.
+root:  ``python tests/golden/make_golden.py --reference PATH`` (or with
+``COMPUTD_REFERENCE=PATH`` in the environment).
 The reference tree is read only; nothing from it is copied into the fixture
 except the computed outputs.
 """
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 import types
 from pathlib import Path
@@ -185,10 +187,13 @@ def case_assembler(ref_asm, ref_pool, rng, out, name, d_A, d_B, r):
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__)
-    ap.add_argument("--reference", default="/root/reference",
-                    help="path of the reference checkout (read only)")
+    ap.add_argument("--reference", default=os.environ.get("COMPUTD_REFERENCE"),
+                    help="path of the reference checkout, read only (default: the "
+                         "COMPUTD_REFERENCE environment variable)")
     ap.add_argument("--out", default=str(HERE / "dwa_golden.npz"))
     args = ap.parse_args(argv)
+    if not args.reference or not os.path.isdir(os.path.join(args.reference, "src")):
+        ap.error("give the reference checkout with --reference PATH or COMPUTD_REFERENCE")
 
     jax_standin.install()
     sys.path.insert(0, args.reference)

@@ -26,7 +26,7 @@ def test_library_exports_every_declared_symbol():
     lib = _lib.load()
     for name in declared_symbols():
         assert hasattr(lib, name), name
-    assert lib.dwa_abi_version() == 1
+    assert lib.dwa_abi_version() == 2
 
 
 def test_only_dwa_symbols_are_exported():
@@ -175,3 +175,32 @@ def test_nvlink_and_projection_entry_points_validate_before_launch():
     assert lib.dwa_assemble_finish(None, 0, 0, None, None, 4, 16, 1.0, None, None, 1e-6, FAKE,
                                    None) == 1
     assert lib.dwa_usage_ema(FAKE, FAKE, -1, 0, 10, 0.01, 0.99, FAKE, None) == 1
+
+
+def test_device_scalar_and_seq_entry_points_validate_before_launch():
+    """dwa_score_topk_dev / dwa_score_backward_dev / dwa_seq_scores: the host
+    checks what it can see (pointers, shapes, alignment) and launches nothing on
+    failure; the scalars themselves are checked on the device."""
+    lib = _lib.load()
+    args = [FAKE, 128, 128, FAKE, 1000, 128, 128, 16]
+    tail = [0, 0, FAKE, FAKE, FAKE, 0, None]
+    # null params, misaligned params, and the shape checks dwa_score_topk makes
+    assert lib.dwa_score_topk_dev(*args, None, *tail) == 1
+    assert lib.dwa_score_topk_dev(*args, FAKE + 2, *tail) == 1
+    assert lib.dwa_score_topk_dev(FAKE, 128, 128, FAKE, 1000, 128, 128, 129, FAKE, *tail) == 2
+    assert lib.dwa_score_topk_dev(*args, FAKE, 0, 0, FAKE, FAKE, None, 0, None) == 6  # workspace
+    assert lib.dwa_score_topk_dev(FAKE, 0, 128, FAKE, 1000, 128, 128, 16, None, *tail) == 0
+    assert lib.dwa_score_backward_dev(FAKE, FAKE, FAKE, 8, 4, None, 1, FAKE, None, None, None) == 1
+    assert lib.dwa_score_backward_dev(FAKE, FAKE, FAKE, 8, 0, FAKE, 1, FAKE, None, None, None) == 1
+    # seq scores: d range, strides, fused without params, key alignment
+    seq = lambda **kw: lib.dwa_seq_scores(*[kw.get(n, v) for n, v in [
+        ("q", FAKE), ("B", 4), ("ldq", 128), ("keys", FAKE), ("N", 1000), ("ldk", 128),
+        ("d", 128), ("params", FAKE), ("sig", 1), ("sims", FAKE), ("lds", 1000),
+        ("fused", FAKE), ("ldf", 1000), ("status", None), ("stream", None)]])
+    assert seq(d=100, ldq=128, ldk=128) == 2
+    assert seq(d=12808, ldq=12808, ldk=12808) == 2
+    assert seq(lds=999) == 1
+    assert seq(params=None) == 1
+    assert seq(keys=FAKE + 8) == 2
+    assert seq(sims=None) == 1
+    assert seq(B=0) == 0 and seq(N=0) == 0

@@ -137,6 +137,23 @@ def test_comparator_catches_planted_mistakes(golden):
     assert O.compare_topk(v, i4, v, i, q, keys, lam, tau, T, sig)
 
 
+def test_score_lookup_comparator_agrees_with_recomputing_one(golden):
+    """compare_topk_from_scores (precomputed f64 scores, for pools too large to
+    recompute on the host) gives the same verdicts as compare_topk."""
+    q, keys, k, lam, tau, T, sig = _case(golden, "c1_gate")
+    v, i = O.tiled_topk(q, keys, k, lam, tau, T, sig)
+    s = O.scores(q, keys)
+    assert O.compare_topk_from_scores(v, i, v, i, s, lam, tau, T, sig) == []
+    i2 = i.copy()
+    i2[0, 3] = int(np.argmin(s[0]))
+    v2 = v.copy()
+    v2[5, 0] *= 1.05
+    for gv, gi in ((v, i2), (v2, i)):
+        a = O.compare_topk(gv, gi, v, i, q, keys, lam, tau, T, sig)
+        b = O.compare_topk_from_scores(gv, gi, v, i, s, lam, tau, T, sig)
+        assert a and b and len(a) == len(b)
+
+
 def test_compare_rows():
     rng = np.random.default_rng(0)
     ref = rng.standard_normal((8, 16))

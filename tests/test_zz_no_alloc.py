@@ -70,3 +70,18 @@ def test_noalloc_rejects_shapes_beyond_its_scratch():
                                     None)
     assert st == _lib.DWA_ERR_UNSUPPORTED_SHAPE
     assert b"built-in" in lib.dwa_last_error()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_noalloc_refuses_a_stream_of_another_device():
+    """The scratch used is the current device's: a stream of another GPU is
+    refused before anything is launched."""
+    lib = _lib.load()
+    torch.cuda.set_device(0)
+    other = torch.cuda.Stream(device=torch.device("cuda", 1))
+    FAKE = 0x10000  # never dereferenced: the call is refused before any launch
+    st = lib.dwa_score_topk_noalloc(FAKE, 256, 128, FAKE, 4096, 128, 128, 16, 1.0, 0.0, 1.0, 0, 0,
+                                    FAKE, FAKE, other.cuda_stream)
+    assert st == _lib.DWA_ERR_INVALID_ARG
+    assert b"belongs to device 1" in lib.dwa_last_error()
