@@ -11,10 +11,10 @@ from ._lib import DWA_MAX_K, DWAArgumentError, DWAError, load as load_library
 from .assembler import WeightAssembler, assemble_finish, lowrank_delta, usage_ema_update
 from .assembly import normalise_alpha, weighted_gather_into, weighted_value_sum
 from .pool import ShardSpec, init_normal, new_normal
-from .retrieval import (HostPipeline, MultiAspectRetrieval, PeerExchange, Retriever, chip_topk,
-                        project_keys,
-                        exchange_candidates, reduce_partials)
-from .tiled_topk import (merge_topk, score_params, score_topk_into, seq_scores,
+from .retrieval import (HostPipeline, HybridParts, MultiAspectRetrieval, PeerExchange, Retriever,
+                        chip_topk, exchange_candidates, project_keys, project_keys_packed,
+                        reduce_partials)
+from .tiled_topk import (merge_topk, score_params, score_topk_into, score_topk_seqmean, seq_scores,
                          tiled_topk_fallback, tiled_topk_fused, workspace_bytes)
 
 __all__ = [
@@ -22,7 +22,8 @@ __all__ = [
     "WeightAssembler", "assemble_finish", "lowrank_delta", "usage_ema_update",
     "normalise_alpha", "weighted_gather_into", "weighted_value_sum", "MultiAspectRetrieval",
     "ShardSpec", "init_normal", "new_normal",
-    "HostPipeline", "PeerExchange", "Retriever", "chip_topk", "project_keys", "exchange_candidates", "reduce_partials",
-    "merge_topk", "score_params", "score_topk_into", "seq_scores", "tiled_topk_fallback",
-    "tiled_topk_fused", "workspace_bytes",
+    "HostPipeline", "HybridParts", "PeerExchange", "Retriever", "chip_topk", "project_keys",
+    "project_keys_packed", "exchange_candidates", "reduce_partials",
+    "merge_topk", "score_params", "score_topk_into", "score_topk_seqmean", "seq_scores",
+    "tiled_topk_fallback", "tiled_topk_fused", "workspace_bytes",
 ]

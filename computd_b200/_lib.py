@@ -41,6 +41,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dwa_score_topk_dev": (_i32, [_c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _i32, _i32,
                                   _c_void_p, _i32, _i64, _c_void_p, _c_void_p, _c_void_p,
                                   ctypes.c_size_t, _c_void_p]),
+    "dwa_score_topk_seqmean": (_i32, [_c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _i32, _i32,
+                                      _c_void_p, _i32, _i64, _i64, _c_void_p, _i64, _c_void_p,
+                                      _c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p]),
+    "dwa_project_keys_packed": (_i32, [_c_void_p, _i64, _i64, _i32, _c_void_p, _i64, _i32, _i32,
+                                       _c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p]),
     "dwa_seq_scores": (_i32, [_c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _i32, _c_void_p,
                               _i32, _c_void_p, _i64, _c_void_p, _i64, _c_void_p, _c_void_p]),
     "dwa_score_backward_dev": (_i32, [_c_void_p, _c_void_p, _c_void_p, _i64, _i32, _c_void_p,
@@ -65,9 +70,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                          _i64, _i32, ctypes.POINTER(_c_void_p), _i32, _i32, _i64,
                                          _c_void_p, _c_void_p]),
     "dwa_reduce_broadcast_peers": (_i32, [_c_void_p, _i32, _i32, _i64, _i64, _i32,
-                                          ctypes.POINTER(_c_void_p), _c_void_p, _i32, _c_void_p,
-                                          _c_void_p]),
-    "dwa_peer_wait": (_i32, [_c_void_p, _i32, _i32, _c_void_p, _c_void_p]),
+                                          ctypes.POINTER(_c_void_p), _c_void_p, _i32, _i64,
+                                          _c_void_p, _c_void_p]),
+    "dwa_peer_wait": (_i32, [_c_void_p, _i32, _i32, _i64, _c_void_p, _c_void_p]),
     "dwa_project_keys": (_i32, [_c_void_p, _i64, _i64, _i32, _c_void_p, _i64, _i32, _i32, _c_void_p,
                                 _c_void_p, _i64, _c_void_p, _c_void_p]),
     "dwa_peer_alloc": (_i32, [ctypes.c_size_t, ctypes.POINTER(_c_void_p), _c_void_p]),
@@ -76,7 +81,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dwa_peer_free": (_i32, [_c_void_p]),
     "dwa_peer_signal": (_i32, [ctypes.POINTER(_c_void_p), _i32, _i32, _i32, _c_void_p]),
     "dwa_merge_topk_peers": (_i32, [ctypes.POINTER(_c_void_p), _i32, _i64, _i32, _c_void_p, _i32,
-                                    _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
+                                    _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
     "dwa_lowrank_delta": (_i32, [_c_void_p, _i32, _i64, _c_void_p, _c_void_p, _i64, _i32, _c_void_p,
                                  _i64, _i64, _i64, _i32, _i32, _i32, _c_void_p, _c_void_p]),
     "dwa_assemble_finish": (_i32, [_c_void_p, _i32, _i64, _c_void_p, _c_void_p, _i64, _i32, _f32,

@@ -6,6 +6,7 @@
 // the same conditions (e.g. lax.top_k with k > N); here they are status codes.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -36,6 +37,11 @@ dwa_status cuda_fail(cudaError_t e, const char* where, const char* detail = null
 }
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+uint64_t peer_wait_ns(int64_t wait_ns) {
+  if (wait_ns <= 0) return dwa::kPeerWaitDefaultNs;
+  return std::min<uint64_t>(static_cast<uint64_t>(wait_ns), dwa::kPeerWaitMaxNs);
+}
 
 dwa_status ok() {
   g_last_error.clear();
@@ -88,7 +94,8 @@ dwa_status score_topk_impl(const char* fn, const void* q, int64_t M, int64_t ldq
                            const void* keys, int64_t N_local, int64_t ldk, int32_t d, int32_t k,
                            float lambda_sharp, float tau, float T, const float* params,
                            int32_t use_sigmoid, int64_t idx_offset, float* out_vals,
-                           int32_t* out_idx, void* ws, size_t ws_bytes, dwa_stream_t stream) {
+                           int32_t* out_idx, void* ws, size_t ws_bytes, dwa_stream_t stream,
+                           const dwa::SeqMeanOut* seq_mean = nullptr) {
   if (M < 0 || N_local < 0) return fail(DWA_ERR_INVALID_ARG, "%s: negative size (M=%lld, N=%lld)",
                                         fn, (long long)M, (long long)N_local);
   if (M == 0) return ok();
@@ -136,8 +143,37 @@ dwa_status score_topk_impl(const char* fn, const void* q, int64_t M, int64_t ldq
   const char* detail = nullptr;
   cudaError_t e = dwa::launch_score_topk(plan, q, ldq, keys, ldk, lambda_sharp, tau, T,
                                          use_sigmoid ? 1 : 0, idx_offset, out_vals, out_idx, ws,
-                                         static_cast<cudaStream_t>(stream), &detail, params);
+                                         static_cast<cudaStream_t>(stream), &detail, params,
+                                         seq_mean);
   if (e != cudaSuccess) return cuda_fail(e, fn, detail);
+  return ok();
+}
+
+dwa_status project_keys_impl(const char* fn, const void* vectors, int64_t N, int64_t ldv, int32_t D,
+                             const void* w_k, int64_t ldw, int32_t S, int32_t d_k,
+                             const float* aspect_w, void* keys_out, int64_t ldo, int32_t* status,
+                             dwa_stream_t stream, bool packed) {
+  if (N < 0) return fail(DWA_ERR_INVALID_ARG, "%s: negative N", fn);
+  if (N == 0) return ok();
+  if (!vectors || !w_k || !aspect_w || !keys_out)
+    return fail(DWA_ERR_INVALID_ARG, "%s: null argument", fn);
+  if (d_k != 32 && d_k != 64 && d_k != 128)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "%s: d_k=%d must be 32, 64 or 128", fn, d_k);
+  if (S < 1 || static_cast<int64_t>(S) * d_k > (1 << 20))
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "%s: S=%d outside [1, 2^20 / d_k]", fn, S);
+  if (D < 8 || D % 8 != 0)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "%s: D=%d must be a positive multiple of 8", fn, D);
+  if (N > INT32_MAX - 256) return fail(DWA_ERR_UNSUPPORTED_SHAPE, "%s: N too large", fn);
+  const int64_t out_cols = packed ? static_cast<int64_t>(S) * d_k : d_k;
+  if (ldv < D || ldw < D || ldo < out_cols)
+    return fail(DWA_ERR_INVALID_ARG, "%s: a row stride is below its row length", fn);
+  if (ldv % 8 || ldw % 8 || ldo % 8 || !aligned(vectors, 16) || !aligned(w_k, 16) ||
+      !aligned(keys_out, 16))
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE,
+                "%s: 16-byte aligned bases and strides (multiples of 8) required", fn);
+  cudaError_t e = dwa::launch_project_keys(vectors, N, ldv, D, w_k, ldw, S, d_k, aspect_w, keys_out,
+                                           ldo, status, static_cast<cudaStream_t>(stream), packed);
+  if (e != cudaSuccess) return cuda_fail(e, fn);
   return ok();
 }
 }  // namespace
@@ -162,6 +198,29 @@ dwa_status dwa_score_topk_dev(const void* q, int64_t M, int64_t ldq, const void*
   if (M > 0 && !params) return fail(DWA_ERR_INVALID_ARG, "dwa_score_topk_dev: null params");
   return score_topk_impl("dwa_score_topk_dev", q, M, ldq, keys, N_local, ldk, d, k, 0.f, 0.f, 1.f,
                          params, use_sigmoid, idx_offset, out_vals, out_idx, ws, ws_bytes, stream);
+}
+
+dwa_status dwa_score_topk_seqmean(const void* q, int64_t M, int64_t ldq, const void* keys,
+                                  int64_t N_local, int64_t ldk, int32_t d, int32_t k,
+                                  const float* params, int32_t use_sigmoid, int64_t idx_offset,
+                                  int64_t seq, float* fused_mean, int64_t ld_mean, float* out_vals,
+                                  int32_t* out_idx, void* ws, size_t ws_bytes,
+                                  dwa_stream_t stream) {
+  if (M > 0) {
+    if (!params) return fail(DWA_ERR_INVALID_ARG, "dwa_score_topk_seqmean: null params");
+    if (!fused_mean) return fail(DWA_ERR_INVALID_ARG, "dwa_score_topk_seqmean: null fused_mean");
+    if (seq < 1 || M % seq != 0)
+      return fail(DWA_ERR_INVALID_ARG, "dwa_score_topk_seqmean: seq=%lld must divide M=%lld",
+                  (long long)seq, (long long)M);
+    if (ld_mean < N_local)
+      return fail(DWA_ERR_INVALID_ARG, "dwa_score_topk_seqmean: ld_mean below N_local");
+    if (!aligned(fused_mean, 4))
+      return fail(DWA_ERR_INVALID_ARG, "dwa_score_topk_seqmean: fused_mean must be 4-byte aligned");
+  }
+  dwa::SeqMeanOut sm{fused_mean, ld_mean, seq < 1 ? 1 : seq};
+  return score_topk_impl("dwa_score_topk_seqmean", q, M, ldq, keys, N_local, ldk, d, k, 0.f, 0.f,
+                         1.f, params, use_sigmoid, idx_offset, out_vals, out_idx, ws, ws_bytes,
+                         stream, &sm);
 }
 
 dwa_status dwa_seq_scores(const float* q, int64_t B, int64_t ldq, const void* keys, int64_t N,
@@ -438,7 +497,8 @@ dwa_status dwa_weighted_gather_peers(const float* vals, const int32_t* gidx, int
 
 dwa_status dwa_reduce_broadcast_peers(const float* inbox, int32_t P, int32_t rank, int64_t block_rows,
                                       int64_t M, int32_t d, void* const* outs, const int32_t* flags,
-                                      int32_t step, int32_t* status, dwa_stream_t stream) {
+                                      int32_t step, int64_t wait_ns, int32_t* status,
+                                      dwa_stream_t stream) {
   if (!inbox || !outs || !flags || !status)
     return fail(DWA_ERR_INVALID_ARG, "dwa_reduce_broadcast_peers: null argument");
   if (P < 1 || P > DWA_MAX_PEERS || rank < 0 || rank >= P)
@@ -454,16 +514,18 @@ dwa_status dwa_reduce_broadcast_peers(const float* inbox, int32_t P, int32_t ran
     o[p] = static_cast<float*>(outs[p]);
   }
   cudaError_t e = dwa::launch_reduce_broadcast_peers(inbox, P, rank, block_rows, M, d, o, flags, step,
-                                                     status, static_cast<cudaStream_t>(stream));
+                                                     peer_wait_ns(wait_ns), status,
+                                                     static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "dwa_reduce_broadcast_peers launch");
   return ok();
 }
 
-dwa_status dwa_peer_wait(const int32_t* flags, int32_t P, int32_t step, int32_t* status,
-                         dwa_stream_t stream) {
+dwa_status dwa_peer_wait(const int32_t* flags, int32_t P, int32_t step, int64_t wait_ns,
+                         int32_t* status, dwa_stream_t stream) {
   if (!flags || !status) return fail(DWA_ERR_INVALID_ARG, "dwa_peer_wait: null argument");
   if (P < 1 || P > DWA_MAX_PEERS) return fail(DWA_ERR_INVALID_ARG, "dwa_peer_wait: P=%d", P);
-  cudaError_t e = dwa::launch_peer_wait(flags, P, step, status, static_cast<cudaStream_t>(stream));
+  cudaError_t e = dwa::launch_peer_wait(flags, P, step, peer_wait_ns(wait_ns), status,
+                                        static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "dwa_peer_wait launch");
   return ok();
 }
@@ -471,27 +533,16 @@ dwa_status dwa_peer_wait(const int32_t* flags, int32_t P, int32_t step, int32_t*
 dwa_status dwa_project_keys(const void* vectors, int64_t N, int64_t ldv, int32_t D, const void* w_k,
                             int64_t ldw, int32_t S, int32_t d_k, const float* aspect_w,
                             void* keys_out, int64_t ldo, int32_t* status, dwa_stream_t stream) {
-  if (N < 0) return fail(DWA_ERR_INVALID_ARG, "dwa_project_keys: negative N");
-  if (N == 0) return ok();
-  if (!vectors || !w_k || !aspect_w || !keys_out)
-    return fail(DWA_ERR_INVALID_ARG, "dwa_project_keys: null argument");
-  if (d_k != 32 && d_k != 64 && d_k != 128)
-    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_project_keys: d_k=%d must be 32, 64 or 128", d_k);
-  if (S < 1 || static_cast<int64_t>(S) * d_k > (1 << 20))
-    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_project_keys: S=%d outside [1, 2^20 / d_k]", S);
-  if (D < 8 || D % 8 != 0)
-    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_project_keys: D=%d must be a positive multiple of 8", D);
-  if (N > INT32_MAX - 256) return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_project_keys: N too large");
-  if (ldv < D || ldw < D || ldo < d_k)
-    return fail(DWA_ERR_INVALID_ARG, "dwa_project_keys: a row stride is below its row length");
-  if (ldv % 8 || ldw % 8 || ldo % 8 || !aligned(vectors, 16) || !aligned(w_k, 16) ||
-      !aligned(keys_out, 16))
-    return fail(DWA_ERR_UNSUPPORTED_SHAPE,
-                "dwa_project_keys: 16-byte aligned bases and strides (multiples of 8) required");
-  cudaError_t e = dwa::launch_project_keys(vectors, N, ldv, D, w_k, ldw, S, d_k, aspect_w, keys_out,
-                                           ldo, status, static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return cuda_fail(e, "dwa_project_keys launch");
-  return ok();
+  return project_keys_impl("dwa_project_keys", vectors, N, ldv, D, w_k, ldw, S, d_k, aspect_w,
+                           keys_out, ldo, status, stream, false);
+}
+
+dwa_status dwa_project_keys_packed(const void* vectors, int64_t N, int64_t ldv, int32_t D,
+                                   const void* w_k, int64_t ldw, int32_t S, int32_t d_k,
+                                   const float* aspect_w, void* keys_out, int64_t ldo,
+                                   int32_t* status, dwa_stream_t stream) {
+  return project_keys_impl("dwa_project_keys_packed", vectors, N, ldv, D, w_k, ldw, S, d_k,
+                           aspect_w, keys_out, ldo, status, stream, true);
 }
 
 dwa_status dwa_peer_alloc(size_t bytes, void** out_ptr, void* out_handle) {
@@ -552,8 +603,9 @@ dwa_status dwa_peer_signal(void* const* flag_bases, int32_t P, int32_t my_rank, 
 }
 
 dwa_status dwa_merge_topk_peers(const void* const* packed, int32_t P, int64_t M, int32_t k,
-                                const int32_t* flags, int32_t step, float* out_vals,
-                                int32_t* out_idx, int32_t* status, dwa_stream_t stream) {
+                                const int32_t* flags, int32_t step, int64_t wait_ns,
+                                float* out_vals, int32_t* out_idx, int32_t* status,
+                                dwa_stream_t stream) {
   if (M < 0) return fail(DWA_ERR_INVALID_ARG, "dwa_merge_topk_peers: negative M");
   if (M == 0) return ok();
   if (!packed || !flags || !out_vals || !out_idx || !status)
@@ -569,8 +621,9 @@ dwa_status dwa_merge_topk_peers(const void* const* packed, int32_t P, int64_t M,
       return fail(DWA_ERR_INVALID_ARG, "dwa_merge_topk_peers: bad list pointer of rank %d", p);
     lists[p] = static_cast<const int32_t*>(packed[p]);
   }
-  cudaError_t e = dwa::launch_merge_topk_peers(lists, P, M, k, flags, step, out_vals, out_idx,
-                                               status, static_cast<cudaStream_t>(stream));
+  cudaError_t e = dwa::launch_merge_topk_peers(lists, P, M, k, flags, step, peer_wait_ns(wait_ns),
+                                               out_vals, out_idx, status,
+                                               static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "dwa_merge_topk_peers launch");
   return ok();
 }

@@ -44,13 +44,22 @@ bool plan_score_topk(int64_t M, int64_t N, int d, int k, int num_sms, ScoreTopkP
 // Number of SMs of the current device (cached per device).
 int device_sm_count();
 
+// Optional output of the fused kernel: out[g * ld + n] = mean over the rows m
+// of group g (rows [g * group_rows, (g + 1) * group_rows)) of v(s[m, n]).
+struct SeqMeanOut {
+  float* out;
+  int64_t ld;
+  int64_t group_rows;  // divides M
+};
+
 // Launches the fused kernel + split merge.  Arguments were validated by the caller.
 // `params` (device {lambda, tau, T}, may be null) overrides the host scalars.
 cudaError_t launch_score_topk(const ScoreTopkPlan& plan, const void* q, int64_t ldq,
                               const void* keys, int64_t ldk, float lambda_sharp, float tau,
                               float T, int use_sigmoid, int64_t idx_offset, float* out_vals,
                               int32_t* out_idx, void* ws, cudaStream_t stream,
-                              const char** err_detail, const float* params = nullptr);
+                              const char** err_detail, const float* params = nullptr,
+                              const SeqMeanOut* seq_mean = nullptr);
 
 // Generic candidate merge.  Candidate (list l, position p, row r) lives at
 // offset l*stride_list + p*stride_pos + r*stride_row.  When `transform` is
@@ -107,21 +116,30 @@ cudaError_t launch_weighted_gather_peers(const float* vals, const int32_t* gidx,
                                          int64_t block_rows, float* alpha_out, cudaStream_t stream);
 cudaError_t launch_reduce_broadcast_peers(const float* inbox, int P, int rank, int64_t block_rows,
                                           int64_t M, int d, float* const* outs, const int32_t* flags,
-                                          int step, int* status, cudaStream_t stream);
-cudaError_t launch_peer_wait(const int32_t* flags, int P, int step, int* status, cudaStream_t stream);
+                                          int step, uint64_t wait_ns, int* status,
+                                          cudaStream_t stream);
+cudaError_t launch_peer_wait(const int32_t* flags, int P, int step, uint64_t wait_ns, int* status,
+                             cudaStream_t stream);
+
+// Limits of the waits for other ranks' flags (the peer merge, reduce and wait):
+// a caller's wait_ns <= 0 takes the default; larger values are capped.
+constexpr uint64_t kPeerWaitDefaultNs = 30ull * 1000000000ull;
+constexpr uint64_t kPeerWaitMaxNs = 600ull * 1000000000ull;
 
 // key_projection.cu
+// packed = false: the collapsed keys [N, d_k]; true: [sqrt(w_s) k_s / (|k_s| + 1e-8)]_s [N, S d_k].
 cudaError_t launch_project_keys(const void* vectors, int64_t N, int64_t ldv, int D, const void* w_k,
                                 int64_t ldw, int S, int d_k, const float* aspect_w, void* keys_out,
-                                int64_t ldo, int* status, cudaStream_t stream);
+                                int64_t ldo, int* status, cudaStream_t stream, bool packed = false);
 
 // merge_topk.cu: NVLink peer exchange
 int max_peers();
 cudaError_t launch_peer_signal(int32_t* const* flag_bases, int n, int my_rank, int value,
                                cudaStream_t stream);
 cudaError_t launch_merge_topk_peers(const int32_t* const* packed, int n, int64_t M, int k,
-                                    const int32_t* flags, int step, float* out_vals,
-                                    int32_t* out_idx, int* status, cudaStream_t stream);
+                                    const int32_t* flags, int step, uint64_t wait_ns,
+                                    float* out_vals, int32_t* out_idx, int* status,
+                                    cudaStream_t stream);
 
 // assembly.cu
 size_t lowrank_delta_smem_bytes(int d_A, int k, int r);

@@ -56,7 +56,14 @@ struct KeyProjArgs {
   int* status;  // may be null
 };
 
-template <int DK>
+// PACK = false: keys_w[n] = sum_s w_s k_s / (|k_s| + 1e-8)  (the collapse of
+//               pallas_hybrid_forward, retrieval.py:261), out [N, DK].
+// PACK = true:  out[n, s DK : (s + 1) DK] = sqrt(w_s) k_s / (|k_s| + 1e-8), the
+//               per-aspect keys side by side, out [N, S DK].  Then
+//               <[sqrt(w_s) q_s]_s, [sqrt(w_s) k_s]_s> = sum_s w_s <q_s, k_s>,
+//               the score of hybrid_forward (retrieval.py:154-165), is one dot
+//               product of length S DK.
+template <int DK, bool PACK>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kKpThreads, 1)
     key_project_kernel(const __grid_constant__ CUtensorMap tmap_v,
                        const __grid_constant__ CUtensorMap tmap_w, const KeyProjArgs a) {
@@ -174,9 +181,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kKpThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int ew = warp & 3;          // TMEM lane quarter
     const int row = ew * 32 + lane;   // pool row within this CTA's 128
-    float acc_out[DK];
+    float acc_out[PACK ? 1 : DK];
 #pragma unroll
-    for (int c = 0; c < DK; ++c) acc_out[c] = 0.f;
+    for (int c = 0; c < (PACK ? 1 : DK); ++c) acc_out[c] = 0.f;
+    const int64_t grow = static_cast<int64_t>(row0) + row;
     const uint32_t lead_tempty0 = map_to_cta(tempty_bar(0), 0);
     const uint32_t lead_tempty1 = map_to_cta(tempty_bar(1), 0);
     bool ok = true;
@@ -204,14 +212,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kKpThreads, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) ss = fmaf(v[j], v[j], ss);
           }
-          const float scale = __ldg(a.w + s_idx) / (sqrtf(ss) + 1e-8f);
-          // pass 2: w_s * segment / (norm + 1e-8) into the collapsed key
+          if constexpr (PACK) {
+            // pass 2: sqrt(w_s) * segment / (norm + 1e-8), stored as segment s of the row
+            const float scale = sqrtf(__ldg(a.w + s_idx)) / (sqrtf(ss) + 1e-8f);
 #pragma unroll
-          for (int c = 0; c < DK / 32; ++c) {
-            float v[32];
-            tmem_ld_32x32b_x32_sync(taddr + sg * DK + 32 * c, v);
+            for (int c = 0; c < DK / 32; ++c) {
+              float v[32];
+              tmem_ld_32x32b_x32_sync(taddr + sg * DK + 32 * c, v);
+              if (grow < a.N) {
+                uint4* dst = reinterpret_cast<uint4*>(a.out + grow * a.ldo +
+                                                      static_cast<int64_t>(s_idx) * DK + 32 * c);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) acc_out[32 * c + j] = fmaf(scale, v[j], acc_out[32 * c + j]);
+                for (int q8 = 0; q8 < 4; ++q8) {
+                  uint4 wv;
+                  uint32_t* wp = reinterpret_cast<uint32_t*>(&wv);
+#pragma unroll
+                  for (int q = 0; q < 4; ++q) {
+                    const __nv_bfloat162 h2 = __floats2bfloat162_rn(
+                        scale * v[8 * q8 + 2 * q], scale * v[8 * q8 + 2 * q + 1]);
+                    wp[q] = *reinterpret_cast<const uint32_t*>(&h2);
+                  }
+                  dst[q8] = wv;
+                }
+              }
+            }
+          } else {
+            const float scale = __ldg(a.w + s_idx) / (sqrtf(ss) + 1e-8f);
+            // pass 2: w_s * segment / (norm + 1e-8) into the collapsed key
+#pragma unroll
+            for (int c = 0; c < DK / 32; ++c) {
+              float v[32];
+              tmem_ld_32x32b_x32_sync(taddr + sg * DK + 32 * c, v);
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                acc_out[32 * c + j] = fmaf(scale, v[j], acc_out[32 * c + j]);
+            }
           }
         }
       }
@@ -219,8 +254,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kKpThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? lead_tempty1 : lead_tempty0);
     }
-    const int64_t grow = static_cast<int64_t>(row0) + row;
-    if (ok && grow < a.N) {
+    if (!PACK && ok && grow < a.N) {
       uint4* dst = reinterpret_cast<uint4*>(a.out + grow * a.ldo);
 #pragma unroll
       for (int c = 0; c < DK / 8; ++c) {
@@ -250,7 +284,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kKpThreads, 1)
   }
 }
 
-template <int DK>
+template <int DK, bool PACK>
 cudaError_t launch_dk(const CUtensorMap& mv, const CUtensorMap& mw, const KeyProjArgs& args,
                       unsigned grid, cudaStream_t stream) {
   static std::atomic<uint64_t> done{0};
@@ -259,12 +293,12 @@ cudaError_t launch_dk(const CUtensorMap& mv, const CUtensorMap& mw, const KeyPro
   if (e != cudaSuccess) return e;
   const uint64_t bit = 1ull << (dev & 63);
   if (!(done.load(std::memory_order_acquire) & bit)) {
-    e = cudaFuncSetAttribute(key_project_kernel<DK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kKpSmemBytes);
+    e = cudaFuncSetAttribute(key_project_kernel<DK, PACK>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kKpSmemBytes);
     if (e != cudaSuccess) return e;
     done.fetch_or(bit, std::memory_order_acq_rel);
   }
-  key_project_kernel<DK><<<grid, kKpThreads, kKpSmemBytes, stream>>>(mv, mw, args);
+  key_project_kernel<DK, PACK><<<grid, kKpThreads, kKpSmemBytes, stream>>>(mv, mw, args);
   return cudaGetLastError();
 }
 
@@ -272,7 +306,7 @@ cudaError_t launch_dk(const CUtensorMap& mv, const CUtensorMap& mw, const KeyPro
 
 cudaError_t launch_project_keys(const void* vectors, int64_t N, int64_t ldv, int D, const void* w_k,
                                 int64_t ldw, int S, int d_k, const float* aspect_w, void* keys_out,
-                                int64_t ldo, int* status, cudaStream_t stream) {
+                                int64_t ldo, int* status, cudaStream_t stream, bool packed) {
   if (N <= 0) return cudaSuccess;
   CUtensorMap mv, mw;
   const uint64_t wrows = static_cast<uint64_t>(S) * d_k;
@@ -291,10 +325,13 @@ cudaError_t launch_project_keys(const void* vectors, int64_t N, int64_t ldv, int
   args.ldo = ldo;
   args.status = status;
   const unsigned grid = 2u * static_cast<unsigned>((N + kKpPairRows - 1) / kKpPairRows);
-  switch (d_k) {
-    case 32: return launch_dk<32>(mv, mw, args, grid, stream);
-    case 64: return launch_dk<64>(mv, mw, args, grid, stream);
-    case 128: return launch_dk<128>(mv, mw, args, grid, stream);
+  switch (d_k * 2 + (packed ? 1 : 0)) {
+    case 64: return launch_dk<32, false>(mv, mw, args, grid, stream);
+    case 128: return launch_dk<64, false>(mv, mw, args, grid, stream);
+    case 256: return launch_dk<128, false>(mv, mw, args, grid, stream);
+    case 65: return launch_dk<32, true>(mv, mw, args, grid, stream);
+    case 129: return launch_dk<64, true>(mv, mw, args, grid, stream);
+    case 257: return launch_dk<128, true>(mv, mw, args, grid, stream);
     default: return cudaErrorInvalidValue;
   }
 }

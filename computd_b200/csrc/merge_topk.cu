@@ -43,6 +43,7 @@ struct MergeArgs {
   const int32_t* peer[kMaxPeers];
   const int32_t* flags;  // this GPU's flag words, one per peer: >= wait_step when ready
   int wait_step;
+  uint64_t wait_ns;      // limit of the wait for the peers' flags
   int* status;
   int64_t stride_list, stride_pos, stride_row;
   int64_t M;
@@ -130,7 +131,7 @@ __global__ void __launch_bounds__(kWarps * 32) merge_sorted_kernel(const MergeAr
     if (lane < a.n_lists) {
       const uint64_t t0 = globaltimer_ns();
       while (ld_acquire_sys(a.flags + lane) < a.wait_step) {
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (globaltimer_ns() - t0 > a.wait_ns) {
           ready = false;
           break;
         }
@@ -340,14 +341,16 @@ cudaError_t launch_peer_signal(int32_t* const* flag_bases, int n, int my_rank, i
 }
 
 cudaError_t launch_merge_topk_peers(const int32_t* const* packed, int n, int64_t M, int k,
-                                    const int32_t* flags, int step, float* out_vals,
-                                    int32_t* out_idx, int* status, cudaStream_t stream) {
+                                    const int32_t* flags, int step, uint64_t wait_ns,
+                                    float* out_vals, int32_t* out_idx, int* status,
+                                    cudaStream_t stream) {
   if (M <= 0) return cudaSuccess;
   if (n < 1 || n > kMaxPeers || k < 1 || k > DWA_MERGE_MAX_K) return cudaErrorInvalidValue;
   MergeArgs a{};
   for (int p = 0; p < n; ++p) a.peer[p] = packed[p];
   a.flags = flags;
   a.wait_step = step;
+  a.wait_ns = wait_ns;
   a.status = status;
   a.stride_list = 0;
   a.stride_pos = 2;

@@ -45,6 +45,7 @@
 #include <mutex>
 
 #include "dwa_internal.h"
+#include "score_params.cuh"
 #include "sm100_ptx.cuh"
 #include "topk_heap.cuh"
 
@@ -206,9 +207,38 @@ struct TopkKernelArgs {
   float* ws_vals;    // [n_split * NWG][m_pad][k] raw scores, sorted best first
   int32_t* ws_idx;   // [n_split * NWG][m_pad][k] local key indices
   int* status;       // device status word
+  // Per-sequence mean of the fused scores (the kernel's AUX variant only):
+  // aux[g * ld_aux + n] += v(s[m, n]) / group_rows for the rows m of group
+  // g = m / group_rows, every key n of the shard.
+  int64_t M;           // real query rows (rows beyond are padding)
+  float* aux;
+  int64_t ld_aux;
+  int64_t group_rows;
+  const float* params;  // device {lambda_sharp, tau, T} or null (then the host values)
+  float lambda_sharp, tau, T;
+  int use_sigmoid;
 };
 
-template <int KCAP, int NWG>
+// Column sums of one 32-column chunk over the warp's 32 rows, in place: each
+// halving step keeps half of the values and adds the partner lane's copy of
+// them, so after five steps lane l holds the sum over all lanes of value l.
+__device__ __forceinline__ float warp_column_sum32(float (&f)[32], int lane) {
+#pragma unroll
+  for (int step = 0; step < 5; ++step) {
+    const int o = 16 >> step;
+    const int H = 16 >> step;
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < H; ++i) {
+      const float send = up ? f[i] : f[i + H];
+      const float keep = up ? f[i + H] : f[i];
+      f[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  return f[0];
+}
+
+template <int KCAP, int NWG, bool AUX>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
     score_topk_kernel(const __grid_constant__ CUtensorMap tmap_q,
                       const __grid_constant__ CUtensorMap tmap_k, const TopkKernelArgs a) {
@@ -466,6 +496,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
         }
       }
     };
+    // AUX: the fused score of every (row, key) of the chunk, summed over the
+    // rows of the row's group (sequence) and added into aux.  Runs after the
+    // chunk's scan and overwrites the chunk's registers.
+    const int64_t grow = static_cast<int64_t>(row0) + row;
+    const int64_t my_group = AUX && grow < a.M ? grow / a.group_rows : -1;
+    ScoreParams sp{a.lambda_sharp, a.tau, a.T};
+    if constexpr (AUX) sp = load_score_params(a.params, a.lambda_sharp, a.tau, a.T);
+    const float inv_T = 1.0f / sp.T;
+    const float aux_scale = AUX ? 1.0f / static_cast<float>(a.group_rows) : 0.0f;
+    const int64_t g0 = __shfl_sync(0xffffffffu, my_group, 0);
+    // rows increase with the lane: lane 0 invalid means the whole warp is padding
+    const bool aux_uniform = __all_sync(0xffffffffu, my_group == g0 || my_group < 0);
+    auto aux_chunk = [&](const uint32_t (&r)[32], int rem, int32_t col0) {
+      float f[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float sc = __uint_as_float(r[j]);
+        float v = __expf(sc * inv_T);
+        if (a.use_sigmoid) v = __fdividef(v, 1.0f + __expf(-sp.lambda_sharp * (sc - sp.tau)));
+        f[j] = (my_group >= 0 && j < rem) ? v * aux_scale : 0.0f;
+      }
+      if (g0 < 0) return;
+      if (aux_uniform) {
+        const float colsum = warp_column_sum32(f, lane);
+        if (lane < rem) atomicAdd(a.aux + g0 * a.ld_aux + col0 + lane, colsum);
+      } else if (my_group >= 0) {
+        // rows of two groups in this warp: every lane adds its own values
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < rem) atomicAdd(a.aux + my_group * a.ld_aux + col0 + j, f[j]);
+      }
+    };
     const uint32_t lead_tempty0 = map_to_cta(tempty_bar(0), 0);
     const uint32_t lead_tempty1 = map_to_cta(tempty_bar(1), 0);
     for (int t = g; t < n_tiles; t += NWG) {
@@ -489,21 +551,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
       const int valid = static_cast<int>(min(static_cast<int64_t>(kTileN), a.N - n0));
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + static_cast<uint32_t>(acc * kTileN);
-      // Chunks of 32 columns, two register sets in flight: the TMEM load of the
-      // next chunk overlaps the scan of the current one.
-      uint32_t ra[32], rb[32];
-      tmem_ld_32x32b_x32_async(taddr, ra);
-      tmem_wait_ld_pin(ra);
-      for (int c = 0; c < valid; c += 64) {
-        const bool has_b = c + 32 < valid;   // warp-uniform
-        if (has_b) tmem_ld_32x32b_x32_async(taddr + c + 32, rb);
-        scan_chunk(ra, valid - c, static_cast<int32_t>(n0 + c));
-        if (has_b) {
-          tmem_wait_ld_pin(rb);
-          const bool has_next = c + 64 < valid;
-          if (has_next) tmem_ld_32x32b_x32_async(taddr + c + 64, ra);
-          scan_chunk(rb, valid - c - 32, static_cast<int32_t>(n0 + c + 32));
-          if (has_next) tmem_wait_ld_pin(ra);
+      if constexpr (AUX) {
+        // One chunk of 32 columns at a time: the aux sums need the registers
+        // the overlapped load of the next chunk would hold.
+        for (int c = 0; c < valid; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32_async(taddr + c, r);
+          tmem_wait_ld_pin(r);
+          scan_chunk(r, valid - c, static_cast<int32_t>(n0 + c));
+          aux_chunk(r, valid - c, static_cast<int32_t>(n0 + c));
+        }
+      } else {
+        // Chunks of 32 columns, two register sets in flight: the TMEM load of
+        // the next chunk overlaps the scan of the current one.
+        uint32_t ra[32], rb[32];
+        tmem_ld_32x32b_x32_async(taddr, ra);
+        tmem_wait_ld_pin(ra);
+        for (int c = 0; c < valid; c += 64) {
+          const bool has_b = c + 32 < valid;   // warp-uniform
+          if (has_b) tmem_ld_32x32b_x32_async(taddr + c + 32, rb);
+          scan_chunk(ra, valid - c, static_cast<int32_t>(n0 + c));
+          if (has_b) {
+            tmem_wait_ld_pin(rb);
+            const bool has_next = c + 64 < valid;
+            if (has_next) tmem_ld_32x32b_x32_async(taddr + c + 64, ra);
+            scan_chunk(rb, valid - c - 32, static_cast<int32_t>(n0 + c + 32));
+            if (has_next) tmem_wait_ld_pin(ra);
+          }
         }
       }
       tc_fence_before();
@@ -568,7 +642,7 @@ __global__ void fill_i32_kernel(int32_t* p, int64_t n, int32_t v) {
 }
 
 // ---------------------------------------------------------------- host side
-template <int KCAP, int NWG>
+template <int KCAP, int NWG, bool AUX>
 cudaError_t configure_once() {
   static std::atomic<uint64_t> done_mask{0};
   int dev = 0;
@@ -576,21 +650,21 @@ cudaError_t configure_once() {
   if (e != cudaSuccess) return e;
   const uint64_t bit = 1ull << (dev & 63);
   if (done_mask.load(std::memory_order_acquire) & bit) return cudaSuccess;
-  e = cudaFuncSetAttribute(score_topk_kernel<KCAP, NWG>,
+  e = cudaFuncSetAttribute(score_topk_kernel<KCAP, NWG, AUX>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                            TopkCfg<KCAP, NWG>::kSmemBytes);
   if (e == cudaSuccess) done_mask.fetch_or(bit, std::memory_order_acq_rel);
   return e;
 }
 
-template <int KCAP, int NWG>
+template <int KCAP, int NWG, bool AUX>
 cudaError_t launch_variant(const ScoreTopkPlan& p, const CUtensorMap& mq, const CUtensorMap& mk,
                            const TopkKernelArgs& args, cudaStream_t stream) {
-  cudaError_t e = configure_once<KCAP, NWG>();
+  cudaError_t e = configure_once<KCAP, NWG, AUX>();
   if (e != cudaSuccess) return e;
   const unsigned grid = 2u * static_cast<unsigned>(p.n_qt) * static_cast<unsigned>(p.n_split);
-  score_topk_kernel<KCAP, NWG><<<grid, threads_for(NWG), TopkCfg<KCAP, NWG>::kSmemBytes, stream>>>(
-      mq, mk, args);
+  score_topk_kernel<KCAP, NWG, AUX>
+      <<<grid, threads_for(NWG), TopkCfg<KCAP, NWG>::kSmemBytes, stream>>>(mq, mk, args);
   return cudaGetLastError();
 }
 
@@ -705,7 +779,8 @@ bool plan_score_topk(int64_t M, int64_t N, int d, int k, int num_sms, ScoreTopkP
 cudaError_t launch_score_topk(const ScoreTopkPlan& p, const void* q, int64_t ldq, const void* keys,
                               int64_t ldk, float lambda_sharp, float tau, float T, int use_sigmoid,
                               int64_t idx_offset, float* out_vals, int32_t* out_idx, void* ws,
-                              cudaStream_t stream, const char** err_detail, const float* params) {
+                              cudaStream_t stream, const char** err_detail, const float* params,
+                              const SeqMeanOut* seq_mean) {
   CUtensorMap mq, mk;
   if (!make_bf16_tile_map(&mq, q, static_cast<uint64_t>(p.d), static_cast<uint64_t>(p.M),
                           static_cast<uint64_t>(ldq), kTileK, kTileM) ||
@@ -730,6 +805,26 @@ cudaError_t launch_score_topk(const ScoreTopkPlan& p, const void* q, int64_t ldq
   args.row_bound = reinterpret_cast<int32_t*>(wsb + kStatusBytes);
   args.ws_vals = reinterpret_cast<float*>(wsb + kStatusBytes + bound_bytes);
   args.ws_idx = reinterpret_cast<int32_t*>(wsb + kStatusBytes + bound_bytes + list_elems * 4);
+  args.M = p.M;
+  args.aux = nullptr;
+  args.ld_aux = 0;
+  args.group_rows = 1;
+  args.params = params;
+  args.lambda_sharp = lambda_sharp;
+  args.tau = tau;
+  args.T = T;
+  args.use_sigmoid = use_sigmoid;
+  if (seq_mean != nullptr) {
+    args.aux = seq_mean->out;
+    args.ld_aux = seq_mean->ld;
+    args.group_rows = seq_mean->group_rows;
+    // the kernel adds into it: start from zero (stream-ordered)
+    const int64_t groups = p.M / seq_mean->group_rows;
+    cudaError_t ez = cudaMemset2DAsync(seq_mean->out, static_cast<size_t>(seq_mean->ld) * 4, 0,
+                                       static_cast<size_t>(p.N) * 4, static_cast<size_t>(groups),
+                                       stream);
+    if (ez != cudaSuccess) return ez;
+  }
 
   cudaError_t e = cudaMemsetAsync(ws, 0, sizeof(int), stream);
   if (e != cudaSuccess) return e;
@@ -750,15 +845,18 @@ cudaError_t launch_score_topk(const ScoreTopkPlan& p, const void* q, int64_t ldq
 
 cudaError_t launch_plan(const ScoreTopkPlan& p, const CUtensorMap& mq, const CUtensorMap& mk,
                         const TopkKernelArgs& args, cudaStream_t stream) {
-  cudaError_t e;
-  switch (p.kcap * 4 + p.nwg) {
-    case 16 * 4 + 2: e = launch_variant<16, 2>(p, mq, mk, args, stream); break;
-    case 32 * 4 + 2: e = launch_variant<32, 2>(p, mq, mk, args, stream); break;
-    case 64 * 4 + 1: e = launch_variant<64, 1>(p, mq, mk, args, stream); break;
-    case 128 * 4 + 1: e = launch_variant<128, 1>(p, mq, mk, args, stream); break;
+  const bool aux = args.aux != nullptr;
+  switch (p.kcap * 8 + p.nwg * 2 + (aux ? 1 : 0)) {
+    case 16 * 8 + 4: return launch_variant<16, 2, false>(p, mq, mk, args, stream);
+    case 32 * 8 + 4: return launch_variant<32, 2, false>(p, mq, mk, args, stream);
+    case 64 * 8 + 2: return launch_variant<64, 1, false>(p, mq, mk, args, stream);
+    case 128 * 8 + 2: return launch_variant<128, 1, false>(p, mq, mk, args, stream);
+    case 16 * 8 + 5: return launch_variant<16, 2, true>(p, mq, mk, args, stream);
+    case 32 * 8 + 5: return launch_variant<32, 2, true>(p, mq, mk, args, stream);
+    case 64 * 8 + 3: return launch_variant<64, 1, true>(p, mq, mk, args, stream);
+    case 128 * 8 + 3: return launch_variant<128, 1, true>(p, mq, mk, args, stream);
     default: return cudaErrorInvalidValue;
   }
-  return e;
 }
 
 }  // namespace dwa

@@ -164,6 +164,7 @@ struct ReduceArgs {
   int* status;
   int64_t block_rows, M;
   int P, rank, d, step;
+  uint64_t wait_ns;  // limit of the wait for the peers' flags
 };
 
 __device__ __forceinline__ int32_t ld_acquire_sys_i32(const int32_t* p) {
@@ -172,12 +173,12 @@ __device__ __forceinline__ int32_t ld_acquire_sys_i32(const int32_t* p) {
   return v;
 }
 
-// Bounded wait of one thread for flags[0..P) >= step.
-__device__ bool wait_flags(const int32_t* flags, int P, int step) {
+// Bounded wait of one thread for flags[0..P) >= step (gives up after wait_ns).
+__device__ bool wait_flags(const int32_t* flags, int P, int step, uint64_t wait_ns) {
   const uint64_t t0 = globaltimer_ns();
   for (int p = 0; p < P; ++p) {
     while (ld_acquire_sys_i32(flags + p) < step) {
-      if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+      if (globaltimer_ns() - t0 > wait_ns) return false;
     }
   }
   return true;
@@ -188,7 +189,7 @@ __device__ bool wait_flags(const int32_t* flags, int P, int step) {
 __global__ void __launch_bounds__(256) reduce_broadcast_kernel(const ReduceArgs a) {
   __shared__ int ready;
   if (threadIdx.x == 0) {
-    ready = wait_flags(a.flags, a.P, a.step) ? 1 : 0;
+    ready = wait_flags(a.flags, a.P, a.step, a.wait_ns) ? 1 : 0;
     if (!ready) atomicCAS(a.status, 0, kStatusTimeout);
   }
   __syncthreads();
@@ -212,8 +213,9 @@ __global__ void __launch_bounds__(256) reduce_broadcast_kernel(const ReduceArgs 
     *reinterpret_cast<float4*>(a.outs[p] + grow * a.d + col) = acc;
 }
 
-__global__ void peer_wait_kernel(const int32_t* flags, int P, int step, int* status) {
-  if (threadIdx.x == 0 && !wait_flags(flags, P, step)) atomicCAS(status, 0, kStatusTimeout);
+__global__ void peer_wait_kernel(const int32_t* flags, int P, int step, uint64_t wait_ns,
+                                 int* status) {
+  if (threadIdx.x == 0 && !wait_flags(flags, P, step, wait_ns)) atomicCAS(status, 0, kStatusTimeout);
 }
 
 }  // namespace
@@ -247,7 +249,8 @@ cudaError_t launch_weighted_gather_peers(const float* vals, const int32_t* gidx,
 
 cudaError_t launch_reduce_broadcast_peers(const float* inbox, int P, int rank, int64_t block_rows,
                                           int64_t M, int d, float* const* outs, const int32_t* flags,
-                                          int step, int* status, cudaStream_t stream) {
+                                          int step, uint64_t wait_ns, int* status,
+                                          cudaStream_t stream) {
   if (P < 1 || P > kMaxPeerRanks || block_rows < 1 || d % 4 != 0) return cudaErrorInvalidValue;
   ReduceArgs a{};
   a.inbox = inbox;
@@ -260,15 +263,17 @@ cudaError_t launch_reduce_broadcast_peers(const float* inbox, int P, int rank, i
   a.rank = rank;
   a.d = d;
   a.step = step;
+  a.wait_ns = wait_ns;
   const int64_t threads = block_rows * (d / 4);
   const int64_t blocks = (threads + 255) / 256;
   reduce_broadcast_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
   return cudaGetLastError();
 }
 
-cudaError_t launch_peer_wait(const int32_t* flags, int P, int step, int* status, cudaStream_t stream) {
+cudaError_t launch_peer_wait(const int32_t* flags, int P, int step, uint64_t wait_ns, int* status,
+                             cudaStream_t stream) {
   if (P < 1 || P > kMaxPeerRanks) return cudaErrorInvalidValue;
-  peer_wait_kernel<<<1, 32, 0, stream>>>(flags, P, step, status);
+  peer_wait_kernel<<<1, 32, 0, stream>>>(flags, P, step, wait_ns, status);
   return cudaGetLastError();
 }
 

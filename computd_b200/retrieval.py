@@ -30,8 +30,8 @@ import torch.distributed as dist
 from . import _lib
 from .assembly import _check_values, normalise_alpha, weighted_gather_into
 from .pool import ShardSpec
-from .tiled_topk import (_as_bf16_rows, _stream_handle, merge_topk, score_topk_into, seq_scores,
-                         tiled_topk_fused, workspace_bytes)
+from .tiled_topk import (_as_bf16_rows, _stream_handle, merge_topk, score_topk_into,
+                         score_topk_seqmean, seq_scores, tiled_topk_fused, workspace_bytes)
 
 
 def _group_rank_world(group) -> tuple[int, int]:
@@ -56,8 +56,17 @@ class PeerExchange:
     packed (score bits, global index) lists into its own CUDA-IPC buffer and
     raises flag[rank] = step on every rank (``dwa_peer_signal``: system fence +
     release stores); then every rank's merge kernel (``dwa_merge_topk_peers``)
-    waits for all flags of this step (bounded: 2 s, then DWA_ERR_TIMEOUT in the
-    status word) and merges the P lists straight from the other GPUs' memory.
+    waits for all flags of this step and merges the P lists straight from the
+    other GPUs' memory.
+
+    Every wait for another rank is bounded by ``wait_s`` (default 30 s, well
+    above the longest layer, so a rank whose host falls behind for a while is
+    still waited for).  A wait that runs out writes -inf / -1 for its rows and
+    DWA_ERR_TIMEOUT in the status word.  The status word is copied to pinned
+    host memory after each waiting launch, and ``check`` (run at the start of
+    every ``Retriever`` call) raises ``DWAError`` once it shows an error: so
+    the failed call's outputs are never used by a following call.  From then
+    on the exchange refuses work until every rank has called ``resync``.
 
     Buffers alternate by step parity.  A rank rewrites the buffer of step s at
     step s + 2 only after its own merge of step s + 1, which waited for every
@@ -76,8 +85,12 @@ class PeerExchange:
     _HDR = 256            # bytes: int32 flag words: [0, 16) lists, [16, 32) partials,
     _STATUS_OFF = 192     # [32, 48) blocks done; status word at byte 192
 
-    def __init__(self, M: int, k: int, group, device: torch.device, d: int | None = None):
+    def __init__(self, M: int, k: int, group, device: torch.device, d: int | None = None,
+                 wait_s: float = 30.0):
         self.rank, self.world = _group_rank_world(group)
+        if not 0.0 < float(wait_s) <= 600.0:
+            raise ValueError("wait_s must be in (0, 600] seconds")
+        self.wait_ns = int(float(wait_s) * 1e9)
         if self.world > 16:
             raise _lib.DWAArgumentError(_lib.DWA_ERR_UNSUPPORTED_SHAPE, "PeerExchange",
                                         "more than 16 ranks")
@@ -149,7 +162,50 @@ class PeerExchange:
             self.out = torch.as_tensor(_DeviceBuffer(self._own + self._out_off, (self.M, self.d), "<f4"),
                                        device=device)
         self.step = 0
+        # the status word as last copied back (pinned), and the copy's completion
+        self._status_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self._status_event = torch.cuda.Event()
+        self._status_pending = False
+        self.failed = 0
         dist.barrier(group=group, device_ids=[device.index])
+
+    def _copy_status(self) -> None:
+        """Enqueue a copy of the status word to pinned host memory (after this stream's
+        waits); ``check`` reads it."""
+        self._status_host.copy_(self._hdr[self._STATUS_OFF // 4:self._STATUS_OFF // 4 + 1],
+                                non_blocking=True)
+        self._status_event.record(torch.cuda.current_stream(self.device))
+        self._status_pending = True
+
+    def check(self) -> None:
+        """Raise ``DWAError`` if a wait of an earlier step ran out (waits for the
+        status copy of the last step, which normally finished long ago)."""
+        if self.failed:
+            raise _lib.DWAError(self.failed, "PeerExchange",
+                                "an earlier cross-rank wait ran out; call resync() on every rank")
+        if not self._status_pending:
+            return
+        self._status_event.synchronize()
+        self._status_pending = False
+        v = int(self._status_host[0])
+        if v != 0:
+            self.failed = v
+            raise _lib.DWAError(v, "PeerExchange",
+                                f"a peer's flags did not arrive within {self.wait_ns / 1e9:.1f} s "
+                                f"by step {self.step}; that step's outputs are -inf / -1.  Call "
+                                "resync() on every rank before the next call")
+
+    def resync(self) -> None:
+        """Collective: after a run-out wait, wait for every rank, clear the flags and
+        the status word and restart the step count, so the exchange is usable again."""
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group, device_ids=[self.device.index])
+        self._hdr.zero_()
+        torch.cuda.synchronize(self.device)
+        self.step = 0
+        self.failed = 0
+        self._status_pending = False
+        dist.barrier(group=self.group, device_ids=[self.device.index])
 
     def publish(self, local_vals: torch.Tensor, local_idx: torch.Tensor) -> None:
         """Pack this rank's [M, k] lists into its buffer and raise its flag on every rank."""
@@ -168,10 +224,12 @@ class PeerExchange:
         lib = _lib.load()
         with torch.cuda.device(self.device):
             st = lib.dwa_merge_topk_peers(self._list_tables[self.step & 1], self.world, self.M,
-                                          self.k, self._own, self.step, out_vals.data_ptr(),
-                                          out_idx.data_ptr(), self._own + self._STATUS_OFF,
+                                          self.k, self._own, self.step, self.wait_ns,
+                                          out_vals.data_ptr(), out_idx.data_ptr(),
+                                          self._own + self._STATUS_OFF,
                                           _stream_handle(self.device))
-        _lib.check(st, "dwa_merge_topk_peers")
+            _lib.check(st, "dwa_merge_topk_peers")
+            self._copy_status()
 
     def gather_partials(self, top_vals: torch.Tensor, top_idx: torch.Tensor, values: torch.Tensor,
                         row_begin: int, row_end: int, alpha_out: torch.Tensor) -> None:
@@ -197,16 +255,17 @@ class PeerExchange:
         with torch.cuda.device(self.device):
             st = lib.dwa_reduce_broadcast_peers(self._own + self._inbox_off, self.world, self.rank,
                                                 self.block_rows, self.M, self.d, self._outs,
-                                                self._own + 64, self.step, status, sh)
+                                                self._own + 64, self.step, self.wait_ns, status, sh)
             _lib.check(st, "dwa_reduce_broadcast_peers")
             st = lib.dwa_peer_signal(self._done_flags, self.world, self.rank, self.step, sh)
             _lib.check(st, "dwa_peer_signal")
-            st = lib.dwa_peer_wait(self._own + 128, self.world, self.step, status, sh)
-        _lib.check(st, "dwa_peer_wait")
+            st = lib.dwa_peer_wait(self._own + 128, self.world, self.step, self.wait_ns, status, sh)
+            _lib.check(st, "dwa_peer_wait")
+            self._copy_status()
         return self.out
 
     def status(self) -> int:
-        """Device status word of the peer merge (0 or DWA_ERR_TIMEOUT); syncs the device."""
+        """Device status word of the peer waits (0 or DWA_ERR_TIMEOUT); syncs the device."""
         torch.cuda.synchronize(self.device)
         return int(self._hdr[self._STATUS_OFF // 4].item())
 
@@ -289,11 +348,15 @@ class Retriever:
 
     ``keys_local`` / ``values_local`` are this rank's rows [row_begin, row_end)
     of the pool (the whole pool when ``group`` is None or has one rank).
+    On a sharded pool every wait for another rank gives up after
+    ``peer_wait_s`` seconds; the next call then raises ``DWAError`` (see
+    ``PeerExchange``) instead of computing on the -1 indices of the failed one.
     """
 
     def __init__(self, keys_local: torch.Tensor, values_local: torch.Tensor, M: int, k: int, *,
                  lambda_sharp: float = 1.0, tau: float = 0.0, T: float = 1.0,
-                 use_sigmoid: bool = False, group=None, exchange: str = "auto"):
+                 use_sigmoid: bool = False, group=None, exchange: str = "auto",
+                 peer_wait_s: float = 30.0):
         self.keys = _as_bf16_rows(keys_local, "keys_local")
         self.values = _check_values(values_local)
         if self.values.shape[0] != self.keys.shape[0]:
@@ -335,7 +398,8 @@ class Retriever:
         self.peer = None
         if use_peer and self.d_v % 8 == 0:
             try:
-                self.peer = PeerExchange(self.M, self.k, self.group, dev, d=self.d_v)
+                self.peer = PeerExchange(self.M, self.k, self.group, dev, d=self.d_v,
+                                         wait_s=peer_wait_s)
             except _lib.DWAError:
                 # raised on every rank together; "auto" falls back to NCCL everywhere
                 if exchange == "nvlink":
@@ -362,6 +426,8 @@ class Retriever:
         (global indices), into ``local_vals`` / ``local_idx``."""
         if tuple(queries.shape) != (self.M, self.d_k):
             raise ValueError(f"queries must be [{self.M}, {self.d_k}], got {tuple(queries.shape)}")
+        if self.peer is not None:
+            self.peer.check()  # raises if a cross-rank wait of an earlier call ran out
         score_topk_into(queries, self.keys, self.k, self.lambda_sharp, self.tau, self.T,
                         self.use_sigmoid, self.local_vals, self.local_idx, self.workspace,
                         idx_offset=self.shard.row_begin)
@@ -590,6 +656,32 @@ def project_keys(vectors: torch.Tensor, W_K: torch.Tensor, w: torch.Tensor,
     return out
 
 
+def project_keys_packed(vectors: torch.Tensor, W_K: torch.Tensor, w: torch.Tensor,
+                        out: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-aspect pool keys side by side, [N, S d_k] bf16:
+    out[n, s d_k : (s + 1) d_k] = sqrt(w[s]) k_s / (|k_s| + 1e-8), k_s = W_K[s] @ v
+    (``dwa_project_keys_packed``: one tcgen05 GEMM, normalisation and scaling in
+    its epilogue).  With queries packed the same way, one dot product of length
+    S d_k is hybrid_forward's aspect-weighted score sum_s w_s <q_s, k_s>
+    (reference retrieval.py:154-165)."""
+    v = _as_bf16_rows(vectors, "vectors")
+    S, d_k, D = W_K.shape
+    if v.shape[1] != D:
+        raise ValueError(f"vectors must be [N, {D}]")
+    wk = W_K.to(device=v.device, dtype=torch.bfloat16).reshape(S * d_k, D).contiguous()
+    wv = w.to(device=v.device, dtype=torch.float32).contiguous()
+    N = v.shape[0]
+    if out is None:
+        out = torch.empty((N, S * d_k), dtype=torch.bfloat16, device=v.device)
+    lib = _lib.load()
+    with torch.cuda.device(v.device):
+        st = lib.dwa_project_keys_packed(v.data_ptr(), N, v.stride(0), D, wk.data_ptr(),
+                                         wk.stride(0), S, d_k, wv.data_ptr(), out.data_ptr(),
+                                         out.stride(0), None, _stream_handle(v.device))
+    _lib.check(st, "dwa_project_keys_packed")
+    return out
+
+
 class MultiAspectRetrieval:
     """Parameters and ``pallas_hybrid_forward`` of the reference's retrieval
     module (src/model/retrieval.py:7-46, 204-343) on B200.
@@ -641,6 +733,62 @@ class MultiAspectRetrieval:
                 acc += w[s] * self._normalize(v @ WK[s].T)
             out[r0:r0 + chunk_rows] = acc.to(torch.bfloat16)
         return out
+
+    def project_keys_packed(self, vectors: torch.Tensor, w: torch.Tensor,
+                            chunk_rows: int = 1 << 16) -> torch.Tensor:
+        """[sqrt(w_s) W_K[s] v / (|W_K[s] v| + 1e-8)]_s for every pool row, [N, S d_k]
+        bf16.  bf16 W_K: the fused tcgen05 kernel (``dwa_project_keys_packed``) when
+        d_k is 32, 64 or 128 and D % 8 == 0; fp32 W_K: fp32 GEMMs chunked over
+        rows, keeping the parameters' precision."""
+        N, D = vectors.shape
+        if (self.W_K.dtype == torch.bfloat16 and self.d_k in (32, 64, 128) and D % 8 == 0
+                and vectors.is_cuda):
+            return project_keys_packed(vectors, self.W_K, w)
+        out = torch.empty((N, self.S * self.d_k), dtype=torch.bfloat16, device=vectors.device)
+        WK = self.W_K.float()
+        sw = w.float().sqrt()
+        for r0 in range(0, N, chunk_rows):
+            v = vectors[r0:r0 + chunk_rows].float()
+            ks = self._normalize(torch.einsum("skd,nd->nsk", WK, v)) * sw[None, :, None]
+            out[r0:r0 + chunk_rows] = ks.reshape(v.shape[0], -1).to(torch.bfloat16)
+        return out
+
+    def hybrid_parts(self, z: torch.Tensor, vectors: torch.Tensor, k_max: int, T: float = 1.0,
+                     lambda_sharp: float = 1.0, use_sigmoid: bool = True) -> "HybridParts":
+        """``hybrid_forward`` with its intermediates (queries_flat / keys_w are the
+        packed [sqrt(w_s) q_s]_s / [sqrt(w_s) k_s]_s the score kernel saw)."""
+        B, seq, d_A = z.shape
+        w = torch.softmax(self.aspect_logits.float(), dim=0)                     # 164
+        tau = (torch.dot(w, self.tau.float()) if use_sigmoid                    # 168
+               else torch.zeros((), dtype=torch.float32, device=w.device))
+        keys_p = self.project_keys_packed(vectors, w)                           # 155-156
+        zf = z.float()
+        queries_s = self._normalize(torch.einsum("skd,btd->btsk", self.W_Q.float(), zf))  # 159-160
+        q_packed = (queries_s * w.sqrt()[None, None, :, None]).reshape(B, seq, -1)
+        queries_flat = q_packed.reshape(B * seq, -1).to(torch.bfloat16)
+        # 163-175: the aspect-weighted score of every (position, key), its gate/exp,
+        # the per-position top-k and the seq mean of the fused scores, in one kernel
+        top_vals, top_idx, alpha_raw_seq = score_topk_seqmean(
+            queries_flat, keys_p, k_max, lambda_sharp, tau, T, use_sigmoid, seq)
+        alpha = normalise_alpha(top_vals).view(B, seq, k_max)                   # 178
+        # 181: the seq mean of sims is linear in the query: one skinny product
+        sims_seq, _ = seq_scores(q_packed.mean(dim=1), keys_p, lambda_sharp, tau, T, use_sigmoid)
+        return HybridParts(alpha, top_idx.view(B, seq, k_max), sims_seq, alpha_raw_seq,
+                           queries_flat, keys_p, tau, top_vals)
+
+    def hybrid_forward(self, z: torch.Tensor, vectors: torch.Tensor, k_max: int, T: float = 1.0,
+                       lambda_sharp: float = 1.0, use_sigmoid: bool = True):
+        """Per-position retrieval over all N with the aspect-weighted score, keeping only
+        the top-k (reference retrieval.py:131-181).  Returns (alpha f32 [B, seq, k],
+        top_idx i32 [B, seq, k], sims_seq f32 [B, N], alpha_raw_seq f32 [B, N]).
+
+        The score sum_s w_s <q_s, k_s> is one dot product of the packed
+        [sqrt(w_s) q_s]_s and [sqrt(w_s) k_s]_s (d = S d_k), so it runs on the same
+        fused score + top-k kernel as ``pallas_hybrid_forward``; alpha_raw_seq (the
+        seq mean of the fused scores, which needs every score) is summed in that
+        kernel's epilogue and never goes through HBM as a [B, seq, N] tensor."""
+        p = self.hybrid_parts(z, vectors, k_max, T, lambda_sharp, use_sigmoid)
+        return p.alpha, p.top_idx, p.sims_seq, p.alpha_raw_seq
 
     def pallas_hybrid_parts(self, z: torch.Tensor, vectors: torch.Tensor, k_max: int,
                             T: float = 1.0, lambda_sharp: float = 1.0, use_sigmoid: bool = True,

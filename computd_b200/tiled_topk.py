@@ -146,6 +146,48 @@ def tiled_topk_fused(queries: torch.Tensor, keys: torch.Tensor, k_max: int, lamb
     return out_vals, out_idx
 
 
+def score_topk_seqmean(queries: torch.Tensor, keys: torch.Tensor, k_max: int, lambda_sharp, tau, T,
+                       use_sigmoid: bool, seq: int, *, idx_offset: int = 0,
+                       workspace: torch.Tensor | None = None
+                       ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Fused score + top-k plus the per-sequence mean of the fused scores over every key
+    (``dwa_score_topk_seqmean``): the queries are ``M / seq`` sequences of ``seq`` rows.
+
+    Returns (top_vals f32 [M, k], top_idx i32 [M, k], fused_mean f32 [M / seq, N]),
+    fused_mean[b, n] = mean over the rows t of sequence b of v(q[b seq + t] . keys[n]),
+    i.e. hybrid_forward's ``alpha_raw.mean(axis=1)`` (reference retrieval.py:176-181).
+    The scalars are read on the device."""
+    queries = _as_bf16_rows(queries, "queries")
+    keys = _as_bf16_rows(keys, "keys")
+    if queries.shape[1] != keys.shape[1] or keys.device != queries.device:
+        raise ValueError("queries and keys must have the same width and device")
+    M, d = queries.shape
+    N = keys.shape[0]
+    seq = int(seq)
+    if seq < 1 or M % seq:
+        raise ValueError(f"seq={seq} must divide the {M} query rows")
+    dev = queries.device
+    k = int(k_max)
+    out_vals = torch.empty((M, k), dtype=torch.float32, device=dev)
+    out_idx = torch.empty((M, k), dtype=torch.int32, device=dev)
+    fused_mean = torch.empty((M // seq, N), dtype=torch.float32, device=dev)
+    if M == 0:
+        return out_vals, out_idx, fused_mean
+    if workspace is None:
+        workspace = torch.empty(max(workspace_bytes(M, N, d, k, dev), 256), dtype=torch.uint8,
+                                device=dev)
+    params = score_params(lambda_sharp, tau, T, dev)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        st = lib.dwa_score_topk_seqmean(
+            queries.data_ptr(), M, queries.stride(0), keys.data_ptr(), N, keys.stride(0), d, k,
+            params.data_ptr(), int(bool(use_sigmoid)), int(idx_offset), seq, fused_mean.data_ptr(),
+            fused_mean.stride(0), out_vals.data_ptr(), out_idx.data_ptr(), workspace.data_ptr(),
+            workspace.numel() * workspace.element_size(), _stream_handle(dev))
+    _lib.check(st, "dwa_score_topk_seqmean")
+    return out_vals, out_idx, fused_mean
+
+
 def seq_scores(q: torch.Tensor, keys: torch.Tensor, lambda_sharp, tau, T, use_sigmoid: bool,
                sims: torch.Tensor | None = None, fused: torch.Tensor | None = None,
                status: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:

@@ -139,6 +139,26 @@ DWA_API dwa_status dwa_score_topk_dev(const void* q, int64_t M, int64_t ldq,
                           void* ws, size_t ws_bytes, dwa_stream_t stream);
 
 /*
+ * dwa_score_topk_dev plus, from the same score tiles, the per-sequence mean of
+ * the fused scores: the queries are `M / seq` sequences of `seq` consecutive
+ * rows, and
+ *   fused_mean[b, n] = (1 / seq) sum_{t < seq} v(s[b * seq + t, n])
+ * for every key n of the shard (f32 [M / seq, ld_mean], overwritten).  This is
+ * hybrid_forward's alpha_raw.mean(axis=1) (src/model/retrieval.py:176-181),
+ * which needs every per-position score and so cannot come from the top-k or
+ * from a mean query; computing it in the score kernel's epilogue keeps the
+ * [M, N] score matrix out of HBM.  seq must divide M; ld_mean >= N_local.
+ * The sums use f32 atomics, so their order (and the last bits) may vary from
+ * call to call.  Other arguments, workspace and results as dwa_score_topk_dev.
+ */
+DWA_API dwa_status dwa_score_topk_seqmean(const void* q, int64_t M, int64_t ldq,
+                          const void* keys, int64_t N_local, int64_t ldk,
+                          int32_t d, int32_t k, const float* params, int32_t use_sigmoid,
+                          int64_t idx_offset, int64_t seq, float* fused_mean, int64_t ld_mean,
+                          float* out_vals, int32_t* out_idx,
+                          void* ws, size_t ws_bytes, dwa_stream_t stream);
+
+/*
  * Sequence-mean auxiliary scores of the retrieval (src/model/retrieval.py:
  * 332-341): for a few query rows q (f32 [B, ldq]; the per-sequence mean
  * queries q_mean_w) against every key of the shard (bf16 [N, ldk]):
@@ -286,6 +306,20 @@ DWA_API dwa_status dwa_project_keys(const void* vectors, int64_t N, int64_t ldv,
                             const float* aspect_w, void* keys_out, int64_t ldo,
                             int32_t* status, dwa_stream_t stream);
 
+/*
+ * The per-aspect keys of hybrid_forward side by side (src/model/retrieval.py:
+ * 154-165): keys_out[n, s d_k + j] = sqrt(w[s]) k_s[j] / (|k_s| + 1e-8) with
+ * k_s = W_K[s] vectors[n].  Since sum_s w_s <q_s, k_s> = <[sqrt(w_s) q_s]_s,
+ * [sqrt(w_s) k_s]_s>, hybrid_forward's aspect-weighted score is one dot
+ * product of length S d_k, i.e. dwa_score_topk on these keys and the queries
+ * packed the same way.  Same kernel and arguments as dwa_project_keys;
+ * keys_out: bf16 [N, ldo], ldo >= S d_k.
+ */
+DWA_API dwa_status dwa_project_keys_packed(const void* vectors, int64_t N, int64_t ldv, int32_t D,
+                            const void* w_k, int64_t ldw, int32_t S, int32_t d_k,
+                            const float* aspect_w, void* keys_out, int64_t ldo,
+                            int32_t* status, dwa_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Cross-shard exchange over NVLink peer memory: the all-gather + merge of
  * _chip_topk (src/model/retrieval.py:295-302) as one kernel that reads the
@@ -318,15 +352,20 @@ DWA_API dwa_status dwa_peer_signal(void* const* flag_bases, int32_t P, int32_t m
  * rank p's int32 [M, k, 2] list (fused score bits, global index), sorted
  * best first, as mapped on this GPU.  Each warp first waits until
  * flags[p] >= step for every p (this GPU's flag array, written by the
- * ranks' dwa_peer_signal); a wait longer than 2 s records DWA_ERR_TIMEOUT in
- * *status, writes -inf / -1 for that row and returns.  out_vals f32 /
- * out_idx i32 [M, k] (ties: lower global index first, as lax.top_k).
- * k must be even and the lists 16-byte aligned (each row is staged in
- * shared memory with 16-byte loads).
+ * ranks' dwa_peer_signal); a wait longer than wait_ns nanoseconds
+ * (<= 0: DWA_PEER_WAIT_DEFAULT_NS; capped at DWA_PEER_WAIT_MAX_NS) records
+ * DWA_ERR_TIMEOUT in *status, writes -inf / -1 for that row and returns.
+ * Choose wait_ns above the longest time a peer can lag (its own score kernel
+ * plus host-side stalls).  out_vals f32 / out_idx i32 [M, k] (ties: lower
+ * global index first, as lax.top_k).  k must be even and the lists 16-byte
+ * aligned (each row is staged in shared memory with 16-byte loads).
  */
+#define DWA_PEER_WAIT_DEFAULT_NS 30000000000LL
+#define DWA_PEER_WAIT_MAX_NS 600000000000LL
 DWA_API dwa_status dwa_merge_topk_peers(const void* const* packed, int32_t P, int64_t M, int32_t k,
-                                const int32_t* flags, int32_t step, float* out_vals,
-                                int32_t* out_idx, int32_t* status, dwa_stream_t stream);
+                                const int32_t* flags, int32_t step, int64_t wait_ns,
+                                float* out_vals, int32_t* out_idx, int32_t* status,
+                                dwa_stream_t stream);
 
 /*
  * Owner-computes value sum with the cross-rank sum over NVLink (the
@@ -342,8 +381,8 @@ DWA_API dwa_status dwa_merge_topk_peers(const void* const* packed, int32_t P, in
  *     and writes the sums into every rank's output (outs[p]: f32 [M, d]);
  *     then dwa_peer_signal on the "block done" flag arrays.
  *  3. dwa_peer_wait on the "block done" flags before the output is read.
- * d % 8 == 0; P <= DWA_MAX_PEERS.  Timeouts (2 s) record DWA_ERR_TIMEOUT in
- * *status.
+ * d % 8 == 0; P <= DWA_MAX_PEERS.  The waits give up after wait_ns (as in
+ * dwa_merge_topk_peers) and record DWA_ERR_TIMEOUT in *status.
  */
 DWA_API dwa_status dwa_weighted_gather_peers(const float* vals, const int32_t* gidx, int64_t M,
                                      int32_t k, const void* values, int64_t row_begin,
@@ -353,9 +392,9 @@ DWA_API dwa_status dwa_weighted_gather_peers(const float* vals, const int32_t* g
 DWA_API dwa_status dwa_reduce_broadcast_peers(const float* inbox, int32_t P, int32_t rank,
                                       int64_t block_rows, int64_t M, int32_t d,
                                       void* const* outs, const int32_t* flags, int32_t step,
-                                      int32_t* status, dwa_stream_t stream);
-DWA_API dwa_status dwa_peer_wait(const int32_t* flags, int32_t P, int32_t step, int32_t* status,
-                         dwa_stream_t stream);
+                                      int64_t wait_ns, int32_t* status, dwa_stream_t stream);
+DWA_API dwa_status dwa_peer_wait(const int32_t* flags, int32_t P, int32_t step, int64_t wait_ns,
+                         int32_t* status, dwa_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Low-rank weight assembly: the consumer of the retrieved rows in a DWA

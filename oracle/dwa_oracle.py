@@ -16,6 +16,9 @@ reference tree):
                          all_gather stacking, transpose/reshape, top_k, take)
 * ``sharded_topk``     — retrieval.py:280-313 (shard_map over a row-sharded pool)
 * ``normalise``        — retrieval.py:326 (alpha = v / (sum v + 1e-8))
+* ``hybrid_forward``   — retrieval.py:131-181 (MultiAspectRetrieval.hybrid_forward:
+                         per-aspect scores weighted by softmax(aspect_logits),
+                         gate/exp, top_k per position, seq means of sims and scores)
 * ``weighted_sum``     — src/model/assembly.py:104,127 (vectors[idx], alpha-weighted sum)
 * ``lowrank_delta``    — src/model/assembly.py:110-127 (U/V/b split, hV, h_delta, b_delta)
 * ``assemble_forward`` — assembly.py:75-128, WeightAssembler.__call__ per-position path
@@ -177,6 +180,37 @@ def retrieve(q, keys, values, k, lambda_sharp=1.0, tau=0.0, T=1.0, use_sigmoid=F
         v, i = sharded_topk(q, keys, k, P, lambda_sharp, tau, T, use_sigmoid, accum=accum)
     a = normalise(v)
     return weighted_sum(a, i, values, accum=accum), a, v, i
+
+
+def _l2n(x: np.ndarray) -> np.ndarray:
+    return x / (np.linalg.norm(x, axis=-1, keepdims=True) + 1e-8)
+
+
+def hybrid_forward(z, vectors, W_Q, W_K, aspect_logits, tau_param, k, T=1.0, lambda_sharp=1.0,
+                   use_sigmoid=True, accum=np.float64):
+    """MultiAspectRetrieval.hybrid_forward (retrieval.py:131-181), computed in `accum`.
+
+    keys_s = normalise(W_K[s] . vectors), queries_s = normalise(W_Q[s] . z) per
+    aspect; sims_w[b, t, n] = sum_s w_s <queries_s[b, t], keys_s[n]> with
+    w = softmax(aspect_logits); alpha_raw = gate * exp(sims_w / T) (gate =
+    sigmoid(lambda (sims_w - w . tau)) when use_sigmoid); top_k per position;
+    alpha = top_vals / (sum + 1e-8); seq means of sims_w and alpha_raw.
+    Returns (alpha f32 [B, seq, k], idx i32 [B, seq, k], sims_seq f64 [B, N],
+    alpha_raw_seq f64 [B, N], top_vals f32 [B, seq, k])."""
+    W_Q = np.asarray(W_Q, accum)
+    W_K = np.asarray(W_K, accum)
+    keys = _l2n(np.einsum("skd,nd->snk", W_K, np.asarray(vectors, accum)))        # 155-156
+    queries = _l2n(np.einsum("skd,btd->sbtk", W_Q, np.asarray(z, accum)))        # 159-160
+    al = np.asarray(aspect_logits, accum)
+    w = np.exp(al - al.max())
+    w = w / w.sum()                                                               # 164
+    sims_w = np.einsum("s,sbtn->btn", w, np.einsum("sbtk,snk->sbtn", queries, keys))  # 163-165
+    tau = float(w @ np.asarray(tau_param, accum)) if use_sigmoid else 0.0          # 168
+    alpha_raw = fused_score(sims_w, lambda_sharp, tau, T, use_sigmoid)             # 168-172
+    top_vals, top_idx = top_k(alpha_raw, k)                                       # 175
+    top_vals = top_vals.astype(np.float32)
+    alpha = normalise(top_vals)                                                   # 178
+    return alpha, top_idx, sims_w.mean(axis=1), alpha_raw.mean(axis=1), top_vals  # 181
 
 
 # --------------------------------------------------------------------------- low-rank assembly

@@ -11,6 +11,7 @@ all_gather, shard_map, ...).  What runs is the reference's own source:
                                   ``WeightAssembler.__call__``, per-position idx
                                   with a flax-LayerNorm stand-in       (lines 75-128)
 * ``src/model/pool.py``          ``VectorPool.update_ema``           (lines 52-55)
+* ``src/model/retrieval.py``     ``MultiAspectRetrieval.hybrid_forward`` (lines 131-181)
 
 Inputs are float32 arrays holding bf16-representable values (the B200 kernel
 takes bf16, so both sides see identical inputs).  Run from the repository
@@ -140,6 +141,50 @@ def case_sharded(ref_tk, ref_ret, ref_asm, rng, out, n_chips=4):
     out["sharded/alpha_raw_seq"] = np.asarray(alpha_raw_seq, np.float32)
 
 
+def case_hybrid(ref_ret, rng, out, name, B, seq, d_A, S, d_k, k, N, D, lam, T, use_sigmoid):
+    """MultiAspectRetrieval.hybrid_forward (retrieval.py:131-181), single device:
+    per-position top-k over all N with the aspect-weighted score, plus the seq
+    means of sims and of the fused scores.  Parameters and inputs hold
+    bf16-representable values (the reference's parameter dtype); the top_k
+    call is recorded for its values."""
+    self = types.SimpleNamespace()
+    self.S, self.d_k, self.N = S, d_k, N
+    self.W_Q = types.SimpleNamespace(value=bf16_round(rng.standard_normal((S, d_k, d_A)) * d_A ** -0.5))
+    self.W_K = types.SimpleNamespace(value=bf16_round(rng.standard_normal((S, d_k, D)) * D ** -0.5))
+    self.aspect_logits = types.SimpleNamespace(value=rng.standard_normal(S).astype(np.float32))
+    self.tau = types.SimpleNamespace(value=(0.1 * rng.standard_normal(S)).astype(np.float32))
+    z = bf16_round(rng.standard_normal((B, seq, d_A)).astype(np.float32))
+    vectors = bf16_round(rng.standard_normal((N, D)).astype(np.float32))
+    recorded = {}
+    lax = ref_ret.jax.lax
+    orig = lax.top_k
+
+    def recording_top_k(x, kk):
+        res = orig(x, kk)
+        recorded["top_vals"] = np.asarray(res[0], np.float32)
+        return res
+
+    lax.top_k = recording_top_k
+    try:
+        alpha, top_idx, sims_seq, alpha_raw_seq = ref_ret.MultiAspectRetrieval.hybrid_forward(
+            self, z, vectors, k, T, lam, use_sigmoid)
+    finally:
+        lax.top_k = orig
+    out[f"{name}/dims"] = np.array([B, seq, d_A, S, d_k, k, N, D])
+    out[f"{name}/params"] = np.array([lam, T, float(use_sigmoid)], dtype=np.float64)
+    out[f"{name}/z"] = _bits(z)
+    out[f"{name}/vectors"] = _bits(vectors)
+    out[f"{name}/W_Q"] = _bits(self.W_Q.value)
+    out[f"{name}/W_K"] = _bits(self.W_K.value)
+    out[f"{name}/aspect_logits"] = self.aspect_logits.value
+    out[f"{name}/tau_param"] = self.tau.value
+    out[f"{name}/alpha"] = np.asarray(alpha, np.float32)
+    out[f"{name}/idx"] = np.asarray(top_idx, np.int32)
+    out[f"{name}/top_vals"] = recorded["top_vals"]
+    out[f"{name}/sims_seq"] = np.asarray(sims_seq, np.float32)
+    out[f"{name}/alpha_raw_seq"] = np.asarray(alpha_raw_seq, np.float32)
+
+
 def case_assembler(ref_asm, ref_pool, rng, out, name, d_A, d_B, r):
     """WeightAssembler.__call__ on per-position (hybrid) idx, non-zero W_base / b_base /
     gamma / LayerNorm parameters, pool rows wider than U|V|b; then VectorPool.update_ema
@@ -211,6 +256,9 @@ def main(argv=None) -> int:
     case_sharded(ref_tk, ref_ret, ref_asm, rng, out)
     case_assembler(ref_asm, ref_pool, rng, out, "asm_eq", 48, 48, 4)
     case_assembler(ref_asm, ref_pool, rng, out, "asm_ne", 40, 24, 8)
+    # appended after the cases above so that their arrays stay as they were
+    case_hybrid(ref_ret, rng, out, "hybrid_gate", 2, 64, 48, 3, 32, 8, 700, 96, 4.0, 0.9, True)
+    case_hybrid(ref_ret, rng, out, "hybrid_exp", 3, 40, 40, 2, 64, 12, 500, 72, 1.0, 0.7, False)
     np.savez_compressed(args.out, **out)
     print(f"wrote {args.out}: {len(out)} arrays")
     return 0

@@ -142,9 +142,10 @@ def test_nvlink_and_projection_entry_points_validate_before_launch():
     assert lib.dwa_peer_signal(_ptrs(FAKE, FAKE), 17, 0, 1, None) == 1         # P > 16
     # peer merge: odd k (16-byte staging), P range, list alignment
     out_v, out_i, st = FAKE + 4096, FAKE + 8192, FAKE + 12288
-    assert lib.dwa_merge_topk_peers(_ptrs(FAKE, FAKE), 2, 8, 5, FAKE, 1, out_v, out_i, st, None) == 2
-    assert lib.dwa_merge_topk_peers(_ptrs(FAKE), 0, 8, 4, FAKE, 1, out_v, out_i, st, None) == 1
-    assert lib.dwa_merge_topk_peers(_ptrs(FAKE + 8, FAKE), 2, 8, 4, FAKE, 1, out_v, out_i, st, None) == 1
+    assert lib.dwa_merge_topk_peers(_ptrs(FAKE, FAKE), 2, 8, 5, FAKE, 1, 0, out_v, out_i, st, None) == 2
+    assert lib.dwa_merge_topk_peers(_ptrs(FAKE), 0, 8, 4, FAKE, 1, 0, out_v, out_i, st, None) == 1
+    assert lib.dwa_merge_topk_peers(_ptrs(FAKE + 8, FAKE), 2, 8, 4, FAKE, 1, 0, out_v, out_i, st,
+                                    None) == 1
     # peer value sum: blocks must cover M, d % 8
     assert lib.dwa_weighted_gather_peers(FAKE, FAKE, 100, 4, FAKE, 0, 10, 64, 64, _ptrs(FAKE, FAKE),
                                          2, 0, 40, None, None) == 1
@@ -152,12 +153,12 @@ def test_nvlink_and_projection_entry_points_validate_before_launch():
                                          2, 0, 50, None, None) == 2
     assert lib.dwa_weighted_gather_peers(FAKE, FAKE, 100, 4, FAKE, 0, 10, 64, 64, _ptrs(FAKE, FAKE),
                                          2, 2, 50, None, None) == 1
-    assert lib.dwa_reduce_broadcast_peers(FAKE, 2, 0, 40, 100, 64, _ptrs(FAKE, FAKE), FAKE, 1, st,
+    assert lib.dwa_reduce_broadcast_peers(FAKE, 2, 0, 40, 100, 64, _ptrs(FAKE, FAKE), FAKE, 1, 0, st,
                                           None) == 1
-    assert lib.dwa_reduce_broadcast_peers(FAKE, 2, 0, 50, 100, 60, _ptrs(FAKE, FAKE), FAKE, 1, st,
+    assert lib.dwa_reduce_broadcast_peers(FAKE, 2, 0, 50, 100, 60, _ptrs(FAKE, FAKE), FAKE, 1, 0, st,
                                           None) == 2
-    assert lib.dwa_peer_wait(None, 2, 1, st, None) == 1
-    assert lib.dwa_peer_wait(FAKE, 0, 1, st, None) == 1
+    assert lib.dwa_peer_wait(None, 2, 1, 0, st, None) == 1
+    assert lib.dwa_peer_wait(FAKE, 0, 1, 0, st, None) == 1
     # key projection: d_k, D, S, strides
     assert lib.dwa_project_keys(FAKE, 10, 64, 64, FAKE, 64, 2, 48, FAKE, FAKE, 64, None, None) == 2
     assert lib.dwa_project_keys(FAKE, 10, 64, 12, FAKE, 64, 2, 32, FAKE, FAKE, 64, None, None) == 2

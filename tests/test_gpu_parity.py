@@ -410,3 +410,66 @@ def test_project_keys_vs_fp32(lib, N, D, S, d_k):
     want = torch.einsum("s,snk->nk", w, ks)
     err = float((got - want).abs().max())
     assert err <= RTOL * float(want.abs().max()), f"max abs err {err}"
+
+
+@pytest.mark.parametrize("name", ["hybrid_gate", "hybrid_exp"])
+def test_hybrid_forward_matches_reference(lib, golden, name):
+    """MultiAspectRetrieval.hybrid_forward (retrieval.py:131-181) against the
+    reference's own run: packed per-aspect keys from the tcgen05 projection,
+    the aspect-weighted score through the fused score + top-k kernel, and the
+    seq mean of the fused scores from that kernel's epilogue.  hybrid_exp has
+    seq = 40, so warps straddle two sequences (the per-lane accumulation path)."""
+    dev = _dev()
+    B, seq, d_A, S, d_k, k, N, D = (int(x) for x in golden[f"{name}/dims"])
+    lam, T, sig = (float(x) for x in golden[f"{name}/params"])
+    sig = bool(sig)
+    m = lib.MultiAspectRetrieval(D=D, d_A=d_A, S=S, d_k=d_k, N=N, device=dev, dtype=torch.bfloat16)
+    m.W_Q = to_dev_bf16(golden[f"{name}/W_Q"])
+    m.W_K = to_dev_bf16(golden[f"{name}/W_K"])
+    m.aspect_logits = torch.from_numpy(golden[f"{name}/aspect_logits"]).to(dev)
+    m.tau = torch.from_numpy(golden[f"{name}/tau_param"]).to(dev)
+    z = to_dev_bf16(golden[f"{name}/z"])
+    vectors = to_dev_bf16(golden[f"{name}/vectors"])
+    p = m.hybrid_parts(z, vectors, k, T, lam, sig)
+    alpha, idx, sims_seq, raw_seq = m.hybrid_forward(z, vectors, k, T, lam, sig)
+    torch.cuda.synchronize()
+    assert alpha.shape == (B, seq, k) and idx.shape == (B, seq, k)
+    assert sims_seq.shape == (B, N) and raw_seq.shape == (B, N)
+    qf = p.queries_flat.float().cpu().numpy()
+    kp = p.keys_w.float().cpu().numpy()
+    errs = O.compare_topk(p.top_vals.cpu().numpy(), p.top_idx.reshape(-1, k).cpu().numpy(),
+                          golden[f"{name}/top_vals"].reshape(-1, k),
+                          golden[f"{name}/idx"].reshape(-1, k), qf, kp, lam, float(p.tau), T, sig,
+                          rtol=RTOL)
+    assert errs == [], errs
+    np.testing.assert_allclose(alpha.cpu().numpy(), golden[f"{name}/alpha"], rtol=RTOL, atol=1e-4)
+    np.testing.assert_allclose(sims_seq.cpu().numpy(), golden[f"{name}/sims_seq"], rtol=RTOL,
+                               atol=1e-3)
+    np.testing.assert_allclose(raw_seq.cpu().numpy(), golden[f"{name}/alpha_raw_seq"], rtol=RTOL)
+    # the second call (no state kept between calls) returns the same selection
+    assert torch.equal(idx, p.top_idx)
+
+
+@pytest.mark.parametrize("B,seq,N,d,k,sig", [(4, 256, 20000, 512, 16, True),
+                                             (3, 96, 9000, 2048, 32, False),
+                                             (2, 300, 5000, 256, 64, True)])
+def test_score_topk_seqmean_vs_fp64(lib, B, seq, N, d, k, sig):
+    """The fused seq-mean epilogue (dwa_score_topk_seqmean) against fp64 means of
+    every (position, key) score on the same bf16 inputs, and its top-k output
+    equal to dwa_score_topk_dev's (the epilogue only adds work)."""
+    dev = _dev()
+    M = B * seq
+    q = lib.new_normal(M, d, seed=d + seq, stddev=d ** -0.5, device=dev)
+    keys = lib.new_normal(N, d, seed=N + k, stddev=d ** -0.5, device=dev)
+    lam, tau, T = 3.0, 0.05, 0.6
+    tv, ti, mean = lib.score_topk_seqmean(q, keys, k, lam, tau, T, sig, seq)
+    params = lib.score_params(lam, tau, T, dev)
+    tv2, ti2 = lib.tiled_topk_fused(q, keys, k, params[0], params[1], params[2], sig)
+    torch.cuda.synchronize()
+    assert torch.equal(ti, ti2) and torch.equal(tv, tv2)
+    s = q.double() @ keys.double().T
+    v = torch.exp(s / T)
+    if sig:
+        v = v * torch.sigmoid(lam * (s - tau))
+    want = v.view(B, seq, N).mean(1)
+    torch.testing.assert_close(mean.double(), want, rtol=1e-4, atol=0)

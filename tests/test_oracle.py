@@ -198,3 +198,21 @@ def test_lowrank_delta_catches_planted_factor_swap(golden):
     swapped[:, :nU], swapped[:, nU:2 * nU] = c["vectors"][:, nU:2 * nU], c["vectors"][:, :nU]
     bad = O.lowrank_delta(c["h"], c["alpha"], c["idx"], swapped, d_A, d_B, r)
     assert np.abs(bad - good).max() > 1e-2 * np.abs(good).max()
+
+
+@pytest.mark.parametrize("name", ["hybrid_gate", "hybrid_exp"])
+def test_oracle_hybrid_forward_matches_reference(golden, name):
+    """oracle.hybrid_forward against the reference's own hybrid_forward run
+    (retrieval.py:131-181): identical indices, values and means within 1e-5."""
+    B, seq, d_A, S, d_k, k, N, D = (int(x) for x in golden[f"{name}/dims"])
+    lam, T, sig = golden[f"{name}/params"]
+    alpha, idx, sims_seq, raw_seq, top_vals = O.hybrid_forward(
+        O.bits_to_f32(golden[f"{name}/z"]), O.bits_to_f32(golden[f"{name}/vectors"]),
+        O.bits_to_f32(golden[f"{name}/W_Q"]), O.bits_to_f32(golden[f"{name}/W_K"]),
+        golden[f"{name}/aspect_logits"], golden[f"{name}/tau_param"], k, float(T), float(lam),
+        bool(sig))
+    np.testing.assert_array_equal(idx, golden[f"{name}/idx"])
+    np.testing.assert_allclose(top_vals, golden[f"{name}/top_vals"], rtol=1e-5)
+    np.testing.assert_allclose(alpha, golden[f"{name}/alpha"], rtol=1e-5, atol=1e-7)
+    np.testing.assert_allclose(sims_seq, golden[f"{name}/sims_seq"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(raw_seq, golden[f"{name}/alpha_raw_seq"], rtol=1e-5)
