@@ -167,8 +167,24 @@ def cpu_sample(keys_rows_fn, n_total, d, k, q_host, use_sigmoid, chunk_rows=1310
     return t_cpu, alpha, best_i
 
 
+def _jax_probe() -> str:
+    """Whether the reference's own runtime (JAX) exists on this host."""
+    try:
+        import jax  # noqa: F401
+
+        return f"jax {jax.__version__} importable (the reference source is not on this host)"
+    except Exception:
+        return "absent"
+
+
 def run_reference(args, wl):
-    """--impl reference: NumPy restatement of the reference's CPU path, host cores."""
+    """--impl reference: NumPy restatement of the reference's CPU path, host cores.
+
+    Each step scores ``--cpu-queries`` sampled queries against a contiguous
+    slice of the pool sized so that all warm-up + timed steps end in about
+    ``--reference-budget-s`` seconds; the per-step time is scaled to the whole
+    pool linearly in pool rows (the scan's cost is proportional to the rows it
+    reads), so the line reports full-pool queries/s."""
     import numpy as np
 
     rank = int(os.environ.get("RANK", "0"))
@@ -178,43 +194,53 @@ def run_reference(args, wl):
     M, N, d, k = wl["M"], wl["N"], wl["d"], wl["k"]
     mq = args.cpu_queries
     rng = np.random.default_rng(0)
-    t0 = time.perf_counter()
-    # pool generated once on the host (bf16-rounded float32), untimed
     from oracle import dwa_oracle as O
 
-    chunk = 131072
-    keys = np.empty((N, d), dtype=np.float32)
-    values = np.empty((N, d), dtype=np.float32)
-    for r0 in range(0, N, chunk):
-        r1 = min(N, r0 + chunk)
-        keys[r0:r1] = O.bf16_round(rng.standard_normal((r1 - r0, d), dtype=np.float32)
-                                   / np.float32(np.sqrt(d)))
-        values[r0:r1] = O.bf16_round(rng.standard_normal((r1 - r0, d), dtype=np.float32))
-    gen_s = time.perf_counter() - t0
-    step_times = []
-    for step in range(args.warmup + args.steps):
+    def make_rows(n):
+        keys = O.bf16_round(rng.standard_normal((n, d), dtype=np.float32) / np.float32(np.sqrt(d)))
+        values = O.bf16_round(rng.standard_normal((n, d), dtype=np.float32))
+        return keys, values
+
+    def step(keys, values):
         q = O.bf16_round(rng.standard_normal((mq, d), dtype=np.float32))
-        t_cpu, alpha, idx = cpu_sample(lambda a, b: keys[a:b], N, d, k, q, wl["use_sigmoid"])
+        t_cpu, alpha, idx = cpu_sample(lambda a, b: keys[a:b], keys.shape[0], d, k, q,
+                                       wl["use_sigmoid"])
         t0 = time.perf_counter()
         O.weighted_sum(alpha, idx, values, accum=np.float32)
-        t_cpu += time.perf_counter() - t0
-        if step >= args.warmup:
-            step_times.append(t_cpu)
+        return t_cpu + time.perf_counter() - t0
+
+    # calibrate on a small slice, then size the slice of the timed steps
+    n_cal = min(N, max(k, 65536))
+    keys, values = make_rows(n_cal)
+    t_cal = step(keys, values) * N / n_cal
+    n_steps = args.warmup + args.steps
+    frac = min(1.0, args.reference_budget_s / max(1e-9, n_steps * t_cal))
+    n_s = int(min(N, max(k, frac * N)))
+    t0 = time.perf_counter()
+    keys, values = make_rows(n_s)   # pool sample generated once on the host, untimed
+    gen_s = time.perf_counter() - t0
+    step_times = []
+    for i in range(n_steps):
+        t = step(keys, values)
+        if i >= args.warmup:
+            step_times.append(t * N / n_s)
     per_step = sum(step_times) / len(step_times)
     qps = mq / per_step
+    sample = (f"{mq} queries per step against a {n_s}-row slice of the {N}-row pool, time scaled "
+              f"to the full pool linearly in rows (NumPy restatement of tiled_topk_fallback + "
+              f"normalise + gather-sum; pool slice generation {gen_s:.1f}s untimed)")
     line = {
         "impl": "reference", "metric": METRIC, "value": qps, "unit": "queries/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32 (bf16-valued inputs)", "data": "synthetic",
         "config": {"workload": args.workload, "M": M, "N": N, "d": d, "k": k,
-                   "desc": wl["desc"], "sample_queries_per_step": mq},
+                   "desc": wl["desc"], "sample_queries_per_step": mq, "sample_pool_rows": n_s},
         "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": threads, "kind": "port",
-                         "sample": f"{mq} queries per step against the full {N}-row pool "
-                                   f"(NumPy restatement of tiled_topk_fallback + normalise + "
-                                   f"gather-sum; pool generation {gen_s:.1f}s untimed)"},
+                         "sample": sample},
         "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
+        "jax": _jax_probe(),
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -382,7 +408,7 @@ def run_ours(args, wl):
         line["key_projection"] = measure_key_projection(world, rank, local_rank)
     if args.lm:
         names = [n for n in args.lm.split(",") if n and (n != "small_char" or world == 1)]
-        line["lm"] = [measure_lm(n, world, rank, local_rank) for n in names]
+        line["lm"] = [measure_lm(n, world, rank, local_rank, group) for n in names]
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -501,7 +527,7 @@ def measure_key_projection(world, rank, local_rank, warmup=2, steps=5):
                          "frac": flops / (ms * 1e-3) / 1e12 / burst, "flops_per_launch": flops}}
 
 
-def measure_lm(cfg_name, world, rank, local_rank, warmup=3, steps=3):
+def measure_lm(cfg_name, world, rank, local_rank, group=None, warmup=3, steps=3):
     """DWA LM forward tokens/s (all ranks run the same forward; the pool is row-sharded)."""
     import torch
     import torch.distributed as dist
@@ -509,15 +535,25 @@ def measure_lm(cfg_name, world, rank, local_rank, warmup=3, steps=3):
     import computd_b200 as cb
     from computd_b200 import dwa_lm
 
-    cfg = {"small_char": dwa_lm.SMALL_CHAR, "large_1b": dwa_lm.LARGE_1B}[cfg_name]
+    cfg = dwa_lm.CONFIGS[cfg_name]
+    if cfg_name == "large_7b":
+        if world < 4:
+            # 16,777,216 rows x 4096 of keys and of values: 256 GiB, more than one or two B200s
+            return {"config": cfg_name, "skipped": "the 256 GiB pool needs 4 or more GPUs"}
+        steps = 2  # ~8.6 s (8 GPUs) to ~17 s (4 GPUs) per forward; warm-up stays at 3
     dev = torch.device("cuda", local_rank)
     spec = cb.ShardSpec(cfg.pool_rows, rank, world)
-    std = cfg.d_model ** -0.5
-    keys = cb.new_normal(spec.n_local, cfg.d_model, seed=31, stddev=std, row_offset=spec.row_begin,
-                         device=dev)
-    values = cb.new_normal(spec.n_local, cfg.d_model, seed=32, stddev=std,
-                           row_offset=spec.row_begin, device=dev)
-    model = dwa_lm.DWALM(cfg, keys, values)
+    if cfg.r > 0:
+        # the reference's pool: N(0, 1) * 0.02 rows of [U | V | b] (pool.py:34, 39)
+        keys = None
+        values = cb.new_normal(spec.n_local, cfg.D, seed=33, stddev=0.02,
+                               row_offset=spec.row_begin, device=dev)
+    else:
+        keys = cb.new_normal(spec.n_local, cfg.key_width, seed=31, stddev=cfg.key_width ** -0.5,
+                             row_offset=spec.row_begin, device=dev)
+        values = cb.new_normal(spec.n_local, cfg.d_model, seed=32, stddev=cfg.d_model ** -0.5,
+                               row_offset=spec.row_begin, device=dev)
+    model = dwa_lm.DWALM(cfg, keys, values, group=group if world > 1 else None)
     g = torch.Generator(device=dev)
     g.manual_seed(7)
     tokens = torch.randint(0, cfg.vocab, (cfg.batch, cfg.seq_len), device=dev, generator=g)
@@ -543,12 +579,19 @@ def measure_lm(cfg_name, world, rank, local_rank, warmup=3, steps=3):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t[0])
-    d, n_tok = cfg.d_model, cfg.tokens
-    retr = cfg.n_layers * 2.0 * n_tok * spec.n_local * d
-    dense = n_tok * (cfg.n_layers * (12.0 * d * d + 2.0 * cfg.seq_len * d)
-                     + 8.0 * d * d + 8.0 * d * cfg.vocab)
+    d, n_tok, kw = cfg.d_model, cfg.tokens, cfg.key_width
+    # tensor-core work per forward on one GPU: the fused score GEMM over this
+    # GPU's shard, the key projection of the shard (r > 0), and the dense
+    # layers (QKV + proj 8 d^2, query_proj 2 d^2, aspect query projection
+    # 2 d S d_k, W_base 2 d^2 per token; attention 4 seq d; PartA 2 d^2,
+    # PartB 8 d^2 + 8 d vocab).  HBM-bound parts (gathers, low-rank delta) are
+    # not in the bound.
+    retr = cfg.n_layers * 2.0 * n_tok * spec.n_local * kw
+    keyproj = cfg.n_layers * 2.0 * spec.n_local * kw * cfg.D if cfg.r > 0 else 0.0
+    dense = n_tok * (cfg.n_layers * (12.0 * d * d + 2.0 * d * kw + 4.0 * cfg.seq_len * d)
+                     + 10.0 * d * d + 8.0 * d * cfg.vocab)
     burst = _peaks()[0]
-    t_roof = (retr + dense) / (burst * 1e12)
+    t_roof = (retr + keyproj + dense) / (burst * 1e12)
     status = model.retriever.status()
     graphed = fwd is not model
     del fwd, model, keys, values
@@ -557,9 +600,12 @@ def measure_lm(cfg_name, world, rank, local_rank, warmup=3, steps=3):
             "unit": "tokens/s", "ms_per_forward": ms, "tokens_per_forward": n_tok,
             "layers": cfg.n_layers, "d_model": d, "pool_rows": cfg.pool_rows,
             "pool_rows_per_gpu": spec.n_local, "top_k": cfg.top_k,
+            "aspects": cfg.S, "d_k": cfg.d_k, "lowrank_r": cfg.r,
+            "pool_layout": ("reference [U|V|b] rows, keys projected per block and forward"
+                            if cfg.r > 0 else "packed keys [N, S d_k] + value rows [N, d]"),
             "roofline": {"t_roof_ms": t_roof * 1e3, "frac": t_roof * 1e3 / ms,
-                         "flops_retrieval_per_gpu": retr, "flops_dense": dense,
-                         "peak": "bf16 burst (MEASURED_PEAKS.json)"},
+                         "flops_retrieval_per_gpu": retr, "flops_key_projection_per_gpu": keyproj,
+                         "flops_dense": dense, "peak": "bf16 burst (MEASURED_PEAKS.json)"},
             "warmup": warmup, "steps": steps, "device_status": status,
             "cuda_graph": graphed}
 
@@ -594,20 +640,25 @@ def _cpu_baseline(args, wl, keys_dev, values_dev, q_dev):
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=320,
+                    help="timed steps (the default gives a timed region of ~4 s at one GPU, "
+                         ">= 20 clock samples)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="op_at_scale")
     ap.add_argument("--cpu-queries", type=int, default=64,
                     help="queries per CPU sample (CPU baseline / reference arm)")
+    ap.add_argument("--reference-budget-s", type=float, default=60.0,
+                    help="CPU seconds the reference arm spends on all its steps")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-assembly", action="store_true",
                     help="skip the WeightAssembler (low-rank consumer) measurement")
     ap.add_argument("--shape", default="",
                     help="MxNxDxK: run the chosen workload's step at these sizes instead "
                          "(profiling and sweeps; the workload is then named by its sizes)")
-    ap.add_argument("--lm", default="small_char,large_1b",
-                    help="DWA LM forwards to time after the op (comma list; empty to skip)")
+    ap.add_argument("--lm", default="small_char,ref_1b,large_1b,large_7b",
+                    help="DWA LM forwards to time after the op (comma list; empty to skip); "
+                         "large_7b runs on 4 or more GPUs")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -164,6 +164,12 @@ class WeightAssembler:
                               self.d_B, self.r, row_begin=rank * n_local)
         if world > 1:
             dist.all_reduce(delta, group=group)
+        return self.finish(h, delta).reshape(*lead, self.d_B)
+
+    def finish(self, h: torch.Tensor, delta: torch.Tensor) -> torch.Tensor:
+        """LayerNorm(residual + gamma * (h W_base^T + b_base + delta)) (assembly.py:128)
+        for h [M, d_A] and the summed delta f32 [M, d_B] of the retrieved rows
+        (h_delta + b_delta; b_delta alone when the pool rows hold only b)."""
         if h.dtype == torch.bfloat16 and self.W_base.dtype == torch.bfloat16:
             # bf16 operands, fp32 result: the tensor-core GEMM (exact products, fp32 sums)
             base = torch.mm(h, self.W_base.t(), out_dtype=torch.float32)
@@ -172,6 +178,5 @@ class WeightAssembler:
             base = torch.addmm(self.b_base.to(torch.float32), h.to(torch.float32),
                                self.W_base.to(torch.float32).t())
         residual = h if self.d_A == self.d_B else None
-        out = assemble_finish(delta, base, residual, self.gamma, self.norm_scale, self.norm_bias,
-                              self.eps)
-        return out.reshape(*lead, self.d_B)
+        return assemble_finish(delta, base, residual, self.gamma, self.norm_scale, self.norm_bias,
+                               self.eps)

@@ -71,19 +71,23 @@ def weighted_value_sum(top_vals: torch.Tensor, top_idx: torch.Tensor, values: to
     return out, alpha
 
 
-def normalise_alpha(top_vals: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+def normalise_alpha(top_vals: torch.Tensor, out: torch.Tensor | None = None,
+                    idx: torch.Tensor | None = None) -> torch.Tensor:
     """alpha = top_vals / (sum(top_vals) + 1e-8) over the last axis (reference retrieval.py:326),
-    computed by the gather kernel with an empty owned row range (no value rows read)."""
+    computed by the gather kernel with an empty owned row range (no value rows read).
+    ``idx`` (i32 [M, k], e.g. the top-k indices) fills the kernel's index operand; it
+    is not read for values."""
     if top_vals.dim() != 2:
         raise ValueError("top_vals must be [M, k]")
     top_vals = top_vals.to(torch.float32).contiguous()
     M, k = top_vals.shape
     if out is None:
         out = torch.empty((M, k), dtype=torch.float32, device=top_vals.device)
+    if idx is None or idx.shape != top_vals.shape or idx.dtype != torch.int32:
+        idx = torch.zeros((M, k), dtype=torch.int32, device=top_vals.device)
     lib = _lib.load()
-    dummy_idx = torch.zeros((M, k), dtype=torch.int32, device=top_vals.device)
     with torch.cuda.device(top_vals.device):
-        st = lib.dwa_weighted_gather(top_vals.data_ptr(), dummy_idx.data_ptr(), M, k, None, 0, 0,
-                                     8, 8, None, out.data_ptr(), _stream_handle(top_vals.device))
+        st = lib.dwa_weighted_gather(top_vals.data_ptr(), idx.contiguous().data_ptr(), M, k, None, 0,
+                                     0, 8, 8, None, out.data_ptr(), _stream_handle(top_vals.device))
     _lib.check(st, "dwa_weighted_gather")
     return out

@@ -1,25 +1,45 @@
 """DWA language model forward — the call site of the retrieval path.
 
 Mirrors the reference's ``DWAModel`` / ``DWABlock`` (src/model/dwa.py:77-216)
-to measure the path inside a model (tokens/s):
+to measure the path inside a model (tokens/s).  Each block composes the
+reference's own pieces in the reference's order (dwa.py:100-130):
 
-    h = PartA(tokens)                                  parts.py:88-143 (embedding + proj + LayerNorm)
-    for each block (dwa.py:100-130):
-        h = h + attn(LayerNorm(h))                      parts.py:30-83 (causal, RoPE)
-        z = query_proj(h)                               dwa.py:105
-        top_vals, top_idx = retrieval(z, pool keys)     retrieval.py:204-343 (this repo's kernels)
-        alpha, b_delta = normalise + gathered sum       retrieval.py:326, assembly.py:104,127
-        h = LayerNorm(h + gamma * (h W_base^T + b_base + b_delta))   assembly.py:130
-    logits = PartB(h)                                   parts.py:146-176
+    h = PartA(tokens)                                   parts.py:88-143
+    for each block:
+        h = attn(h)                                      dwa.py:101-102, parts.py:30-83
+        z = query_proj(h)                                dwa.py:103
+        alpha, idx = MultiAspectRetrieval(z, pool)       retrieval.py:131-181 (hybrid layout)
+        h = WeightAssembler(h, alpha, idx, pool)         dwa.py:129, assembly.py:75-128
+    logits = PartB(h)                                    parts.py:146-176
 
-The pool is one (keys, values) pair shared by every block, as the reference
-shares ``pool.vectors`` (dwa.py:182,195), optionally row-sharded over a
-process group (one retrieval all-gather + merge + value all-reduce per block).
-Differences from the reference, by scope: the query/key aspect projections of
-``MultiAspectRetrieval`` are folded into ``query_proj`` (the pool keys are
-taken as already projected), and the low-rank U.V assembly term (``h_delta``)
-is not computed (a "next" item).  Dense layers are plain torch/cuBLAS; all
-retrieval work runs in libdwa_b200.so.
+Retrieval (``MultiAspectRetrieval`` parameters W_Q [S, d_k, d], aspect_logits
+and tau, retrieval.py:22-44): the per-position queries are projected per
+aspect, L2-normalised and packed as [sqrt(w_s) q_s]_s (d = S d_k), so that one
+dot product with the packed pool keys [sqrt(w_s) k_s]_s is hybrid_forward's
+aspect-weighted score sum_s w_s <q_s, k_s> (retrieval.py:154-165); the fused
+score + top-k kernel keeps the k best per position (retrieval.py:175) and
+alpha = v / (sum v + 1e-8) (178).
+
+The pool comes in one of two layouts:
+
+* ``r > 0`` (the reference's own layout, configs/large_1b.py): pool vectors
+  [N, D] hold [U (d r) | V (r d) | b (d)] rows (assembly.py:10-14).  Each
+  block projects its pool keys from them with its own W_K [S, d_k, D]
+  (retrieval.py:155-156: one tcgen05 launch per block and forward, as the
+  reference's training forward recomputes them), and the WeightAssembler adds
+  h_delta + b_delta = sum_j alpha_j (U_j (V_j h) + b_j) (assembly.py:104-128,
+  ``dwa_lowrank_delta``) before LayerNorm(h + gamma (h W_base^T + b_base + .)).
+* ``r == 0`` (the benchmark layouts: a synthetic [N, S d_k] key pool standing
+  in for the cached packed keys, and value rows [N, d]): the retrieved value
+  rows are the b vectors of the WeightAssembler formula, b_delta =
+  sum_j alpha_j V_j (the gathered weighted sum, ``dwa_weighted_gather``), with
+  no low-rank term.
+
+The pool is shared by every block (dwa.py:182, 195) and optionally row-sharded
+over a process group (one cross-shard merge per block, owner-computes value
+sums).  Dense layers (attention, projections, PartA/PartB) are plain
+torch/cuBLAS; retrieval, key projection, assembly delta and its LayerNorm
+finish run in libdwa_b200.so.
 """
 from __future__ import annotations
 
@@ -30,7 +50,9 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .retrieval import Retriever
+from .assembler import WeightAssembler
+from .retrieval import MultiAspectRetrieval, Retriever, project_keys_packed
+from .tiled_topk import score_params
 
 
 @dataclass(frozen=True)
@@ -43,6 +65,9 @@ class DWALMConfig:
     batch: int
     pool_rows: int
     top_k: int
+    S: int                    # retrieval aspects; S * d_k is the packed key width
+    d_k: int
+    r: int = 0                # low-rank assembly rank (0: value rows only)
     T: float = 1.0
     lambda_sharp: float = 1.0
     use_sigmoid: bool = False
@@ -51,14 +76,32 @@ class DWALMConfig:
     def tokens(self) -> int:
         return self.batch * self.seq_len
 
+    @property
+    def key_width(self) -> int:
+        return self.S * self.d_k
 
-# Shapes of the benchmark configurations.
+    @property
+    def D(self) -> int:
+        """Pool row width: [U | V | b] for r > 0, the value rows (d) otherwise."""
+        d = self.d_model
+        return 2 * d * self.r + d if self.r > 0 else d
+
+
+# Benchmark configurations (BASELINE.json): keys [N, d] with d = S d_k, values [N, d].
 SMALL_CHAR = DWALMConfig(vocab=65, d_model=384, n_layers=6, n_heads=6, seq_len=256, batch=16,
-                         pool_rows=65536, top_k=32)
+                         pool_rows=65536, top_k=32, S=6, d_k=64)
 LARGE_1B = DWALMConfig(vocab=32000, d_model=2048, n_layers=24, n_heads=16, seq_len=2048, batch=8,
-                       pool_rows=4194304, top_k=64)
+                       pool_rows=4194304, top_k=64, S=16, d_k=128)
 LARGE_7B = DWALMConfig(vocab=32000, d_model=4096, n_layers=32, n_heads=32, seq_len=4096, batch=4,
-                       pool_rows=16777216, top_k=128)
+                       pool_rows=16777216, top_k=128, S=32, d_k=128)
+# The reference's own 1B model (configs/large_1b.py:31-70): d_A = d_B = 1280,
+# pool 16384 x 21760 ([U | V | b], r = 8), k_max 16, S = 8 aspects of d_k = 64,
+# 16 heads, 12 assembly layers, seq 1024 (batch 8), vocab 64400.
+REF_1B = DWALMConfig(vocab=64400, d_model=1280, n_layers=12, n_heads=16, seq_len=1024, batch=8,
+                     pool_rows=16384, top_k=16, S=8, d_k=64, r=8)
+
+CONFIGS = {"small_char": SMALL_CHAR, "large_1b": LARGE_1B, "large_7b": LARGE_7B,
+           "ref_1b": REF_1B}
 
 
 def _rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
@@ -95,40 +138,78 @@ class CausalSelfAttention(nn.Module):
 
 
 class DWABlock(nn.Module):
-    """dwa.py:77-130 with the retrieval and gathered sum on this repo's kernels."""
+    """dwa.py:77-130: attention, query_proj, MultiAspectRetrieval (hybrid layout) on
+    this repo's kernels, WeightAssembler."""
 
-    def __init__(self, cfg: DWALMConfig, device, dtype):
+    def __init__(self, cfg: DWALMConfig, device, dtype, group=None, seed: int = 0):
         super().__init__()
         d = cfg.d_model
+        self.cfg = cfg
+        self.group = group
         self.attn = CausalSelfAttention(d, cfg.n_heads, cfg.seq_len, device, dtype)
-        self.query_proj = nn.Linear(d, d, device=device, dtype=dtype)
-        self.W_base = nn.Linear(d, d, device=device, dtype=dtype)      # h_base (assembly.py:128)
-        self.gamma = nn.Parameter(torch.ones((), device=device, dtype=dtype))
-        self.norm = nn.LayerNorm(d, device=device, dtype=dtype)
+        self.query_proj = nn.Linear(d, d, device=device, dtype=dtype)        # dwa.py:87-96
+        self.retrieval = MultiAspectRetrieval(D=cfg.D if cfg.r > 0 else 8, d_A=d, S=cfg.S,
+                                              d_k=cfg.d_k, N=cfg.pool_rows, device=device,
+                                              dtype=dtype, seed=seed)
+        if cfg.r == 0:
+            self.retrieval.W_K = None  # the key pool is given (cached packed keys)
+        self.assembler = WeightAssembler(d, d, cfg.r, device=device)       # dwa.py:98
+        # the retrieval's runtime scalars on the device (tau = w . tau, retrieval.py:168)
+        self._params = torch.empty(3, dtype=torch.float32, device=device)
 
-    def forward(self, h: torch.Tensor, retriever: Retriever) -> torch.Tensor:
-        B, S, C = h.shape
+    def queries(self, z: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """([sqrt(w_s) q_s / (|q_s| + 1e-8)]_s packed per position, bf16 [B * seq, S d_k];
+        w = softmax(aspect_logits))
+        (retrieval.py:159-160 with the aspect weights folded in)."""
+        B, S_len, C = z.shape
+        w = torch.softmax(self.retrieval.aspect_logits.float(), dim=0)
+        q = torch.einsum("btd,skd->btsk", z, self.retrieval.W_Q)
+        qf = q.float()
+        qf = qf * (w.sqrt()[None, None, :, None] /
+                   (torch.linalg.vector_norm(qf, dim=-1, keepdim=True) + 1e-8))
+        return qf.reshape(B * S_len, -1).to(torch.bfloat16), w
+
+    def forward(self, h: torch.Tensor, retriever: Retriever,
+                vectors: torch.Tensor | None = None) -> torch.Tensor:
+        B, S_len, C = h.shape
+        cfg = self.cfg
         h = self.attn(h)
-        z = self.query_proj(h).reshape(B * S, C)
-        out, alpha, _, _ = retriever(z)                  # fused score+top-k, merge, gathered sum
-        b_delta = out.view(B, S, -1).to(h.dtype)
-        return self.norm(h + self.gamma * (self.W_base(h) + b_delta))
+        z = self.query_proj(h)
+        q, w = self.queries(z)
+        tau = (torch.dot(w, self.retrieval.tau.float()) if cfg.use_sigmoid
+               else torch.zeros((), dtype=torch.float32, device=w.device))
+        self._params.copy_(score_params(cfg.lambda_sharp, tau, cfg.T, h.device))
+        if cfg.r > 0:
+            # this block's pool keys from the pool vectors (retrieval.py:155-156)
+            project_keys_packed(vectors, self.retrieval.W_K, w, out=retriever.keys)
+        out, alpha, _, idx = retriever(q, params=self._params)
+        hf = h.reshape(B * S_len, C)
+        if cfg.r > 0:
+            h_mid = self.assembler(hf, alpha, idx, vectors, group=self.group)    # dwa.py:129
+        else:
+            h_mid = self.assembler.finish(hf, out)                              # b_delta = out
+        return h_mid.view(B, S_len, C).to(h.dtype)
 
 
 class DWALM(nn.Module):
-    """dwa.py:133-216 forward: PartA -> DWABlocks over one shared pool -> PartB."""
+    """dwa.py:133-216 forward: PartA -> DWABlocks over one shared pool -> PartB.
 
-    def __init__(self, cfg: DWALMConfig, pool_keys: torch.Tensor, pool_values: torch.Tensor,
+    ``r == 0``: ``pool_keys`` [N_local, S d_k] and ``pool_values`` [N_local, d].
+    ``r > 0``: ``pool_values`` are the pool vectors [N_local, D] and ``pool_keys``
+    must be None (each block projects its own keys every forward)."""
+
+    def __init__(self, cfg: DWALMConfig, pool_keys: torch.Tensor | None, pool_values: torch.Tensor,
                  group=None, dtype=torch.bfloat16, seed: int = 0):
         super().__init__()
-        device = pool_keys.device
+        device = pool_values.device
         torch.manual_seed(seed)
         d = cfg.d_model
         self.cfg = cfg
         self.embed = nn.Embedding(cfg.vocab, d, device=device, dtype=dtype)   # PartA (parts.py:97-98)
         self.embed_proj = nn.Linear(d, d, bias=False, device=device, dtype=dtype)
         self.embed_norm = nn.LayerNorm(d, device=device, dtype=dtype)
-        self.blocks = nn.ModuleList(DWABlock(cfg, device, dtype) for _ in range(cfg.n_layers))
+        self.blocks = nn.ModuleList(DWABlock(cfg, device, dtype, group, seed=seed * 1000 + i)
+                                    for i in range(cfg.n_layers))
         self.head_norm = nn.LayerNorm(d, device=device, dtype=dtype)        # PartB (parts.py:146-176)
         self.fc1 = nn.Linear(d, 4 * d, device=device, dtype=dtype)
         self.fc2 = nn.Linear(4 * d, cfg.vocab, device=device, dtype=dtype)
@@ -137,10 +218,21 @@ class DWALM(nn.Module):
                 nn.init.normal_(m.weight, std=math.sqrt(2.0 / m.in_features))
                 if m.bias is not None:
                     nn.init.zeros_(m.bias)
-        for blk in self.blocks:  # W_base starts at zero (assembly.py:37-39)
-            nn.init.zeros_(blk.W_base.weight)
+        if cfg.r > 0:
+            if pool_keys is not None:
+                raise ValueError("with r > 0 the blocks project their own keys: pass pool_keys=None")
+            self.vectors = pool_values
+            # one key buffer, rewritten by each block's projection before its retrieval
+            pool_keys = torch.empty((pool_values.shape[0], cfg.key_width), dtype=torch.bfloat16,
+                                    device=device)
+            values = None
+        else:
+            if pool_keys is None or pool_keys.shape[1] != cfg.key_width:
+                raise ValueError(f"pool_keys must be [N, {cfg.key_width}]")
+            self.vectors = None
+            values = pool_values
         # one retrieval plan shared by all blocks (same pool, same token count)
-        self.retriever = Retriever(pool_keys, pool_values, cfg.tokens, cfg.top_k,
+        self.retriever = Retriever(pool_keys, values, cfg.tokens, cfg.top_k,
                                    lambda_sharp=cfg.lambda_sharp, T=cfg.T,
                                    use_sigmoid=cfg.use_sigmoid, group=group)
 
@@ -148,7 +240,7 @@ class DWALM(nn.Module):
     def forward(self, token_ids: torch.Tensor) -> torch.Tensor:
         h = self.embed_norm(self.embed_proj(self.embed(token_ids)))
         for blk in self.blocks:
-            h = blk(h, self.retriever)
+            h = blk(h, self.retriever, self.vectors)
         return self.fc2(F.gelu(self.fc1(self.head_norm(h))))
 
 

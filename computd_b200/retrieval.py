@@ -358,8 +358,10 @@ class Retriever:
                  use_sigmoid: bool = False, group=None, exchange: str = "auto",
                  peer_wait_s: float = 30.0):
         self.keys = _as_bf16_rows(keys_local, "keys_local")
-        self.values = _check_values(values_local)
-        if self.values.shape[0] != self.keys.shape[0]:
+        # values_local None: top-k and alpha only (the caller consumes the indices
+        # itself, e.g. the low-rank WeightAssembler)
+        self.values = _check_values(values_local) if values_local is not None else None
+        if self.values is not None and self.values.shape[0] != self.keys.shape[0]:
             raise ValueError("keys_local and values_local must hold the same pool rows")
         self.group = group
         self.rank, self.world = _group_rank_world(group)
@@ -367,7 +369,7 @@ class Retriever:
         self.shard = ShardSpec(self.n_local * self.world, self.rank, self.world)
         self.M, self.k = int(M), int(k)
         self.d_k = self.keys.shape[1]
-        self.d_v = self.values.shape[1]
+        self.d_v = self.values.shape[1] if self.values is not None else 0
         self.lambda_sharp, self.tau, self.T = float(lambda_sharp), float(tau), float(T)
         self.use_sigmoid = bool(use_sigmoid)
         dev = self.keys.device
@@ -381,7 +383,7 @@ class Retriever:
         else:
             self.top_vals, self.top_idx = self.local_vals, self.local_idx
         self.alpha = torch.empty((self.M, self.k), dtype=f32, device=dev)
-        self.out = torch.empty((self.M, self.d_v), dtype=f32, device=dev)
+        self.out = (torch.empty((self.M, self.d_v), dtype=f32, device=dev) if self.d_v else None)
         nbytes = workspace_bytes(self.M, self.n_local, self.d_k, self.k, dev)
         if nbytes == 0:
             raise _lib.DWAArgumentError(_lib.DWA_ERR_UNSUPPORTED_SHAPE, "Retriever",
@@ -398,13 +400,13 @@ class Retriever:
         self.peer = None
         if use_peer and self.d_v % 8 == 0:
             try:
-                self.peer = PeerExchange(self.M, self.k, self.group, dev, d=self.d_v,
+                self.peer = PeerExchange(self.M, self.k, self.group, dev, d=self.d_v or None,
                                          wait_s=peer_wait_s)
             except _lib.DWAError:
                 # raised on every rank together; "auto" falls back to NCCL everywhere
                 if exchange == "nvlink":
                     raise
-        if self.peer is not None:
+        if self.peer is not None and self.d_v:
             self.out = self.peer.out  # the owners write the summed blocks straight into it
         if self.world > 1 and self.peer is None:
             self._packed_local = torch.empty((self.M, self.k, 2), dtype=i32, device=dev)
@@ -419,18 +421,23 @@ class Retriever:
         the four plus the cross-shard merge."""
         if self.world == 1:
             return 4
+        if self.values is None:
+            return 7 if self.peer is not None else 5
         return 10 if self.peer is not None else 5
 
-    def topk_local(self, queries: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    def topk_local(self, queries: torch.Tensor, params: torch.Tensor | None = None
+                   ) -> tuple[torch.Tensor, torch.Tensor]:
         """This rank's shard only: fused score + top-k and the split merge
-        (global indices), into ``local_vals`` / ``local_idx``."""
+        (global indices), into ``local_vals`` / ``local_idx``.  ``params``
+        (device f32 [3], ``score_params``) overrides the constructor's scalars
+        for this call and is read on the device (a learned tau needs no host sync)."""
         if tuple(queries.shape) != (self.M, self.d_k):
             raise ValueError(f"queries must be [{self.M}, {self.d_k}], got {tuple(queries.shape)}")
         if self.peer is not None:
             self.peer.check()  # raises if a cross-rank wait of an earlier call ran out
         score_topk_into(queries, self.keys, self.k, self.lambda_sharp, self.tau, self.T,
                         self.use_sigmoid, self.local_vals, self.local_idx, self.workspace,
-                        idx_offset=self.shard.row_begin)
+                        idx_offset=self.shard.row_begin, params=params)
         return self.local_vals, self.local_idx
 
     def exchange(self) -> None:
@@ -471,7 +478,11 @@ class Retriever:
         self.merge()
 
     def gather(self) -> None:
-        """Owner-computes alpha-weighted sum over this rank's pool rows."""
+        """Owner-computes alpha-weighted sum over this rank's pool rows (alpha only
+        when the retriever has no value rows)."""
+        if self.values is None:
+            normalise_alpha(self.top_vals, self.alpha, idx=self.top_idx)
+            return
         if self.peer is not None:
             self.peer.gather_partials(self.top_vals, self.top_idx, self.values, self.shard.row_begin,
                                       self.shard.row_end, self.alpha)
@@ -480,6 +491,8 @@ class Retriever:
                              self.shard.row_begin, self.shard.row_end)
 
     def reduce(self) -> None:
+        if self.values is None:
+            return
         if self.peer is not None:
             self.peer.reduce_broadcast()
             return
@@ -500,9 +513,10 @@ class Retriever:
         self.reduce()
         return self.out, self.alpha, self.top_vals, self.top_idx
 
-    def __call__(self, queries: torch.Tensor):
-        """Returns (out f32 [M, d_v], alpha f32 [M, k], top_vals f32 [M, k], top_idx i32 [M, k])."""
-        self.topk_local(queries)
+    def __call__(self, queries: torch.Tensor, params: torch.Tensor | None = None):
+        """Returns (out f32 [M, d_v] or None without value rows, alpha f32 [M, k],
+        top_vals f32 [M, k], top_idx i32 [M, k])."""
+        self.topk_local(queries, params)
         return self.finish()
 
     def status(self) -> int:

@@ -42,6 +42,20 @@ def test_reference_arm_line():
     e2e = d["e2e"]
     assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+    assert d["jax"]  # the probe of the reference's own runtime is recorded
+
+
+def test_reference_arm_stays_within_its_budget():
+    """The default 320 timed steps: each step scores a pool slice sized to the
+    budget, and the time is scaled to the full pool."""
+    import time
+
+    t0 = time.time()
+    d = _line(_run("--impl", "reference", "--workload", "c1_op", "--warmup", "3",
+                   "--cpu-queries", "8", "--reference-budget-s", "6"))
+    assert d["steps"] == 320
+    assert 0 < d["config"]["sample_pool_rows"] <= 16384
+    assert time.time() - t0 < 120
 
 
 def test_shape_override_names_the_workload_by_its_sizes():
