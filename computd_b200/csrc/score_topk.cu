@@ -8,8 +8,8 @@
 // which materialises the whole [M, N] score matrix before a sort-based top-k.
 // Here each [256 x 256] score tile lives only in tensor memory (TMEM); the
 // epilogue keeps the k best (score, index) per query row in registers (a
-// sorted list, k <= 64) or in a shared-memory heap (k = 128), so the full
-// score matrix never reaches HBM.
+// sorted list, k <= 64; for k > 64 the best 64 in registers and the rest in
+// a shared-memory heap), so the full score matrix never reaches HBM.
 //
 // Launch unit = a CTA pair (cluster of 2 on neighbouring SMs) running
 // tcgen05.mma.cta_group::2: one 256 x 256 x 16 MMA covers 256 query rows (128
@@ -57,6 +57,7 @@ namespace {
 constexpr int threads_for(int nwg) { return 64 + 128 * nwg; }
 constexpr int kMaxDynSmem = 232448;  // 227 KB opt-in limit on sm_100
 constexpr int kPairRows = 2 * kTileM;      // 256 query rows per CTA pair
+constexpr int64_t kSplitListMinWork = int64_t(1) << 20;  // key tiles x d per unit, see plan_score_topk
 constexpr int kKeysPerCta = kTileN / 2;    // 128 keys of each 256-key tile per CTA
 
 template <int KCAP, int NWG>
@@ -64,9 +65,12 @@ struct TopkCfg {
   static constexpr int kStageA = kTileM * kTileK * 2;       // 16 KB: this CTA's query rows
   static constexpr int kStageB = kKeysPerCta * kTileK * 2;  // 16 KB: this CTA's half of the keys
   static constexpr int kStageBytes = kStageA + kStageB;
-  // k <= 64 keeps its lists in registers; k = 128 uses one shared-memory heap
-  // per row per warpgroup
-  static constexpr int kHeapBytes = KCAP > 64 ? KCAP * kTileM * 8 * NWG : 0;
+  // k <= 64 keeps its lists in registers; the two-level list (KCAP 128) keeps
+  // ranks 65..128 in a shared-memory heap per row per warpgroup, the whole-heap
+  // variant (KCAP 129) all 128
+  static constexpr int kHeapBytes = KCAP == 129   ? 128 * kTileM * 8 * NWG
+                                    : KCAP > 64 ? (KCAP - 64) * kTileM * 8 * NWG
+                                                : 0;
   static constexpr int kBarBytes = 256;
   static constexpr int kStagesFit = (kMaxDynSmem - 1024 - kHeapBytes - kBarBytes) / kStageBytes;
   static constexpr int kStages = kStagesFit > 7 ? 7 : kStagesFit;
@@ -138,7 +142,56 @@ struct RegTopK {
   }
 };
 
-// Per-row top-k in a shared-memory heap, for KCAP = 128 (too many registers).
+// Per-row top-k for 64 < k <= 128 (KCAP = 128), in two levels: the best 64
+// in a register list (RegTopK<64>, the k <= 64 machinery) and ranks 65..k in a
+// min-heap of k - 64 entries in shared memory, whose root (the k-th best) is
+// the admission threshold.  Everything in the register list ranks above
+// everything in the heap: an entry enters the heap either because it does
+// not beat the list's 64th entry, or because a better entry pushed it out of
+// the list.  Keeping the best half in registers halves the shared memory the
+// lists take (64 KB per CTA instead of 128 KB), which buys the operand ring
+// two more stages.
+struct SplitTopK {
+  RegTopK<64> upper;
+  SmemHeap lower;  // k - 64 entries per row
+  int row;
+  __device__ __forceinline__ void init(int) {
+    upper.init(64);
+    lower.init(row);
+  }
+  __device__ __forceinline__ float worst() const { return lower.score(0, row); }
+  // (x, xi) must rank above the heap root (the caller's admission cut).
+  __device__ __forceinline__ void insert(float x, int32_t xi) {
+    if (x > upper.worst()) {
+      // x joins the register list; its old 64th entry drops to rank 65
+      const float es = upper.s[63];
+      const int32_t ei = upper.i[63];
+      upper.insert(x, xi);
+      float rs;
+      int32_t ri;
+      lower.load(0, row, rs, ri);
+      if (topk_worse(rs, ri, es, ei)) lower.replace_root(row, es, ei);
+    } else {
+      lower.replace_root(row, x, xi);
+    }
+  }
+  __device__ __forceinline__ void write_out(float* vs, int32_t* is, int k) const {
+    upper.write_out(vs, is, 64);
+    lower.sort_best_first(row);
+    for (int p = 0; p < k - 64; ++p) {
+      float hs;
+      int32_t hi;
+      lower.load(p, row, hs, hi);
+      vs[64 + p] = hs;
+      is[64 + p] = hi;
+    }
+  }
+};
+
+// Per-row top-k for 64 < k <= 128 wholly in a shared-memory heap (128 KB per
+// CTA, three ring stages).  Each insert is one sift-down, cheaper than the
+// two-level list's register network plus heap step, so it wins when a unit's
+// key range is short and its lists spend much of it filling up.
 struct HeapTopK {
   SmemHeap heap;
   int row;
@@ -157,12 +210,20 @@ struct HeapTopK {
   }
 };
 
+// KCAP values: 16, 32, 64 (register lists), 128 (two-level list) and
+// kCapHeap128 (k in (64, 128] in a whole shared-memory heap).
+constexpr int kCapHeap128 = 129;
+
 template <int KCAP>
 struct TopKFor {
   using type = RegTopK<KCAP>;
 };
 template <>
 struct TopKFor<128> {
+  using type = SplitTopK;
+};
+template <>
+struct TopKFor<kCapHeap128> {
   using type = HeapTopK;
 };
 
@@ -394,8 +455,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
     const int ew = warp & 3;           // TMEM lane quarter this warp may access
     const int row = ew * 32 + lane;    // query row within this CTA's 128
     typename TopKFor<KCAP>::type topk;
-    if constexpr (KCAP > 64) {
-      topk.heap = SmemHeap{heap0 + static_cast<uint32_t>(g * KCAP * kTileM * 8), kTileM, a.k};
+    if constexpr (KCAP == kCapHeap128) {
+      topk.heap = SmemHeap{heap0 + static_cast<uint32_t>(g * 128 * kTileM * 8), kTileM, a.k};
+      topk.row = row;
+    } else if constexpr (KCAP > 64) {
+      topk.lower = SmemHeap{heap0 + static_cast<uint32_t>(g * (KCAP - 64) * kTileM * 8), kTileM,
+                            a.k - 64};
       topk.row = row;
     }
     topk.init(a.k);
@@ -763,6 +828,15 @@ bool plan_score_topk(int64_t M, int64_t N, int d, int k, int num_sms, ScoreTopkP
   // units go in groups of G query tiles x all splits (G * n_split about the
   // resident pair count): G query tiles stay in L2 and each key tile is
   // read once per group.
+  // k in (64, 128]: the two-level list (five ring stages) when a unit's MMA
+  // work (key tiles x d) is long next to filling its lists; the whole-heap
+  // list (three stages, cheaper inserts) otherwise.  Measured, same indices:
+  // 16384 x 2,097,152 x 4096 (546-tile units) 241.5 vs 270.0 ms,
+  // 16384 x 262,144 x 4096 (128-tile units) 35.5 vs 35.4 ms,
+  // 8192 x 131,072 x 1024 (57-tile units) 5.71 vs 4.57 ms.
+  if (p.kcap == 128 &&
+      (p.n_kt + p.n_split - 1) / p.n_split * static_cast<int64_t>(d) < kSplitListMinWork)
+    p.kcap = 129;
   const int64_t query_bytes = p.m_pad * static_cast<int64_t>(p.num_kb) * kTileK * 2;
   p.group = 0;
   if (query_bytes > (64ll << 20)) {
@@ -851,10 +925,12 @@ cudaError_t launch_plan(const ScoreTopkPlan& p, const CUtensorMap& mq, const CUt
     case 32 * 8 + 4: return launch_variant<32, 2, false>(p, mq, mk, args, stream);
     case 64 * 8 + 2: return launch_variant<64, 1, false>(p, mq, mk, args, stream);
     case 128 * 8 + 2: return launch_variant<128, 1, false>(p, mq, mk, args, stream);
+    case 129 * 8 + 2: return launch_variant<129, 1, false>(p, mq, mk, args, stream);
     case 16 * 8 + 5: return launch_variant<16, 2, true>(p, mq, mk, args, stream);
     case 32 * 8 + 5: return launch_variant<32, 2, true>(p, mq, mk, args, stream);
     case 64 * 8 + 3: return launch_variant<64, 1, true>(p, mq, mk, args, stream);
     case 128 * 8 + 3: return launch_variant<128, 1, true>(p, mq, mk, args, stream);
+    case 129 * 8 + 3: return launch_variant<129, 1, true>(p, mq, mk, args, stream);
     default: return cudaErrorInvalidValue;
   }
 }

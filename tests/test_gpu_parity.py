@@ -473,3 +473,32 @@ def test_score_topk_seqmean_vs_fp64(lib, B, seq, N, d, k, sig):
         v = v * torch.sigmoid(lam * (s - tau))
     want = v.view(B, seq, N).mean(1)
     torch.testing.assert_close(mean.double(), want, rtol=1e-4, atol=0)
+
+
+@pytest.mark.parametrize("k", [100, 128])
+def test_exact_ties_two_level_list(lib, k):
+    """k > 64 over units whose key tiles x d reach 2^20 takes the two-level list
+    (best 64 in registers, the rest in a shared-memory heap).  18944 queries =
+    74 query tiles, one unit per CTA pair, each over all 2048 key tiles of
+    524,288 duplicated integer keys of width 512: every score is exact and ties
+    abound.  Every row's indices must equal lax.top_k's (values descending,
+    lower index first), computed on the GPU from composite integer keys
+    (score, -index)."""
+    dev = _dev()
+    M, N, d = 18944, 524288, 512
+    g = torch.Generator(device=dev).manual_seed(k)
+    q = torch.randint(-2, 3, (M, d), generator=g, device=dev).to(torch.bfloat16)
+    base = torch.randint(-2, 3, (N // 16, d), generator=g, device=dev).to(torch.bfloat16)
+    keys = base[torch.randint(0, N // 16, (N,), generator=g, device=dev)].contiguous()
+    T = 512.0  # |s| <= 2048: s / T is exact, exp(s / T) finite and strictly increasing in s
+    v, i = lib.tiled_topk_fused(q, keys, k, 1.0, 0.0, T, False)
+    torch.cuda.synchronize()
+    kf = keys.float()
+    ar = torch.arange(N, device=dev, dtype=torch.int64)
+    for r0 in range(0, M, 512):
+        s = (q[r0:r0 + 512].float() @ kf.T).to(torch.int64)     # exact integer scores
+        comp = s * (1 << 26) - ar                                # higher score, then lower index
+        ref = torch.topk(comp, k, dim=1, sorted=True).indices.to(torch.int32)
+        assert torch.equal(i[r0:r0 + 512], ref), r0
+        want_v = torch.exp(torch.gather(s, 1, ref.long()).double() / T).float()
+        torch.testing.assert_close(v[r0:r0 + 512], want_v, rtol=1e-6, atol=0)
