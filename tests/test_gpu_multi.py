@@ -139,6 +139,39 @@ def _worker(rank, world, port, q):
             err = float((hm - h1).abs().max()) / max(float(h1.abs().max()), 1e-12)
             if err > 1e-3:
                 msg = f"sharded WeightAssembler differs from the single-GPU one (rel {err:.2e})"
+        # the DWA LM on the sharded pool against the same model on one GPU (rank 0),
+        # both pool layouts; every rank runs the same collectives
+        from computd_b200.dwa_lm import DWALM, DWALMConfig
+        for r_lm in (0, 2):
+            cfg = DWALMConfig(vocab=65, d_model=64, n_layers=2, n_heads=4, seq_len=64, batch=2,
+                              pool_rows=8192, top_k=8, S=2, d_k=32, r=r_lm)
+            lspec = cb.ShardSpec(cfg.pool_rows, rank, world)
+
+            def pools(rows, off):
+                if r_lm:
+                    return None, cb.new_normal(rows, cfg.D, seed=71, stddev=0.3, row_offset=off,
+                                               device=dev)
+                return (cb.new_normal(rows, cfg.key_width, seed=72, stddev=cfg.key_width ** -0.5,
+                                      row_offset=off, device=dev),
+                        cb.new_normal(rows, cfg.d_model, seed=73, stddev=cfg.d_model ** -0.5,
+                                      row_offset=off, device=dev))
+
+            lk, lv = pools(lspec.n_local, lspec.row_begin)
+            lm = DWALM(cfg, lk, lv)
+            tokens = torch.randint(0, cfg.vocab, (cfg.batch, cfg.seq_len), device=dev,
+                                   generator=torch.Generator(device=dev).manual_seed(3))
+            logits = lm(tokens)
+            st_lm = lm.retriever.status()
+            if rank == 0 and msg == "ok":
+                fk, fv = pools(cfg.pool_rows, 0)
+                lm1 = DWALM(cfg, fk, fv, group=g0)
+                logits1 = lm1(tokens)
+                torch.cuda.synchronize()
+                err = float((logits.float() - logits1.float()).abs().max())
+                scale = float(logits1.float().abs().max())
+                if st_lm != 0 or not err <= 2e-2 * scale:
+                    msg = f"sharded LM (r={r_lm}) differs from one GPU: {err:.3g} of {scale:.3g}"
+            lm.retriever.close()
         if msg == "ok" and not same:
             msg = "nvlink exchange differs from the NCCL path"
         if msg == "ok" and st_p != 0:
