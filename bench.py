@@ -406,6 +406,8 @@ def run_ours(args, wl):
     if not args.no_assembly:
         line["assembly"] = measure_assembly(world, rank, local_rank, group)
         line["key_projection"] = measure_key_projection(world, rank, local_rank)
+        if world == 1:
+            line["hybrid"] = measure_hybrid(local_rank)
     if args.lm:
         names = [n for n in args.lm.split(",") if n and (n != "small_char" or world == 1)]
         line["lm"] = [measure_lm(n, world, rank, local_rank, group) for n in names]
@@ -525,6 +527,74 @@ def measure_key_projection(world, rank, local_rank, warmup=2, steps=5):
             "roofline": {"bound": "tensor", "kernel": "key_project_kernel",
                          "achieved": flops / (ms * 1e-3) / 1e12, "peak": burst, "unit": "TFLOP/s",
                          "frac": flops / (ms * 1e-3) / 1e12 / burst, "flops_per_launch": flops}}
+
+
+def measure_hybrid(local_rank, warmup=3, steps=10):
+    """MultiAspectRetrieval.hybrid_forward (retrieval.py:131-181) on the reference's
+    1B layout (configs/large_1b.py: d_A 1280, S = 8 aspects of d_k = 64, pool
+    16384 x 21760, k = 16, batch 8 x seq 1024), one GPU: packed key projection,
+    fused score + top-k with the seq-mean epilogue, seq scores, alpha.  Also the
+    fused kernel with and without the seq-mean epilogue on the same packed
+    inputs, and the seq-scores kernel on one GPU's shard of the 7B LM pool
+    (4 sequence-mean queries against 2,097,152 x 4096 keys) against HBM."""
+    import torch
+
+    import computd_b200 as cb
+
+    dev = torch.device("cuda", local_rank)
+    B, seq, d_A, S, d_k, N, D, k = 8, 1024, 1280, 8, 64, 16384, 21760, 16
+    m = cb.MultiAspectRetrieval(D=D, d_A=d_A, S=S, d_k=d_k, N=N, device=dev, seed=5)
+    vectors = cb.new_normal(N, D, seed=81, stddev=0.02, device=dev)
+    z = cb.new_normal(B * seq, d_A, seed=82, device=dev).view(B, seq, d_A)
+
+    def timed(fn, n):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    ms_fwd = timed(lambda: m.hybrid_forward(z, vectors, k, 1.0, 1.0, True), steps)
+    p = m.hybrid_parts(z, vectors, k, 1.0, 1.0, True)
+    q, keys = p.queries_flat, p.keys_w
+    params = cb.score_params(1.0, p.tau, 1.0, dev)
+    ms_aux = timed(lambda: cb.score_topk_seqmean(q, keys, k, params[0], params[1], params[2], True,
+                                                 seq), steps)
+    ms_plain = timed(lambda: cb.tiled_topk_fused(q, keys, k, params[0], params[1], params[2], True),
+                     steps)
+    burst, _, hbm, _ = _peaks()
+    flops = 2.0 * B * seq * N * S * d_k
+    del m, vectors, z, p, q, keys
+    torch.cuda.empty_cache()
+    # seq scores at the 7B shard: HBM-bound
+    Ns, ds, Bs = 2097152, 4096, 4
+    ks = cb.new_normal(Ns, ds, seed=83, stddev=ds ** -0.5, device=dev)
+    qm = torch.randn((Bs, ds), device=dev) * ds ** -0.5
+    sims = torch.empty((Bs, Ns), dtype=torch.float32, device=dev)
+    fused = torch.empty_like(sims)
+    ms_seq = timed(lambda: cb.seq_scores(qm, ks, 1.0, 0.0, 1.0, True, sims=sims, fused=fused), 5)
+    bytes_seq = Ns * ds * 2.0 + 2.0 * Bs * Ns * 4 + Bs * ds * 4.0
+    del ks, qm, sims, fused
+    torch.cuda.empty_cache()
+    return {"config": "reference 1B hybrid layout: batch 8 x seq 1024, d_A 1280, S 8 x d_k 64, "
+                      "pool 16384 x 21760, k 16, gate on",
+            "hybrid_forward_ms": ms_fwd, "tokens_per_s": B * seq / (ms_fwd * 1e-3),
+            "score_topk_seqmean_ms": ms_aux, "score_topk_plain_ms": ms_plain,
+            "seqmean_overhead": ms_aux / ms_plain - 1.0,
+            "roofline_score": {"bound": "tensor", "flops_per_launch": flops,
+                               "achieved": flops / (ms_aux * 1e-3) / 1e12, "peak": burst,
+                               "unit": "TFLOP/s",
+                               "frac": flops / (ms_aux * 1e-3) / 1e12 / burst},
+            "seq_scores": {"shape": f"{Bs} x {Ns} x {ds}", "ms_per_launch": ms_seq,
+                           "roofline": {"bound": "hbm", "algorithmic_bytes": bytes_seq,
+                                        "achieved": bytes_seq / (ms_seq * 1e-3) / 1e9,
+                                        "peak": hbm, "unit": "GB/s",
+                                        "frac": bytes_seq / (ms_seq * 1e-3) / 1e9 / hbm}}}
 
 
 def measure_lm(cfg_name, world, rank, local_rank, group=None, warmup=3, steps=3):
