@@ -87,7 +87,7 @@ class DWALMConfig:
         return 2 * d * self.r + d if self.r > 0 else d
 
 
-# Benchmark configurations: keys [N, d] with d = S d_k, values [N, d].
+# The benchmark LM configurations: pool keys [N, d] with d = S d_k, values [N, d].
 SMALL_CHAR = DWALMConfig(vocab=65, d_model=384, n_layers=6, n_heads=6, seq_len=256, batch=16,
                          pool_rows=65536, top_k=32, S=6, d_k=64)
 LARGE_1B = DWALMConfig(vocab=32000, d_model=2048, n_layers=24, n_heads=16, seq_len=2048, batch=8,
