@@ -24,8 +24,8 @@
 //   warps 2-5  epilogue: warp w reads TMEM lanes 32*(w%4).. with tcgen05.ld;
 //              thread = one query row; the list's k-th entry = admission
 //              threshold; candidates are buffered per lane and inserted in
-//              warp-wide passes (k <= 32: warps 2-9, two warpgroups taking
-//              alternate tiles)
+//              warp-wide passes (k <= 32: warps 2-9, two warpgroups each
+//              scanning half of every tile's columns)
 //
 // Work unit = (pair query tile, contiguous range of key tiles).  Units are
 // ordered split-major so the pairs resident at one time sweep the same few
@@ -320,7 +320,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
   auto full_bar = [&](int s) { return bar0 + 8u * s; };             // leader: TMA bytes, both CTAs
   auto empty_bar = [&](int s) { return bar0 + 8u * (S + s); };      // each: stage free again
   auto tfull_bar = [&](int acc) { return bar0 + 8u * (2 * S + acc); };       // each: acc ready
-  auto tempty_bar = [&](int acc) { return bar0 + 8u * (2 * S + 2 + acc); };  // leader: 8 warps
+  auto tempty_bar = [&](int acc) { return bar0 + 8u * (2 * S + 2 + acc); };  // leader: all epilogue warps
   const uint32_t drain_bar = bar0 + 8u * (2 * S + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_area + 8 * (2 * S + 5));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -359,7 +359,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
     }
     for (int acc = 0; acc < 2; ++acc) {
       mbar_init(tfull_bar(acc), 1);
-      mbar_init(tempty_bar(acc), 8);
+      mbar_init(tempty_bar(acc), 2 * 4 * NWG);  // every epilogue warp of both CTAs
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -449,9 +449,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
     // of the same query row has published; the union's k-th best is at least
     // that, so lower scores can never reach the final top-k.  Scores equal to
     // the bound stay admissible (they may win an index tie).
-    // With two warpgroups, warpgroup g takes the tiles t = g, g + 2, ...: it
-    // owns TMEM accumulator buffer g and has two MMA tile-times per tile.
+    // With two warpgroups, warpgroup g scans columns [128 g, 128 g + 128) of
+    // every tile (keys tile * 256 + 128 g + j, so each list still sees its
+    // keys in increasing order).  Both scan the same accumulator at once and
+    // release it together, so a tile costs max(MMA, epilogue / 2).  (Taking
+    // alternate tiles instead costs (MMA + epilogue) / 2: with two TMEM
+    // buffers the MMA of tile t + 2 waits for tile t's release, so the second
+    // warpgroup would only overlap the MMA, never the other warpgroup.)
     const int g = (warp - 2) >> 2;     // epilogue warpgroup
+    constexpr int kColsPerWg = kTileN / NWG;
     const int ew = warp & 3;           // TMEM lane quarter this warp may access
     const int row = ew * 32 + lane;    // query row within this CTA's 128
     typename TopKFor<KCAP>::type topk;
@@ -595,7 +601,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
     };
     const uint32_t lead_tempty0 = map_to_cta(tempty_bar(0), 0);
     const uint32_t lead_tempty1 = map_to_cta(tempty_bar(1), 0);
-    for (int t = g; t < n_tiles; t += NWG) {
+    for (int t = 0; t < n_tiles; ++t) {
       const int acc = t & 1;
       const uint32_t use = static_cast<uint32_t>(t >> 1);
       // warp-uniform outcome: the votes below need all 32 lanes on the same path
@@ -603,8 +609,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
       // The row's shared bounds as published so far, read before the scan so
-      // the latency hides behind it (with two warpgroups the registers are
-      // short and each warpgroup has two tile-times per tile: read after it).
+      // the latency hides behind it.  With two warpgroups the 16 registers
+      // are not there (10 warps share four 16K-register sub-partitions: at
+      // most 168 per thread), so they are read after the scan.
       int4 sb0, sb1, sb2, sb3;
       if constexpr (NWG == 1) {
         sb0 = ld_relaxed_gpu_v4(bound_ptr);
@@ -614,33 +621,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
       }
       const int64_t n0 = (kt_begin + t) * kTileN;
       const int valid = static_cast<int>(min(static_cast<int64_t>(kTileN), a.N - n0));
+      // this warpgroup's columns [cb, ce) of the tile (empty on a short last tile)
+      const int cb = g * kColsPerWg;
+      const int ce = min(valid, cb + kColsPerWg);
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + static_cast<uint32_t>(acc * kTileN);
       if constexpr (AUX) {
         // One chunk of 32 columns at a time: the aux sums need the registers
         // the overlapped load of the next chunk would hold.
-        for (int c = 0; c < valid; c += 32) {
+        for (int c = cb; c < ce; c += 32) {
           uint32_t r[32];
           tmem_ld_32x32b_x32_async(taddr + c, r);
           tmem_wait_ld_pin(r);
-          scan_chunk(r, valid - c, static_cast<int32_t>(n0 + c));
-          aux_chunk(r, valid - c, static_cast<int32_t>(n0 + c));
+          scan_chunk(r, ce - c, static_cast<int32_t>(n0 + c));
+          aux_chunk(r, ce - c, static_cast<int32_t>(n0 + c));
         }
-      } else {
+      } else if (cb < ce) {
         // Chunks of 32 columns, two register sets in flight: the TMEM load of
         // the next chunk overlaps the scan of the current one.
         uint32_t ra[32], rb[32];
-        tmem_ld_32x32b_x32_async(taddr, ra);
+        tmem_ld_32x32b_x32_async(taddr + cb, ra);
         tmem_wait_ld_pin(ra);
-        for (int c = 0; c < valid; c += 64) {
-          const bool has_b = c + 32 < valid;   // warp-uniform
+        for (int c = cb; c < ce; c += 64) {
+          const bool has_b = c + 32 < ce;   // warp-uniform
           if (has_b) tmem_ld_32x32b_x32_async(taddr + c + 32, rb);
-          scan_chunk(ra, valid - c, static_cast<int32_t>(n0 + c));
+          scan_chunk(ra, ce - c, static_cast<int32_t>(n0 + c));
           if (has_b) {
             tmem_wait_ld_pin(rb);
-            const bool has_next = c + 64 < valid;
+            const bool has_next = c + 64 < ce;
             if (has_next) tmem_ld_32x32b_x32_async(taddr + c + 64, ra);
-            scan_chunk(rb, valid - c - 32, static_cast<int32_t>(n0 + c + 32));
+            scan_chunk(rb, ce - c - 32, static_cast<int32_t>(n0 + c + 32));
             if (has_next) tmem_wait_ld_pin(ra);
           }
         }
@@ -795,7 +805,7 @@ bool plan_score_topk(int64_t M, int64_t N, int d, int k, int num_sms, ScoreTopkP
   p.n_kt = (N + kTileN - 1) / kTileN;
   p.num_kb = (d + kTileK - 1) / kTileK;
   p.m_pad = n_qt * kPairRows;
-  // Two epilogue warpgroups (one list each, alternating tiles) for k <= 32,
+  // Two epilogue warpgroups (one list each, half of every tile's columns) for k <= 32,
   // where the register lists leave room for 10 warps; k >= 64 keeps one.
   p.nwg = p.kcap <= 32 ? 2 : 1;
   // Choose the number of key-range splits: minimise the modelled makespan
