@@ -628,40 +628,87 @@ dwa_status dwa_merge_topk_peers(const void* const* packed, int32_t P, int64_t M,
   return ok();
 }
 
+namespace {
+// Argument checks shared by the two low-rank entry points; `fn` names the caller.
+dwa_status check_lowrank_args(const char* fn, const void* h, int64_t ldh, const float* alpha,
+                              const int32_t* gidx, int64_t M, int32_t k, const void* vectors,
+                              int64_t row_begin, int64_t row_end, int64_t ldv, int32_t d_A,
+                              int32_t d_B, int32_t r, const float* delta) {
+  if (M < 0) return fail(DWA_ERR_INVALID_ARG, "%s: negative M", fn);
+  if (!h || !alpha || !gidx || !delta)
+    return fail(DWA_ERR_INVALID_ARG, "%s: null h/alpha/gidx/delta", fn);
+  if (k < 1 || k > DWA_MAX_K)
+    return fail(k < 1 ? DWA_ERR_INVALID_ARG : DWA_ERR_UNSUPPORTED_SHAPE,
+                "%s: k=%d outside [1, %d]", fn, k, DWA_MAX_K);
+  if (d_A < 8 || d_A % 8 != 0 || d_A > 8192 || d_B < 8 || d_B % 8 != 0)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE,
+                "%s: d_A=%d (multiple of 8, <= 8192) / d_B=%d (multiple of 8)", fn, d_A, d_B);
+  if (r < 1 || r > 32) return fail(DWA_ERR_UNSUPPORTED_SHAPE, "%s: r=%d outside [1, 32]", fn, r);
+  if (M > INT32_MAX) return fail(DWA_ERR_UNSUPPORTED_SHAPE, "%s: M too large", fn);
+  if (ldh < d_A) return fail(DWA_ERR_INVALID_ARG, "%s: ldh below d_A", fn);
+  if (row_begin < 0 || row_end < row_begin || row_end > INT32_MAX)
+    return fail(DWA_ERR_INVALID_ARG, "%s: bad owned row range", fn);
+  if (row_end > row_begin) {
+    const int64_t need = static_cast<int64_t>(d_B) * r + static_cast<int64_t>(r) * d_A + d_B;
+    if (!vectors) return fail(DWA_ERR_INVALID_ARG, "%s: null vectors", fn);
+    if (ldv < need)
+      return fail(DWA_ERR_INVALID_ARG, "%s: ldv=%lld below d_B r + r d_A + d_B = %lld", fn,
+                  (long long)ldv, (long long)need);
+    if (ldv % 8 != 0 || !aligned(vectors, 16))
+      return fail(DWA_ERR_UNSUPPORTED_SHAPE,
+                  "%s: vectors need 16-byte aligned rows (ldv %% 8 == 0)", fn);
+  }
+  return DWA_OK;
+}
+}  // namespace
+
 dwa_status dwa_lowrank_delta(const void* h, int32_t h_is_bf16, int64_t ldh, const float* alpha,
                              const int32_t* gidx, int64_t M, int32_t k, const void* vectors,
                              int64_t row_begin, int64_t row_end, int64_t ldv, int32_t d_A,
                              int32_t d_B, int32_t r, float* delta, dwa_stream_t stream) {
-  if (M < 0) return fail(DWA_ERR_INVALID_ARG, "dwa_lowrank_delta: negative M");
   if (M == 0) return ok();
-  if (!h || !alpha || !gidx || !delta)
-    return fail(DWA_ERR_INVALID_ARG, "dwa_lowrank_delta: null h/alpha/gidx/delta");
-  if (k < 1 || k > DWA_MAX_K)
-    return fail(k < 1 ? DWA_ERR_INVALID_ARG : DWA_ERR_UNSUPPORTED_SHAPE,
-                "dwa_lowrank_delta: k=%d outside [1, %d]", k, DWA_MAX_K);
-  if (d_A < 8 || d_A % 8 != 0 || d_A > 8192 || d_B < 8 || d_B % 8 != 0)
-    return fail(DWA_ERR_UNSUPPORTED_SHAPE,
-                "dwa_lowrank_delta: d_A=%d (multiple of 8, <= 8192) / d_B=%d (multiple of 8)", d_A,
-                d_B);
-  if (r < 1 || r > 32) return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_lowrank_delta: r=%d outside [1, 32]", r);
-  if (M > INT32_MAX) return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_lowrank_delta: M too large");
-  if (ldh < d_A) return fail(DWA_ERR_INVALID_ARG, "dwa_lowrank_delta: ldh below d_A");
-  if (row_begin < 0 || row_end < row_begin || row_end > INT32_MAX)
-    return fail(DWA_ERR_INVALID_ARG, "dwa_lowrank_delta: bad owned row range");
-  if (row_end > row_begin) {
-    const int64_t need = static_cast<int64_t>(d_B) * r + static_cast<int64_t>(r) * d_A + d_B;
-    if (!vectors) return fail(DWA_ERR_INVALID_ARG, "dwa_lowrank_delta: null vectors");
-    if (ldv < need)
-      return fail(DWA_ERR_INVALID_ARG, "dwa_lowrank_delta: ldv=%lld below d_B r + r d_A + d_B = %lld",
-                  (long long)ldv, (long long)need);
-    if (ldv % 8 != 0 || !aligned(vectors, 16))
-      return fail(DWA_ERR_UNSUPPORTED_SHAPE,
-                  "dwa_lowrank_delta: vectors need 16-byte aligned rows (ldv %% 8 == 0)");
-  }
+  const dwa_status st = check_lowrank_args("dwa_lowrank_delta", h, ldh, alpha, gidx, M, k, vectors,
+                                           row_begin, row_end, ldv, d_A, d_B, r, delta);
+  if (st != DWA_OK) return st;
   cudaError_t e = dwa::launch_lowrank_delta(h, h_is_bf16 ? 1 : 0, ldh, alpha, gidx, M, k, vectors,
                                             row_begin, row_end, ldv, d_A, d_B, r, delta,
                                             static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "dwa_lowrank_delta launch");
+  return ok();
+}
+
+size_t dwa_lowrank_delta_rows_workspace(int64_t M, int32_t k, int64_t n_rows, int32_t d_B) {
+  if (M < 0 || k < 1 || n_rows < 0 || d_B < 1) return 0;
+  return dwa::lowrank_rows_workspace_bytes(M, k, n_rows, d_B);
+}
+
+dwa_status dwa_lowrank_delta_rows(const void* h, int32_t h_is_bf16, int64_t ldh,
+                                  const float* alpha, const int32_t* gidx, int64_t M, int32_t k,
+                                  const void* vectors, int64_t row_begin, int64_t row_end,
+                                  int64_t ldv, int32_t d_A, int32_t d_B, int32_t r, float* delta,
+                                  void* workspace, size_t workspace_bytes, dwa_stream_t stream) {
+  const char* fn = "dwa_lowrank_delta_rows";
+  if (M == 0) return ok();
+  const dwa_status st = check_lowrank_args(fn, h, ldh, alpha, gidx, M, k, vectors, row_begin,
+                                           row_end, ldv, d_A, d_B, r, delta);
+  if (st != DWA_OK) return st;
+  if (M * static_cast<int64_t>(k) > INT32_MAX)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "%s: M k above INT32_MAX", fn);
+  if (dwa::lowrank_rows_smem_bytes(d_A, d_B, r) > 200 * 1024)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE,
+                "%s: a row's U | V | b (%d bytes) exceeds 200 KB of shared memory", fn,
+                dwa::lowrank_rows_smem_bytes(d_A, d_B, r));
+  if (!aligned(h, 16) || ldh % (h_is_bf16 ? 8 : 4) != 0)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "%s: h rows must be 16-byte aligned", fn);
+  if (!aligned(delta, 16)) return fail(DWA_ERR_UNSUPPORTED_SHAPE, "%s: delta not 16-byte aligned", fn);
+  const size_t need = dwa::lowrank_rows_workspace_bytes(M, k, row_end - row_begin, d_B);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+    return fail(DWA_ERR_WORKSPACE, "%s: workspace needs %zu bytes, 256-byte aligned (got %zu)", fn,
+                need, workspace_bytes);
+  cudaError_t e = dwa::launch_lowrank_rows(h, h_is_bf16 ? 1 : 0, ldh, alpha, gidx, M, k, vectors,
+                                           row_begin, row_end, ldv, d_A, d_B, r, delta, workspace,
+                                           static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_lowrank_delta_rows launch");
   return ok();
 }
 

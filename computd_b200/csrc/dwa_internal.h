@@ -147,6 +147,13 @@ cudaError_t launch_lowrank_delta(const void* h, int h_bf16, int64_t ldh, const f
                                  const int32_t* gidx, int64_t M, int k, const void* vectors,
                                  int64_t row_begin, int64_t row_end, int64_t ldv, int d_A, int d_B,
                                  int r, float* delta, cudaStream_t stream);
+// lowrank_rows.cu: the same delta, row-stationary (rows read once), with a caller workspace
+size_t lowrank_rows_workspace_bytes(int64_t M, int k, int64_t n_rows, int d_B);
+int lowrank_rows_smem_bytes(int d_A, int d_B, int r);
+cudaError_t launch_lowrank_rows(const void* h, int h_bf16, int64_t ldh, const float* alpha,
+                                const int32_t* gidx, int64_t M, int k, const void* vectors,
+                                int64_t row_begin, int64_t row_end, int64_t ldv, int d_A, int d_B,
+                                int r, float* delta, void* ws, cudaStream_t stream);
 cudaError_t launch_assemble_finish(const void* residual, int res_bf16, int64_t ldr,
                                    const float* base, const float* delta, int64_t M, int d_B,
                                    float gamma, const float* ln_scale, const float* ln_bias,

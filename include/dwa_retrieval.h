@@ -421,6 +421,31 @@ DWA_API dwa_status dwa_lowrank_delta(const void* h, int32_t h_is_bf16, int64_t l
                              float* delta, dwa_stream_t stream);
 
 /*
+ * The same delta as dwa_lowrank_delta, organised by pool row: the (token,
+ * entry) pairs are sorted by owned row, each selected row's U | V | b is read
+ * from HBM about once and applied to every token that selected it, each pair
+ * writes alpha (U_j (V_j h[m]) + b_j) to its own slot of the workspace, and a
+ * final pass sums each token's slots in entry order (no float atomics: the
+ * result is the same on every run).  Reads ~1.2x the selected rows instead of
+ * one row per (token, entry), at the cost of M k d_B floats written and read
+ * back.  Sums may differ from dwa_lowrank_delta's in the last bits (another
+ * order of the V_j h[m] dot products).
+ * Extra requirements: M k <= INT32_MAX; the row's U | V | b
+ * ((d_B r + r d_A + d_B) bf16) at most 200 KB; h rows 16-byte aligned (ldh a
+ * multiple of 8 for bf16, 4 for f32); delta 16-byte aligned.
+ * workspace: >= dwa_lowrank_delta_rows_workspace(M, k, row_end - row_begin,
+ * d_B) bytes, 256-byte aligned, not shared with a concurrent call.
+ */
+DWA_API size_t dwa_lowrank_delta_rows_workspace(int64_t M, int32_t k, int64_t n_rows,
+                                                int32_t d_B);
+DWA_API dwa_status dwa_lowrank_delta_rows(const void* h, int32_t h_is_bf16, int64_t ldh,
+                                          const float* alpha, const int32_t* gidx, int64_t M,
+                                          int32_t k, const void* vectors, int64_t row_begin,
+                                          int64_t row_end, int64_t ldv, int32_t d_A,
+                                          int32_t d_B, int32_t r, float* delta, void* workspace,
+                                          size_t workspace_bytes, dwa_stream_t stream);
+
+/*
  * out[m, :] = LayerNorm(residual[m, :] + gamma * (base[m, :] + delta[m, :]))
  * (assembly.py:128: residual = h_A when d_A == d_B, base = h_A W_base^T +
  * b_base, computed by the caller's GEMM).  residual (bf16 or f32, stride

@@ -173,6 +173,21 @@ def test_nvlink_and_projection_entry_points_validate_before_launch():
                                  None) == 2
     assert lib.dwa_lowrank_delta(FAKE, 1, 64, FAKE, FAKE, 4, 2, FAKE, 0, 10, 100, 64, 16, 8, FAKE,
                                  None) == 1
+    # row-stationary low-rank assembly: same checks, then its own limits
+    need = lib.dwa_lowrank_delta_rows_workspace(8192, 16, 16384, 1280)
+    assert need >= 8192 * 16 * 1280 * 4 + 8192 * 16 * 4 + 16384 * 8
+    assert lib.dwa_lowrank_delta_rows_workspace(-1, 16, 16384, 1280) == 0
+    D = 1280 * 8 + 8 * 1280 + 1280
+    rows = lambda M, k, d_A, d_B, r, ldv, ws, ws_bytes: lib.dwa_lowrank_delta_rows(
+        FAKE, 1, d_A, FAKE, FAKE, M, k, FAKE, 0, 16384, ldv, d_A, d_B, r, FAKE, ws, ws_bytes, None)
+    assert rows(4, 2, 1280, 1280, 8, D, None, 0) == _lib.DWA_ERR_WORKSPACE
+    assert rows(4, 2, 1280, 1280, 8, D, FAKE, 16) == _lib.DWA_ERR_WORKSPACE
+    assert rows(4, 2, 1280, 1280, 0, D, FAKE, 1 << 40) == 2          # r outside [1, 32]
+    assert rows(4, 2, 1280, 1280, 8, 100, FAKE, 1 << 40) == 1        # ldv below the row
+    D_big = 8192 * 8 + 8 * 8192 + 8192                               # 272 KB of U | V | b
+    assert rows(4, 2, 8192, 8192, 8, D_big, FAKE, 1 << 40) == 2
+    assert rows(1 << 27, 32, 1280, 1280, 8, D, FAKE, 1 << 62) == 2   # M k above INT32_MAX
+    assert rows(0, 2, 1280, 1280, 8, D, None, 0) == 0                # empty batch: no-op
     assert lib.dwa_assemble_finish(None, 0, 0, None, None, 4, 16, 1.0, None, None, 1e-6, FAKE,
                                    None) == 1
     assert lib.dwa_usage_ema(FAKE, FAKE, -1, 0, 10, 0.01, 0.99, FAKE, None) == 1

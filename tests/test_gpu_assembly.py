@@ -62,7 +62,8 @@ def test_assembler_matches_reference_call(lib, golden, name):
     (64, 500, 128, 128, 3, 5, 8),        # odd rank
     (33, 400, 512, 256, 16, 32, 16),     # r = 16, k = 32
 ])
-def test_lowrank_delta_vs_oracle(lib, M, N, d_A, d_B, r, k, extra):
+@pytest.mark.parametrize("rows", [False, True])   # per-token / row-stationary kernels
+def test_lowrank_delta_vs_oracle(lib, M, N, d_A, d_B, r, k, extra, rows):
     rng = np.random.default_rng(M + N + r)
     D = d_B * r + r * d_A + d_B + extra
     vectors = O.bf16_round((rng.standard_normal((N, D)) * 0.2).astype(np.float32))
@@ -70,15 +71,18 @@ def test_lowrank_delta_vs_oracle(lib, M, N, d_A, d_B, r, k, extra):
     alpha = rng.random((M, k)).astype(np.float32)
     idx = np.stack([rng.choice(N, size=k, replace=False) for _ in range(M)]).astype(np.int32)
     got = lib.lowrank_delta(_bf16(h), torch.from_numpy(alpha).to(_dev()),
-                            torch.from_numpy(idx).to(_dev()), _bf16(vectors), d_A, d_B, r)
+                            torch.from_numpy(idx).to(_dev()), _bf16(vectors), d_A, d_B, r,
+                            rows=rows)
     _close(got.cpu().numpy(), O.lowrank_delta(h, alpha, idx, vectors, d_A, d_B, r))
     # f32 rows of h give the same result
     got32 = lib.lowrank_delta(torch.from_numpy(h).to(_dev()), torch.from_numpy(alpha).to(_dev()),
-                              torch.from_numpy(idx).to(_dev()), _bf16(vectors), d_A, d_B, r)
+                              torch.from_numpy(idx).to(_dev()), _bf16(vectors), d_A, d_B, r,
+                              rows=rows)
     torch.testing.assert_close(got32, got, rtol=1e-5, atol=1e-5)
 
 
-def test_lowrank_delta_owner_computes_partials_add_up(lib):
+@pytest.mark.parametrize("rows", [False, True])
+def test_lowrank_delta_owner_computes_partials_add_up(lib, rows):
     rng = np.random.default_rng(7)
     M, N, d_A, d_B, r, k, P = 120, 900, 128, 96, 8, 12, 3
     D = d_B * r + r * d_A + d_B
@@ -86,14 +90,63 @@ def test_lowrank_delta_owner_computes_partials_add_up(lib):
     h = _bf16(rng.standard_normal((M, d_A)).astype(np.float32))
     alpha = torch.from_numpy(rng.random((M, k)).astype(np.float32)).to(_dev())
     idx = torch.from_numpy(rng.integers(0, N, (M, k)).astype(np.int32)).to(_dev())
-    full = lib.lowrank_delta(h, alpha, idx, vectors, d_A, d_B, r)
+    full = lib.lowrank_delta(h, alpha, idx, vectors, d_A, d_B, r, rows=rows)
     n = N // P
     parts = sum(lib.lowrank_delta(h, alpha, idx, vectors[p * n:(p + 1) * n], d_A, d_B, r,
-                                  row_begin=p * n) for p in range(P))
+                                  row_begin=p * n, rows=rows) for p in range(P))
     torch.testing.assert_close(parts, full, rtol=1e-4, atol=1e-4)
     # a shard that owns none of the rows contributes exactly zero
-    none = lib.lowrank_delta(h, alpha, idx, vectors[:8], d_A, d_B, r, row_begin=N + 10)
+    none = lib.lowrank_delta(h, alpha, idx, vectors[:8], d_A, d_B, r, row_begin=N + 10,
+                             rows=rows)
     assert torch.count_nonzero(none) == 0
+
+
+def test_lowrank_rows_skewed_rows_and_determinism(lib):
+    """Row-stationary path: a few rows selected by every token (their pairs span
+    many 32-pair chunks), repeated rows inside a token, the per-token kernel as
+    the reference, and two runs bit-identical (no float atomics)."""
+    rng = np.random.default_rng(21)
+    M, N, d_A, d_B, r, k = 700, 3000, 256, 192, 8, 16
+    D = d_B * r + r * d_A + d_B
+    vectors = _bf16((rng.standard_normal((N, D)) * 0.2).astype(np.float32))
+    h = _bf16(rng.standard_normal((M, d_A)).astype(np.float32))
+    alpha = torch.from_numpy(rng.random((M, k)).astype(np.float32)).to(_dev())
+    idx_np = rng.integers(0, N, (M, k)).astype(np.int32)
+    idx_np[:, 0] = 5            # every token selects row 5 ...
+    idx_np[:, 1] = 2999         # ... and the last row
+    idx_np[::3, 2] = 5          # a third of them select row 5 twice
+    idx = torch.from_numpy(idx_np).to(_dev())
+    ref = lib.lowrank_delta(h, alpha, idx, vectors, d_A, d_B, r, rows=False)
+    a1 = lib.lowrank_delta(h, alpha, idx, vectors, d_A, d_B, r, rows=True)
+    a2 = lib.lowrank_delta(h, alpha, idx, vectors, d_A, d_B, r, rows=True)
+    torch.testing.assert_close(a1, ref, rtol=1e-4, atol=1e-4)
+    assert torch.equal(a1, a2)
+
+
+def test_lowrank_rows_reference_1b_layout(lib):
+    """The reference's 1B layout (d 1280, r 8, 16,384 pool rows of [U | V | b],
+    k 16) at 2048 tokens: the row-stationary path against the per-token kernel
+    on all tokens and against the oracle on 48 sampled tokens."""
+    rng = np.random.default_rng(5)
+    M, N, d, r, k = 2048, 16384, 1280, 8, 16
+    D = d * r + r * d + d
+    g = torch.Generator(device=_dev()).manual_seed(3)
+    vectors = (torch.randn(N, D, device=_dev(), generator=g) * 0.02).to(torch.bfloat16)
+    h = torch.randn(M, d, device=_dev(), generator=g).to(torch.bfloat16)
+    alpha = torch.softmax(torch.randn(M, k, device=_dev(), generator=g), -1)
+    idx = torch.stack([torch.randperm(N, device=_dev(), generator=g)[:k] for _ in range(M)]).to(
+        torch.int32)
+    ref = lib.lowrank_delta(h, alpha, idx, vectors, d, d, r, rows=False)
+    got = lib.lowrank_delta(h, alpha, idx, vectors, d, d, r, rows=True)
+    torch.testing.assert_close(got, ref, rtol=1e-4, atol=1e-5)
+    rows_m = rng.choice(M, size=48, replace=False)
+    sel = torch.from_numpy(rows_m).to(_dev())
+    i_s = idx[sel].cpu().numpy()
+    uniq, inv = np.unique(i_s, return_inverse=True)
+    vec_s = vectors[torch.from_numpy(uniq).to(_dev())].float().cpu().numpy()
+    want = O.lowrank_delta(h[sel].float().cpu().numpy(), alpha[sel].cpu().numpy(),
+                           inv.reshape(i_s.shape).astype(np.int32), vec_s, d, d, r)
+    _close(got[sel].cpu().numpy(), want)
 
 
 def test_assemble_finish_vs_oracle(lib):
