@@ -460,30 +460,50 @@ def measure_assembly(world, rank, local_rank, group, warmup=3, steps=10):
         asm(h, alpha, idx, vectors, group=grp)
     e1.record()
     barrier()
-    # the fused delta kernel alone (this rank's owned rows)
+    # the delta alone (this rank's owned rows), on the path WeightAssembler takes
+    # (row-stationary when rows are shared by >= 4 tokens), then the per-token
+    # kernel for comparison
+    from computd_b200.assembler import _rows_path_fits
+    rows = _rows_path_fits(M, k, spec.n_local, d_A, d_B, r)
     for _ in range(steps):
-        cb.lowrank_delta(h, alpha, idx, vectors, d_A, d_B, r, row_begin=spec.row_begin)
+        cb.lowrank_delta(h, alpha, idx, vectors, d_A, d_B, r, row_begin=spec.row_begin, rows=rows)
     e2.record()
+    e3 = torch.cuda.Event(enable_timing=True)
+    for _ in range(steps):
+        cb.lowrank_delta(h, alpha, idx, vectors, d_A, d_B, r, row_begin=spec.row_begin, rows=False)
+    e3.record()
     barrier()
-    t = torch.tensor([e0.elapsed_time(e1) / steps, e1.elapsed_time(e2) / steps],
-                     dtype=torch.float64, device=dev)
+    t = torch.tensor([e0.elapsed_time(e1) / steps, e1.elapsed_time(e2) / steps,
+                      e2.elapsed_time(e3) / steps], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, ms_delta = float(t[0]), float(t[1])
-    owned = float(((idx >= spec.row_begin) & (idx < spec.row_end)).sum())
-    # algorithmic bytes of the delta kernel: each owned selected row's U, V and b
-    # blocks once, h once per token, delta written once
-    bytes_delta = owned * (D * 2.0) + M * (d_A * 2.0 + d_B * 4.0)
+    ms, ms_delta, ms_token = float(t[0]), float(t[1]), float(t[2])
+    own = (idx >= spec.row_begin) & (idx < spec.row_end)
+    owned = float(own.sum())
+    uniq = float(torch.unique(idx[own]).numel())
+    # algorithmic bytes.  Per-token kernel: each owned selected row's U, V and b
+    # blocks once per (token, entry), h once per token, delta written once.
+    # Row-stationary: each distinct owned row once, each pair's d_B-float slot
+    # written and read back once, h and delta once.
+    bytes_token = owned * (D * 2.0) + M * (d_A * 2.0 + d_B * 4.0)
+    bytes_rows = uniq * (D * 2.0) + owned * d_B * 8.0 + M * (d_A * 2.0 + d_B * 4.0)
+    bytes_delta = bytes_rows if rows else bytes_token
     hbm = _peaks()[2]
     del vectors, h, idx, alpha, asm
     torch.cuda.empty_cache()
     return {"config": "reference 1B assembly layout (d_A=d_B=1280, r=8, D=21760, k=16, N=16384)",
             "tokens_per_step": M, "tokens_per_s": M / (ms * 1e-3), "unit": "tokens/s",
             "ms_per_step": ms, "pool_rows_per_gpu": spec.n_local,
-            "roofline": {"bound": "hbm", "kernel": "lowrank_delta_kernel", "ms_per_launch": ms_delta,
+            "roofline": {"bound": "hbm",
+                         "kernel": ("lowrank_rows: pair sort + row kernel + per-token slot sum"
+                                    if rows else "lowrank_delta_staged_kernel"),
+                         "ms_per_launch": ms_delta,
                          "achieved": bytes_delta / (ms_delta * 1e-3) / 1e9, "peak": hbm,
                          "unit": "GB/s", "frac": bytes_delta / (ms_delta * 1e-3) / 1e9 / hbm,
                          "algorithmic_bytes_per_launch": bytes_delta},
+            "per_token_kernel": {"ms_per_launch": ms_token,
+                                 "algorithmic_bytes_per_launch": bytes_token,
+                                 "frac": bytes_token / (ms_token * 1e-3) / 1e9 / hbm},
             "data": "synthetic: uniform distinct indices per token, random weights"}
 
 
