@@ -63,13 +63,16 @@ def _capture_block0(model, tokens):
     return logits, rec
 
 
-@pytest.mark.parametrize("r", [0, 2])
-def test_dwa_lm_block_matches_oracle(r):
+# (r, pool rows): value rows; [U | V | b] rows read per token (192 tokens x 8 over
+# 4096 rows); [U | V | b] rows shared by ~6 tokens each, so the assembler takes
+# the row-stationary path
+@pytest.mark.parametrize("r,pool", [(0, 4096), (2, 4096), (2, 256)])
+def test_dwa_lm_block_matches_oracle(r, pool):
     import computd_b200 as cb
     from computd_b200.dwa_lm import DWALMConfig
 
     cfg = DWALMConfig(vocab=65, d_model=64, n_layers=2, n_heads=4, seq_len=64, batch=3,
-                      pool_rows=4096, top_k=8, S=2, d_k=32, r=r)
+                      pool_rows=pool, top_k=8, S=2, d_k=32, r=r)
     model, keys, pool = _model(cfg, seed=11 + r)
     tokens = torch.randint(0, cfg.vocab, (cfg.batch, cfg.seq_len), device=pool.device,
                            generator=torch.Generator(device=pool.device).manual_seed(r))
@@ -103,12 +106,16 @@ def test_dwa_lm_block_matches_oracle(r):
     assert O.compare_rows(got, want, rtol=2e-2) == []
 
 
-@pytest.mark.parametrize("r", [0, 2])
-def test_dwa_lm_graph_replay_matches_eager(r):
+@pytest.mark.parametrize("r,pool", [(0, 4096), (2, 4096), (2, 256)])
+def test_dwa_lm_graph_replay_matches_eager(r, pool):
+    from computd_b200.assembler import _rows_path_fits
     from computd_b200.dwa_lm import DWALMConfig, GraphedForward
 
     cfg = DWALMConfig(vocab=65, d_model=128, n_layers=3, n_heads=4, seq_len=64, batch=2,
-                      pool_rows=4096, top_k=8, S=4, d_k=32, r=r)
+                      pool_rows=pool, top_k=8, S=4, d_k=32, r=r)
+    if r > 0:  # the parametrisation covers both assembly paths
+        assert _rows_path_fits(cfg.tokens, cfg.top_k, pool, cfg.d_model, cfg.d_model, r) == (
+            pool == 256)
     model, _, pool = _model(cfg, seed=21 + r)
     dev = pool.device
     g = torch.Generator(device=dev).manual_seed(5)
