@@ -260,7 +260,8 @@ __global__ void __launch_bounds__(kRowThreads) lowrank_rows_kernel(const RowsArg
       float acc[RMAX];
 #pragma unroll
       for (int t = 0; t < RMAX; ++t) acc[t] = 0.f;
-      for (int c = lane; c < a_words; c += 32) {
+#pragma unroll 4
+      for (int c = lane; c < a_words; c += 32) {  // unrolled: the h loads (L2) go out together
         float x[8];
         if constexpr (HBF16) {
           const uint4 hw =
@@ -288,6 +289,7 @@ __global__ void __launch_bounds__(kRowThreads) lowrank_rows_kernel(const RowsArg
         }
       }
       float* out = a.part + static_cast<int64_t>(pid) * a.d_B;
+#pragma unroll 4
       for (int i = lane; i < a.d_B; i += 32) {
         float u = 0.f;
         if constexpr (VEC_U) {
