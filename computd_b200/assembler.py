@@ -41,20 +41,23 @@ def _rows(x: torch.Tensor, name: str) -> tuple[torch.Tensor, int]:
     return x, 1 if x.dtype == torch.bfloat16 else 0
 
 
-_ROWS_WORKSPACE: dict[int, torch.Tensor] = {}
+_ROWS_WORKSPACE: dict[tuple[int, int], torch.Tensor] = {}
 
 
 def lowrank_rows_workspace(M: int, k: int, n_rows: int, d_B: int,
                            device: torch.device) -> torch.Tensor:
     """The row-stationary path's scratch (``dwa_lowrank_delta_rows_workspace``
-    bytes), one buffer per device that grows on demand and is shared by every
-    caller: calls must be ordered on one stream (the blocks of a forward are)."""
+    bytes): one buffer per (device, current stream) that grows on demand and is
+    shared by the calls on that stream, which the stream orders (the blocks of
+    a forward).  Calls on other streams get buffers of their own; a CUDA-graph
+    capture allocates its buffer from the graph's pool."""
     need = int(_lib.load().dwa_lowrank_delta_rows_workspace(M, k, n_rows, d_B))
     dev = torch.device(device)
-    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    index = dev.index if dev.index is not None else torch.cuda.current_device()
+    key = (index, torch.cuda.current_stream(index).cuda_stream)
     ws = _ROWS_WORKSPACE.get(key)
     if ws is None or ws.numel() < need:
-        ws = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
+        ws = torch.empty(max(need, 256), dtype=torch.uint8, device=torch.device("cuda", index))
         _ROWS_WORKSPACE[key] = ws
     return ws
 
