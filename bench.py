@@ -408,6 +408,7 @@ def run_ours(args, wl):
         line["key_projection"] = measure_key_projection(world, rank, local_rank)
         if world == 1:
             line["hybrid"] = measure_hybrid(local_rank)
+            line["backward"] = measure_backward(local_rank)
     if args.lm:
         names = [n for n in args.lm.split(",") if n and (n != "small_char" or world == 1)]
         line["lm"] = [measure_lm(n, world, rank, local_rank, group) for n in names]
@@ -615,6 +616,67 @@ def measure_hybrid(local_rank, warmup=3, steps=10):
                                         "achieved": bytes_seq / (ms_seq * 1e-3) / 1e9,
                                         "peak": hbm, "unit": "GB/s",
                                         "frac": bytes_seq / (ms_seq * 1e-3) / 1e9 / hbm}}}
+
+
+def measure_backward(local_rank, warmup=2, steps=5):
+    """The custom VJP of the retrieval op (computd_b200.autograd.retrieve; the
+    reference trains through its plain-jnp path, retrieval.py:268-271) at the
+    op-at-scale shape: 8192 queries x 1,048,576-row pool, d 1024, k 64.
+
+    Two timings: the backward with only the queries requiring grad (one
+    launch of dwa_retrieval_backward: <dout, V[idx]> and <q, K[idx]>, the
+    score derivative and the ds-weighted key-row sum), and the full backward, which
+    also scatter-adds into dense f32 key and value gradients of the whole pool
+    (8 GiB zero-filled, then converted to bf16: allocation work, not kernels)."""
+    import torch
+
+    import computd_b200 as cb
+    from computd_b200.autograd import retrieve
+
+    M, N, d, k = 8192, 1 << 20, 1024, 64
+    dev = torch.device("cuda", local_rank)
+    keys = cb.new_normal(N, d, seed=51, stddev=d ** -0.5, device=dev)
+    values = cb.new_normal(N, d, seed=52, stddev=1.0, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(53)
+    q0 = torch.randn((M, d), device=dev, generator=g).to(torch.bfloat16)
+    dout = torch.randn((M, d), device=dev, generator=g)
+    res = {"config": "op-at-scale retrieval backward: 8192 x 1,048,576 x 1024, k 64, bf16 pool",
+           "data": "synthetic"}
+    for name, kv_grad in (("queries_only", False), ("all_inputs", True)):
+        q = q0.clone().requires_grad_(True)
+        kk = keys.requires_grad_(kv_grad)
+        vv = values.requires_grad_(kv_grad)
+        ts = []
+        for it in range(warmup + steps):
+            out, _, _ = retrieve(q, kk, vv, k)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            out.backward(dout)
+            e1.record()
+            torch.cuda.synchronize()
+            if it >= warmup:
+                ts.append(e0.elapsed_time(e1))
+            q.grad = None
+            kk.grad = None
+            vv.grad = None
+            del out
+        res[f"{name}_ms"] = sorted(ts)[len(ts) // 2]
+    keys.requires_grad_(False)
+    values.requires_grad_(False)
+    # algorithmic bytes of the queries-only backward (one fused launch on one
+    # GPU): each selected key and value row once (M k bf16 rows each), q and
+    # dout once, dq written
+    b = 2.0 * M * k * d * 2 + M * d * 2 + M * d * 4 + M * d * 4
+    hbm = _peaks()[2]
+    res["roofline_queries_only"] = {"bound": "hbm", "algorithmic_bytes": b,
+                                    "achieved": b / (res["queries_only_ms"] * 1e-3) / 1e9,
+                                    "peak": hbm, "unit": "GB/s",
+                                    "frac": b / (res["queries_only_ms"] * 1e-3) / 1e9 / hbm}
+    del keys, values, q0, dout
+    torch.cuda.empty_cache()
+    return res
 
 
 def measure_lm(cfg_name, world, rank, local_rank, group=None, warmup=3, steps=3):

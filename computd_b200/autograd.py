@@ -81,26 +81,42 @@ class _RetrievalFn(torch.autograd.Function):
         M, k = ti.shape
         d_k, d_v = kk.shape[1], vv.shape[1]
         dout = dout.to(torch.float32).contiguous()
-        # dalpha = <dout, V[idx]>, s = <q, K[idx]>: owned partial dots, summed over ranks
-        dalpha = gather_dot(dout, ti, vv, row_begin)
-        s = gather_dot(q, ti, kk, row_begin)
-        if world > 1:
-            dist.all_reduce(dalpha, group=group)
-            dist.all_reduce(s, group=group)
         ds = torch.empty((M, k), dtype=torch.float32, device=dev)
         dparams = torch.zeros(3, dtype=torch.float32, device=dev)
+        dq = grad_k = grad_v = None
+        if world == 1 and k <= 128:
+            # the whole pool here: s, dalpha, ds and dq in one launch, each
+            # selected row read once (dwa_retrieval_backward)
+            dq = torch.empty((M, d_k), dtype=torch.float32, device=dev)
+            pq, qbf, ldq = _vec_args(q)
+            with torch.cuda.device(dev):
+                st = lib.dwa_retrieval_backward(
+                    pq, qbf, ldq, dout.data_ptr(), dout.stride(0), kk.data_ptr(), kk.stride(0),
+                    d_k, vv.data_ptr(), vv.stride(0), d_v, tv.data_ptr(), ti.data_ptr(), M, k,
+                    row_begin, row_begin + kk.shape[0], lam, tau, T, None, int(use_sigmoid),
+                    ds.data_ptr(), dq.data_ptr(), dparams.data_ptr(), None, sh)
+            _lib.check(st, "dwa_retrieval_backward")
+            if not ctx.needs_input_grad[0]:
+                dq = None
+        else:
+            # dalpha = <dout, V[idx]>, s = <q, K[idx]>: owned partial dots, summed over ranks
+            dalpha = gather_dot(dout, ti, vv, row_begin)
+            s = gather_dot(q, ti, kk, row_begin)
+            if world > 1:
+                dist.all_reduce(dalpha, group=group)
+                dist.all_reduce(s, group=group)
+            with torch.cuda.device(dev):
+                st = lib.dwa_score_backward(tv.data_ptr(), s.data_ptr(), dalpha.data_ptr(), M, k,
+                                            lam, tau, T, int(use_sigmoid), ds.data_ptr(),
+                                            dparams.data_ptr(), sh)
+                _lib.check(st, "dwa_score_backward")
+                if ctx.needs_input_grad[0]:
+                    dq = torch.empty((M, d_k), dtype=torch.float32, device=dev)
+                    st = lib.dwa_gather_rows(ds.data_ptr(), ti.data_ptr(), M, k, kk.data_ptr(),
+                                             row_begin, row_begin + kk.shape[0], kk.stride(0), d_k,
+                                             dq.data_ptr(), 0, sh)
+                    _lib.check(st, "dwa_gather_rows")
         with torch.cuda.device(dev):
-            st = lib.dwa_score_backward(tv.data_ptr(), s.data_ptr(), dalpha.data_ptr(), M, k, lam,
-                                        tau, T, int(use_sigmoid), ds.data_ptr(),
-                                        dparams.data_ptr(), sh)
-            _lib.check(st, "dwa_score_backward")
-            dq = grad_k = grad_v = None
-            if ctx.needs_input_grad[0]:
-                dq = torch.empty((M, d_k), dtype=torch.float32, device=dev)
-                st = lib.dwa_gather_rows(ds.data_ptr(), ti.data_ptr(), M, k, kk.data_ptr(),
-                                         row_begin, row_begin + kk.shape[0], kk.stride(0), d_k,
-                                         dq.data_ptr(), 0, sh)
-                _lib.check(st, "dwa_gather_rows")
             if ctx.needs_input_grad[1]:
                 grad_k = torch.zeros((kk.shape[0], d_k), dtype=torch.float32, device=dev)
                 pa, abf, lda = _vec_args(q)

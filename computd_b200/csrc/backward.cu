@@ -12,6 +12,9 @@
 //   dV[idx_j] += alpha_j dout,  dK[idx_j] += ds_j q           scatter_add_rows
 //   dlambda, dtau, dT: sums over (m, j)                       score_backward
 //
+// On one GPU the queries side (s, dalpha, ds, dq) runs as one launch,
+// retrieval_backward_kernel, reading each selected row once.
+//
 // Every kernel works on an owned row range [row_begin, row_end) of the pool
 // (owner-computes): on a sharded pool each rank's partial dalpha / s / dq are
 // summed with one all-reduce, and each rank updates only its own rows.
@@ -205,6 +208,177 @@ __global__ void __launch_bounds__(kWarps * 32)
   }
 }
 
+// ---------------------------------------------------------------- fused (one GPU)
+// The queries-side backward in one launch when the whole pool is on this GPU
+// (no all-reduce between the dot products and the score derivative): CTA = one
+// query m.  (1) warps split the k entries: s_j = <q, K_j>, dalpha_j =
+// <dout, V_j>, each selected K and V row read once; (2) warp 0: ds_j and the
+// lambda / tau / T terms exactly as score_backward_kernel; (3) all threads:
+// dq = sum_j ds_j K_j over column slices, re-reading the K rows this CTA just
+// read (from L2).  Replaces gather_dot x 2 + score_backward + gather_rows.
+constexpr int kBwdMaxK = 128;
+
+struct FusedBwdArgs {
+  const void* q;
+  int q_bf16;
+  int64_t ldq;
+  const float* dout;
+  int64_t ld_dout;
+  const uint16_t* keys;
+  int64_t ldk;
+  int d_k;
+  const uint16_t* values;
+  int64_t ldv;
+  int d_v;
+  const float* v;
+  const int32_t* idx;
+  int64_t M;
+  int k;
+  int64_t row_begin, row_end;
+  float lambda_sharp, tau, T;
+  const float* params;
+  int use_sigmoid;
+  float* ds;
+  float* dq;
+  float* dparams;
+  int* status;
+};
+
+__global__ void __launch_bounds__(kWarps * 32, 1) retrieval_backward_kernel(const FusedBwdArgs a) {
+  __shared__ int32_t g_s[kBwdMaxK];
+  __shared__ float s_s[kBwdMaxK], da_s[kBwdMaxK], ds_s[kBwdMaxK];
+  __shared__ int ok_s;
+  const int64_t m = blockIdx.x;
+  const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+  const int k = a.k;
+  for (int j = tid; j < k; j += kWarps * 32) g_s[j] = a.idx[m * k + j];
+  __syncthreads();
+  // (1) s_j and dalpha_j, entries j = w, w + 8, ...
+  for (int j = w; j < k; j += kWarps) {
+    const int32_t g = g_s[j];
+    float sj = 0.f, dj = 0.f;
+    if (g >= a.row_begin && g < a.row_end) {  // warp-uniform
+      const uint16_t* kr = a.keys + static_cast<int64_t>(g - a.row_begin) * a.ldk;
+      const uint16_t* vr = a.values + static_cast<int64_t>(g - a.row_begin) * a.ldv;
+#pragma unroll 4
+      for (int c = lane * 8; c < a.d_k; c += 256) {  // unrolled: the row's loads go out together
+        float fa[8], fr[8];
+        load_a8(a.q, a.q_bf16, m * a.ldq + c, fa);
+        bf16x8(__ldg(reinterpret_cast<const uint4*>(kr + c)), fr);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sj = fmaf(fa[e], fr[e], sj);
+      }
+#pragma unroll 4
+      for (int c = lane * 8; c < a.d_v; c += 256) {
+        float fa[8], fr[8];
+        load_a8(a.dout, 0, m * a.ld_dout + c, fa);
+        bf16x8(__ldg(reinterpret_cast<const uint4*>(vr + c)), fr);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dj = fmaf(fa[e], fr[e], dj);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        sj += __shfl_xor_sync(0xffffffffu, sj, o);
+        dj += __shfl_xor_sync(0xffffffffu, dj, o);
+      }
+    }
+    if (lane == 0) {
+      s_s[j] = sj;
+      da_s[j] = dj;
+    }
+  }
+  __syncthreads();
+  // (2) ds_j and the scalar-parameter terms (score_backward_kernel's formulas)
+  if (w == 0) {
+    float lambda_sharp = a.lambda_sharp, tau = a.tau, T = a.T;
+    bool ok = true;
+    if (a.params != nullptr) {
+      const ScoreParams p = load_score_params(a.params, lambda_sharp, tau, T);
+      lambda_sharp = p.lambda_sharp;
+      tau = p.tau;
+      T = p.T;
+      ok = T > 0.0f && isfinite(T) && (!a.use_sigmoid || (isfinite(lambda_sharp) && isfinite(tau)));
+      if (!ok && lane == 0) record_status(a.status, kStatusDeviceCheck);
+    }
+    float sv = 0.f, sdv = 0.f;
+    for (int j = lane; j < k; j += 32) {
+      const float vj = a.v[m * k + j];
+      sv += vj;
+      sdv += da_s[j] * vj;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      sv += __shfl_xor_sync(0xffffffffu, sv, o);
+      sdv += __shfl_xor_sync(0xffffffffu, sdv, o);
+    }
+    const float den = sv + 1e-8f;
+    float g_lam = 0.f, g_tau = 0.f, g_T = 0.f;
+    for (int j = lane; j < k; j += 32) {
+      const float vj = a.v[m * k + j];
+      const float sj = s_s[j];
+      const float dv = da_s[j] / den - sdv / (den * den);
+      float dvds;
+      if (a.use_sigmoid) {
+        const float gj = 1.0f / (1.0f + expf(-(lambda_sharp * (sj - tau))));
+        dvds = vj * (lambda_sharp * (1.0f - gj) + 1.0f / T);
+        g_lam += dv * vj * (1.0f - gj) * (sj - tau);
+        g_tau += -dv * vj * lambda_sharp * (1.0f - gj);
+      } else {
+        dvds = vj / T;
+      }
+      g_T += -dv * vj * sj / (T * T);
+      const float dsj = ok ? dv * dvds : NAN;
+      ds_s[j] = dsj;
+      a.ds[m * k + j] = dsj;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      g_lam += __shfl_xor_sync(0xffffffffu, g_lam, o);
+      g_tau += __shfl_xor_sync(0xffffffffu, g_tau, o);
+      g_T += __shfl_xor_sync(0xffffffffu, g_T, o);
+    }
+    if (lane == 0) {
+      ok_s = ok ? 1 : 0;
+      if (ok && a.dparams) {
+        atomicAdd(a.dparams + 0, g_lam);
+        atomicAdd(a.dparams + 1, g_tau);
+        atomicAdd(a.dparams + 2, g_T);
+      }
+    }
+  }
+  __syncthreads();
+  // (3) dq[m, c..c+3] = sum_j ds_j K_j[c..c+3]: 4 columns per thread per step,
+  // the k rows in blocks of 8 so eight loads are in flight
+  const bool ok = ok_s != 0;
+  for (int c = tid * 4; c < a.d_k; c += kWarps * 32 * 4) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int j0 = 0; j0 < k; j0 += 8) {
+      uint2 raw[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = j0 + u;
+        const int32_t g = j < k ? g_s[j] : -1;
+        raw[u] = (g >= a.row_begin && g < a.row_end)
+                     ? __ldg(reinterpret_cast<const uint2*>(
+                           a.keys + static_cast<int64_t>(g - a.row_begin) * a.ldk + c))
+                     : make_uint2(0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = j0 + u;
+        const float wj = j < k ? ds_s[j] : 0.f;
+        acc[0] = fmaf(wj, __uint_as_float(raw[u].x << 16), acc[0]);
+        acc[1] = fmaf(wj, __uint_as_float(raw[u].x & 0xFFFF0000u), acc[1]);
+        acc[2] = fmaf(wj, __uint_as_float(raw[u].y << 16), acc[2]);
+        acc[3] = fmaf(wj, __uint_as_float(raw[u].y & 0xFFFF0000u), acc[3]);
+      }
+    }
+    float4 r = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    if (!ok) r = make_float4(NAN, NAN, NAN, NAN);
+    *reinterpret_cast<float4*>(a.dq + m * a.d_k + c) = r;
+  }
+}
+
 inline unsigned blocks_for(int64_t M) { return static_cast<unsigned>((M + kWarps - 1) / kWarps); }
 
 }  // namespace
@@ -236,6 +410,22 @@ cudaError_t launch_gather_rows(const float* wts, const int32_t* idx, int64_t M, 
   gather_rows_kernel<<<blocks_for(M), kWarps * 32, 0, stream>>>(
       wts, idx, M, k, static_cast<const uint16_t*>(rows), row_begin, row_end, ldr, d, out,
       accumulate);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_retrieval_backward(const void* q, int q_bf16, int64_t ldq, const float* dout,
+                                      int64_t ld_dout, const void* keys, int64_t ldk, int d_k,
+                                      const void* values, int64_t ldv, int d_v, const float* v,
+                                      const int32_t* idx, int64_t M, int k, int64_t row_begin,
+                                      int64_t row_end, float lambda_sharp, float tau, float T,
+                                      const float* params, int use_sigmoid, float* ds, float* dq,
+                                      float* dparams, int* status, cudaStream_t stream) {
+  if (M <= 0) return cudaSuccess;
+  if (k < 1 || k > kBwdMaxK) return cudaErrorInvalidValue;
+  FusedBwdArgs a{q, q_bf16, ldq, dout, ld_dout, static_cast<const uint16_t*>(keys), ldk, d_k,
+                 static_cast<const uint16_t*>(values), ldv, d_v, v, idx, M, k, row_begin,
+                 row_end, lambda_sharp, tau, T, params, use_sigmoid, ds, dq, dparams, status};
+  retrieval_backward_kernel<<<static_cast<unsigned>(M), kWarps * 32, 0, stream>>>(a);
   return cudaGetLastError();
 }
 

@@ -412,6 +412,39 @@ dwa_status dwa_score_backward_dev(const float* vals, const float* scores, const 
   return ok();
 }
 
+dwa_status dwa_retrieval_backward(const void* q, int32_t q_is_bf16, int64_t ldq,
+                                  const float* dout, int64_t ld_dout, const void* keys,
+                                  int64_t ldk, int32_t d_k, const void* values, int64_t ldv,
+                                  int32_t d_v, const float* vals, const int32_t* gidx, int64_t M,
+                                  int32_t k, int64_t row_begin, int64_t row_end,
+                                  float lambda_sharp, float tau, float T, const float* params,
+                                  int32_t use_sigmoid, float* dscores, float* dq, float* dparams,
+                                  int32_t* status, dwa_stream_t stream) {
+  const char* fn = "dwa_retrieval_backward";
+  if (M < 0) return fail(DWA_ERR_INVALID_ARG, "%s: negative M", fn);
+  if (M == 0) return ok();
+  if (M > INT32_MAX) return fail(DWA_ERR_UNSUPPORTED_SHAPE, "%s: M too large", fn);
+  if (k > 128) return fail(DWA_ERR_UNSUPPORTED_SHAPE, "%s: k=%d above 128", fn, k);
+  if (!vals || !dscores || !dq) return fail(DWA_ERR_INVALID_ARG, "%s: null vals/dscores/dq", fn);
+  if (!aligned(dq, 16) || d_k % 4 != 0)
+    return fail(DWA_ERR_INVALID_ARG, "%s: dq must be 16-byte aligned", fn);
+  if (params && !status)
+    return fail(DWA_ERR_INVALID_ARG, "%s: device params need a status word", fn);
+  if (!params && (!(T > 0.f) || !std::isfinite(T)))
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "%s: temperature T must be finite and > 0", fn);
+  dwa_status st = check_rows_args(fn, gidx, M, k, keys, row_begin, row_end, ldk, d_k, 8);
+  if (st == DWA_OK) st = check_rows_args(fn, gidx, M, k, values, row_begin, row_end, ldv, d_v, 8);
+  if (st == DWA_OK) st = check_vec_arg(fn, q, q_is_bf16, ldq, d_k);
+  if (st == DWA_OK) st = check_vec_arg(fn, dout, 0, ld_dout, d_v);
+  if (st != DWA_OK) return st;
+  cudaError_t e = dwa::launch_retrieval_backward(
+      q, q_is_bf16 ? 1 : 0, ldq, dout, ld_dout, keys, ldk, d_k, values, ldv, d_v, vals, gidx, M, k,
+      row_begin, row_end, lambda_sharp, tau, T, params, use_sigmoid ? 1 : 0, dscores, dq, dparams,
+      status, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_retrieval_backward launch");
+  return ok();
+}
+
 dwa_status dwa_gather_rows(const float* weights, const int32_t* gidx, int64_t M, int32_t k,
                            const void* rows, int64_t row_begin, int64_t row_end, int64_t ldr,
                            int32_t d, float* out, int32_t accumulate, dwa_stream_t stream) {

@@ -147,6 +147,14 @@ cudaError_t launch_lowrank_delta(const void* h, int h_bf16, int64_t ldh, const f
                                  const int32_t* gidx, int64_t M, int k, const void* vectors,
                                  int64_t row_begin, int64_t row_end, int64_t ldv, int d_A, int d_B,
                                  int r, float* delta, cudaStream_t stream);
+// backward.cu: the queries-side backward of a one-GPU pool in one launch
+cudaError_t launch_retrieval_backward(const void* q, int q_bf16, int64_t ldq, const float* dout,
+                                      int64_t ld_dout, const void* keys, int64_t ldk, int d_k,
+                                      const void* values, int64_t ldv, int d_v, const float* v,
+                                      const int32_t* idx, int64_t M, int k, int64_t row_begin,
+                                      int64_t row_end, float lambda_sharp, float tau, float T,
+                                      const float* params, int use_sigmoid, float* ds, float* dq,
+                                      float* dparams, int* status, cudaStream_t stream);
 // lowrank_rows.cu: the same delta, row-stationary (rows read once), with a caller workspace
 size_t lowrank_rows_workspace_bytes(int64_t M, int k, int64_t n_rows, int d_B);
 int lowrank_rows_smem_bytes(int d_A, int d_B, int r);

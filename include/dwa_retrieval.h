@@ -265,6 +265,31 @@ DWA_API dwa_status dwa_score_backward_dev(const float* vals, const float* scores
                           int64_t M, int32_t k, const float* params, int32_t use_sigmoid,
                           float* dscores, float* dparams, int32_t* status, dwa_stream_t stream);
 
+/*
+ * The queries-side backward in one launch, for a pool held whole by this GPU
+ * (every gidx inside [row_begin, row_end); on a row-sharded pool the partial
+ * dot products must be summed across ranks first, so use dwa_gather_dot +
+ * dwa_score_backward + dwa_gather_rows there).  Per query m:
+ *   s_j = <q[m], keys[gidx_j]>, dalpha_j = <dout[m], values[gidx_j]>,
+ *   dscores as dwa_score_backward, dq[m] = sum_j dscores_j keys[gidx_j],
+ * each selected key and value row read from HBM once.  Results equal the
+ * four-kernel path (same sums in the same order).  q bf16 (q_is_bf16 = 1) or
+ * f32; dout f32 [M, ld_dout]; keys / values bf16 rows; vals f32 [M, k] (the
+ * forward's fused scores); gidx i32 [M, k]; k <= 128.  dscores f32 [M, k],
+ * dq f32 [M, d_k] (16-byte aligned) are written; dparams (3 floats) is
+ * accumulated into and may be NULL.  params: NULL (host lambda_sharp / tau /
+ * T) or three device floats, checked on the device as in
+ * dwa_score_backward_dev (then status, a device int32, may not be NULL).
+ * d_k, d_v, ldk, ldv multiples of 8; all row pointers 16-byte aligned.
+ */
+DWA_API dwa_status dwa_retrieval_backward(const void* q, int32_t q_is_bf16, int64_t ldq,
+                          const float* dout, int64_t ld_dout, const void* keys, int64_t ldk,
+                          int32_t d_k, const void* values, int64_t ldv, int32_t d_v,
+                          const float* vals, const int32_t* gidx, int64_t M, int32_t k,
+                          int64_t row_begin, int64_t row_end, float lambda_sharp, float tau,
+                          float T, const float* params, int32_t use_sigmoid, float* dscores,
+                          float* dq, float* dparams, int32_t* status, dwa_stream_t stream);
+
 /* out[m, :] (= or +=) sum_j w[m, j] rows[gidx[m, j] - row_begin, :] over owned rows. */
 DWA_API dwa_status dwa_gather_rows(const float* weights, const int32_t* gidx, int64_t M, int32_t k,
                           const void* rows, int64_t row_begin, int64_t row_end, int64_t ldr,

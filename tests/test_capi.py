@@ -173,6 +173,16 @@ def test_nvlink_and_projection_entry_points_validate_before_launch():
                                  None) == 2
     assert lib.dwa_lowrank_delta(FAKE, 1, 64, FAKE, FAKE, 4, 2, FAKE, 0, 10, 100, 64, 16, 8, FAKE,
                                  None) == 1
+    # fused backward: limits checked before any launch
+    bwd = lambda **kw: lib.dwa_retrieval_backward(
+        kw.get("q", FAKE), 1, 64, FAKE, 64, FAKE, 64, 64, FAKE, 64, 64, FAKE, FAKE, 4,
+        kw.get("k", 8), 0, 100, 1.0, 0.0, kw.get("T", 1.0), kw.get("params", None), 0,
+        FAKE, kw.get("dq", FAKE), None, kw.get("status", None), None)
+    assert bwd(k=129) == 2                     # k above 128
+    assert bwd(T=0.0) == 2                     # host temperature must be > 0
+    assert bwd(params=FAKE) == 1               # device params need a status word
+    assert bwd(dq=FAKE + 4) == 1               # dq not 16-byte aligned
+    assert bwd(q=None) == 1
     # row-stationary low-rank assembly: same checks, then its own limits
     need = lib.dwa_lowrank_delta_rows_workspace(8192, 16, 16384, 1280)
     assert need >= 8192 * 16 * 1280 * 4 + 8192 * 16 * 4 + 16384 * 8

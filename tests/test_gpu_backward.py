@@ -57,3 +57,61 @@ def test_retrieval_gradients(M, N, d, dv, k, sig):
     if sig:
         _close(lam.grad, lf.grad)
         _close(tau.grad, tf.grad)
+
+
+@pytest.mark.parametrize("M,N,d,dv,k,sig,q_bf16,dev_params",
+                         [(300, 5000, 1024, 512, 64, False, True, False),
+                          (129, 2000, 128, 64, 100, True, True, True),
+                          (33, 700, 40, 24, 7, True, False, False)])
+def test_fused_backward_equals_the_four_kernel_path(M, N, d, dv, k, sig, q_bf16, dev_params):
+    """dwa_retrieval_backward (one launch, each selected row read once) gives
+    the dscores, dq and scalar-parameter sums of dwa_gather_dot x 2 +
+    dwa_score_backward + dwa_gather_rows bit for bit (the same sums in the
+    same order)."""
+    from computd_b200 import _lib
+    from computd_b200.tiled_topk import _stream_handle
+
+    lib = _lib.load()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(M + k)
+    q = torch.randn(M, d, device=dev, generator=g)
+    q = q.to(torch.bfloat16) if q_bf16 else q
+    K = (torch.randn(N, d, device=dev, generator=g) * d ** -0.5).to(torch.bfloat16)
+    V = torch.randn(N, dv, device=dev, generator=g).to(torch.bfloat16)
+    dout = torch.randn(M, dv, device=dev, generator=g)
+    idx = torch.stack([torch.randperm(N, device=dev, generator=g)[:k] for _ in range(M)]).to(
+        torch.int32)
+    v = torch.rand(M, k, device=dev, generator=g) + 0.05   # fused scores of the forward
+    lam, tau, T = 3.0, 0.1, 0.7
+    sh = _stream_handle(dev)
+    qbf = 1 if q_bf16 else 0
+    # the four-kernel path
+    s = torch.empty(M, k, device=dev)
+    dalpha = torch.empty(M, k, device=dev)
+    ds_ref = torch.empty(M, k, device=dev)
+    dq_ref = torch.empty(M, d, device=dev)
+    dp_ref = torch.zeros(3, device=dev)
+    assert lib.dwa_gather_dot(dout.data_ptr(), 0, dv, idx.data_ptr(), M, k, V.data_ptr(), 0, N,
+                              dv, dv, dalpha.data_ptr(), sh) == 0
+    assert lib.dwa_gather_dot(q.data_ptr(), qbf, d, idx.data_ptr(), M, k, K.data_ptr(), 0, N, d, d,
+                              s.data_ptr(), sh) == 0
+    assert lib.dwa_score_backward(v.data_ptr(), s.data_ptr(), dalpha.data_ptr(), M, k, lam, tau, T,
+                                  int(sig), ds_ref.data_ptr(), dp_ref.data_ptr(), sh) == 0
+    assert lib.dwa_gather_rows(ds_ref.data_ptr(), idx.data_ptr(), M, k, K.data_ptr(), 0, N, d, d,
+                               dq_ref.data_ptr(), 0, sh) == 0
+    # one launch
+    ds = torch.empty(M, k, device=dev)
+    dq = torch.empty(M, d, device=dev)
+    dp = torch.zeros(3, device=dev)
+    params = torch.tensor([lam, tau, T], device=dev) if dev_params else None
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    assert lib.dwa_retrieval_backward(
+        q.data_ptr(), qbf, d, dout.data_ptr(), dv, K.data_ptr(), d, d, V.data_ptr(), dv, dv,
+        v.data_ptr(), idx.data_ptr(), M, k, 0, N, lam, tau, T,
+        params.data_ptr() if dev_params else None, int(sig), ds.data_ptr(), dq.data_ptr(),
+        dp.data_ptr(), status.data_ptr() if dev_params else None, sh) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(ds, ds_ref)
+    assert torch.equal(dq, dq_ref)
+    torch.testing.assert_close(dp, dp_ref, rtol=1e-5, atol=1e-6)  # atomics: order varies
+    assert int(status.item()) == 0
