@@ -121,6 +121,11 @@ def test_lowrank_rows_skewed_rows_and_determinism(lib):
     a2 = lib.lowrank_delta(h, alpha, idx, vectors, d_A, d_B, r, rows=True)
     torch.testing.assert_close(a1, ref, rtol=1e-4, atol=1e-4)
     assert torch.equal(a1, a2)
+    # h as a column slice of a wider activation (row stride 320 > d_A)
+    wide = torch.zeros((M, d_A + 64), dtype=torch.bfloat16, device=_dev())
+    wide[:, 32:32 + d_A] = h
+    a3 = lib.lowrank_delta(wide[:, 32:32 + d_A], alpha, idx, vectors, d_A, d_B, r, rows=True)
+    assert torch.equal(a3, a1)
 
 
 def test_lowrank_rows_reference_1b_layout(lib):
