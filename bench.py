@@ -625,9 +625,9 @@ def measure_backward(local_rank, warmup=2, steps=5):
 
     Two timings: the backward with only the queries requiring grad (one
     launch of dwa_retrieval_backward: <dout, V[idx]> and <q, K[idx]>, the
-    score derivative and the ds-weighted key-row sum), and the full backward, which
-    also scatter-adds into dense f32 key and value gradients of the whole pool
-    (8 GiB zero-filled, then converted to bf16: allocation work, not kernels)."""
+    score derivative and the ds-weighted key-row sum), and the full backward,
+    which also writes the dense bf16 key and value gradients of the whole pool
+    (dwa_row_gradient: 2 GiB each, every row written once)."""
     import torch
 
     import computd_b200 as cb

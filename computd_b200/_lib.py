@@ -88,6 +88,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                       _c_void_p, _i64, _i32, _c_void_p, _c_void_p, _i64, _i32,
                                       _i64, _i64, _f32, _f32, _f32, _c_void_p, _i32, _c_void_p,
                                       _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
+    "dwa_row_gradient_workspace": (ctypes.c_size_t, [_i64, _i32, _i64]),
+    "dwa_row_gradient": (_i32, [_c_void_p, _c_void_p, _i64, _i32, _c_void_p, _i32, _i64, _i64, _i64,
+                                _c_void_p, _i32, _i64, _i32, _c_void_p, ctypes.c_size_t,
+                                _c_void_p]),
     "dwa_lowrank_delta_rows_workspace": (ctypes.c_size_t, [_i64, _i32, _i64, _i32]),
     "dwa_lowrank_delta_rows": (_i32, [_c_void_p, _i32, _i64, _c_void_p, _c_void_p, _i64, _i32,
                                       _c_void_p, _i64, _i64, _i64, _i32, _i32, _i32, _c_void_p,

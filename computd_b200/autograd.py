@@ -48,6 +48,27 @@ def gather_dot(a: torch.Tensor, idx: torch.Tensor, rows: torch.Tensor, row_begin
     return out
 
 
+def _row_gradient(w: torch.Tensor, idx: torch.Tensor, a: torch.Tensor, row_begin: int, n_rows: int,
+                  d: int, dtype: torch.dtype, stream) -> torch.Tensor:
+    """grad [n_rows, d] of the owned rows: sum of w[m, j] a[m] over the entries
+    that selected each row, zero elsewhere (dwa_row_gradient), bf16 or f32."""
+    M, k = idx.shape
+    dev = a.device
+    out_dtype = dtype if dtype in (torch.bfloat16, torch.float32) else torch.float32
+    grad = torch.empty((n_rows, d), dtype=out_dtype, device=dev)
+    lib = _lib.load()
+    ws = torch.empty(max(int(lib.dwa_row_gradient_workspace(M, k, n_rows)), 256), dtype=torch.uint8,
+                     device=dev)
+    pa, abf, lda = _vec_args(a)
+    with torch.cuda.device(dev):
+        st = lib.dwa_row_gradient(w.data_ptr(), idx.data_ptr(), M, k, pa, abf, lda, row_begin,
+                                  row_begin + n_rows, grad.data_ptr(),
+                                  1 if out_dtype == torch.bfloat16 else 0, grad.stride(0), d,
+                                  ws.data_ptr(), ws.numel(), stream)
+    _lib.check(st, "dwa_row_gradient")
+    return grad.to(dtype)
+
+
 class _RetrievalFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, queries, keys, values, lam, tau, T, k, use_sigmoid, group):
@@ -116,24 +137,15 @@ class _RetrievalFn(torch.autograd.Function):
                                              row_begin, row_begin + kk.shape[0], kk.stride(0), d_k,
                                              dq.data_ptr(), 0, sh)
                     _lib.check(st, "dwa_gather_rows")
-        with torch.cuda.device(dev):
-            if ctx.needs_input_grad[1]:
-                grad_k = torch.zeros((kk.shape[0], d_k), dtype=torch.float32, device=dev)
-                pa, abf, lda = _vec_args(q)
-                st = lib.dwa_scatter_add_rows(ds.data_ptr(), ti.data_ptr(), M, k, pa, abf, lda,
-                                              row_begin, row_begin + kk.shape[0],
-                                              grad_k.data_ptr(), grad_k.stride(0), d_k, sh)
-                _lib.check(st, "dwa_scatter_add_rows")
-            if ctx.needs_input_grad[2]:
-                grad_v = torch.zeros((vv.shape[0], d_v), dtype=torch.float32, device=dev)
-                pa, abf, lda = _vec_args(dout)
-                st = lib.dwa_scatter_add_rows(alpha.data_ptr(), ti.data_ptr(), M, k, pa, abf, lda,
-                                              row_begin, row_begin + vv.shape[0],
-                                              grad_v.data_ptr(), grad_v.stride(0), d_v, sh)
-                _lib.check(st, "dwa_scatter_add_rows")
+        qd, kd, vd = ctx.in_dtypes
+        # dK[r] = sum ds q over the entries that selected row r, dV[r] = sum alpha dout:
+        # the whole owned gradient written once, in the parameter's dtype
+        if ctx.needs_input_grad[1]:
+            grad_k = _row_gradient(ds, ti, q, row_begin, kk.shape[0], d_k, kd, sh)
+        if ctx.needs_input_grad[2]:
+            grad_v = _row_gradient(alpha, ti, dout, row_begin, vv.shape[0], d_v, vd, sh)
         if dq is not None and world > 1:
             dist.all_reduce(dq, group=group)
-        qd, kd, vd = ctx.in_dtypes
         grads_p = [dparams[i].clone() if ctx.param_tensors[i] and ctx.needs_input_grad[3 + i] else None
                    for i in range(3)]
         return (dq.to(qd) if dq is not None else None,

@@ -18,6 +18,7 @@
 // Every kernel works on an owned row range [row_begin, row_end) of the pool
 // (owner-computes): on a sharded pool each rank's partial dalpha / s / dq are
 // summed with one all-reduce, and each rank updates only its own rows.
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -379,6 +380,60 @@ __global__ void __launch_bounds__(kWarps * 32, 1) retrieval_backward_kernel(cons
   }
 }
 
+// ---------------------------------------------------------------- dense row gradients
+// grad[r, :] = sum over the pairs (m, j) that selected owned row r of
+// w[m, j] a[m, :] (fp32 sums), written for every owned row (zero where no
+// pair selected it) in bf16 or f32: the whole dense gradient in one write,
+// from the row-sorted pair list (pair_sort.cu), with no float atomics and no
+// separate zero fill or dtype conversion.  One warp per row, 8 columns per lane.
+struct RowGradArgs {
+  const float* w;
+  const int32_t* offsets;
+  const int32_t* pairs;
+  int k;
+  const void* a;
+  int a_bf16;
+  int64_t lda;
+  int64_t n_rows;
+  void* grad;
+  int64_t ldg;
+  int d;
+};
+
+template <bool OUT_BF16>
+__global__ void __launch_bounds__(kWarps * 32) row_gradient_kernel(const RowGradArgs g) {
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * kWarps + w;
+  if (r >= g.n_rows) return;
+  const int32_t p0 = g.offsets[r], p1 = g.offsets[r + 1];
+  for (int c = lane * 8; c < g.d; c += 256) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int32_t p = p0; p < p1; ++p) {
+      const int32_t pid = g.pairs[p];
+      const float wt = g.w[pid];
+      float x[8];
+      load_a8(g.a, g.a_bf16, static_cast<int64_t>(pid / g.k) * g.lda + c, x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = fmaf(wt, x[e], acc[e]);
+    }
+    if constexpr (OUT_BF16) {
+      uint32_t packed[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(acc[2 * e]));
+        const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(acc[2 * e + 1]));
+        packed[e] = lo | (hi << 16);
+      }
+      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(g.grad) + r * g.ldg + c) =
+          make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    } else {
+      float4* dst = reinterpret_cast<float4*>(static_cast<float*>(g.grad) + r * g.ldg + c);
+      dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+  }
+}
+
 inline unsigned blocks_for(int64_t M) { return static_cast<unsigned>((M + kWarps - 1) / kWarps); }
 
 }  // namespace
@@ -426,6 +481,33 @@ cudaError_t launch_retrieval_backward(const void* q, int q_bf16, int64_t ldq, co
                  static_cast<const uint16_t*>(values), ldv, d_v, v, idx, M, k, row_begin,
                  row_end, lambda_sharp, tau, T, params, use_sigmoid, ds, dq, dparams, status};
   retrieval_backward_kernel<<<static_cast<unsigned>(M), kWarps * 32, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+size_t row_gradient_workspace_bytes(int64_t M, int k, int64_t n_rows) {
+  return pair_sort_workspace_bytes(M * k, n_rows);
+}
+
+cudaError_t launch_row_gradient(const float* w, const int32_t* idx, int64_t M, int k, const void* a,
+                                int a_bf16, int64_t lda, int64_t row_begin, int64_t row_end,
+                                void* grad, int grad_bf16, int64_t ldg, int d, void* ws,
+                                cudaStream_t stream) {
+  const int64_t n_rows = row_end - row_begin;
+  if (n_rows <= 0) return cudaSuccess;
+  const size_t row_bytes = static_cast<size_t>(d) * (grad_bf16 ? 2 : 4);
+  if (M <= 0) {  // no pairs: the gradient is zero
+    return cudaMemset2DAsync(grad, static_cast<size_t>(ldg) * (grad_bf16 ? 2 : 4), 0, row_bytes,
+                             static_cast<size_t>(n_rows), stream);
+  }
+  PairSort sorted;
+  cudaError_t e = launch_sort_pairs_by_row(idx, M * k, row_begin, row_end, ws, &sorted, stream);
+  if (e != cudaSuccess) return e;
+  RowGradArgs g{w, sorted.offsets, sorted.pairs, k, a, a_bf16, lda, n_rows, grad, ldg, d};
+  const unsigned blocks = static_cast<unsigned>((n_rows + kWarps - 1) / kWarps);
+  if (grad_bf16)
+    row_gradient_kernel<true><<<blocks, kWarps * 32, 0, stream>>>(g);
+  else
+    row_gradient_kernel<false><<<blocks, kWarps * 32, 0, stream>>>(g);
   return cudaGetLastError();
 }
 

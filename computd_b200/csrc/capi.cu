@@ -445,6 +445,39 @@ dwa_status dwa_retrieval_backward(const void* q, int32_t q_is_bf16, int64_t ldq,
   return ok();
 }
 
+size_t dwa_row_gradient_workspace(int64_t M, int32_t k, int64_t n_rows) {
+  if (M < 0 || k < 1 || n_rows < 0) return 0;
+  return dwa::row_gradient_workspace_bytes(M, k, n_rows);
+}
+
+dwa_status dwa_row_gradient(const float* weights, const int32_t* gidx, int64_t M, int32_t k,
+                            const void* a, int32_t a_is_bf16, int64_t lda, int64_t row_begin,
+                            int64_t row_end, void* grad, int32_t grad_is_bf16, int64_t ldg,
+                            int32_t d, void* workspace, size_t workspace_bytes,
+                            dwa_stream_t stream) {
+  const char* fn = "dwa_row_gradient";
+  if (M < 0) return fail(DWA_ERR_INVALID_ARG, "%s: negative M", fn);
+  if (M * static_cast<int64_t>(k) > INT32_MAX)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "%s: M k above INT32_MAX", fn);
+  dwa_status st = check_rows_args(fn, gidx, M, k, grad, row_begin, row_end, ldg, d, 8);
+  if (st != DWA_OK) return st;
+  if (row_end == row_begin) return ok();  // no owned rows: nothing to write
+  if (M > 0) {
+    if (!weights) return fail(DWA_ERR_INVALID_ARG, "%s: null weights", fn);
+    st = check_vec_arg(fn, a, a_is_bf16, lda, d);
+    if (st != DWA_OK) return st;
+    const size_t need = dwa::row_gradient_workspace_bytes(M, k, row_end - row_begin);
+    if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+      return fail(DWA_ERR_WORKSPACE, "%s: workspace needs %zu bytes, 256-byte aligned (got %zu)",
+                  fn, need, workspace_bytes);
+  }
+  cudaError_t e = dwa::launch_row_gradient(weights, gidx, M, k, a, a_is_bf16 ? 1 : 0, lda,
+                                           row_begin, row_end, grad, grad_is_bf16 ? 1 : 0, ldg, d,
+                                           workspace, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_row_gradient launch");
+  return ok();
+}
+
 dwa_status dwa_gather_rows(const float* weights, const int32_t* gidx, int64_t M, int32_t k,
                            const void* rows, int64_t row_begin, int64_t row_end, int64_t ldr,
                            int32_t d, float* out, int32_t accumulate, dwa_stream_t stream) {

@@ -155,6 +155,21 @@ cudaError_t launch_retrieval_backward(const void* q, int q_bf16, int64_t ldq, co
                                       int64_t row_end, float lambda_sharp, float tau, float T,
                                       const float* params, int use_sigmoid, float* ds, float* dq,
                                       float* dparams, int* status, cudaStream_t stream);
+// pair_sort.cu: (query, entry) pairs of an index array sorted by owned row
+struct PairSort {
+  int32_t* offsets;  // [n_rows + 1]: pairs of owned row r at pairs[offsets[r] .. offsets[r + 1])
+  int32_t* pairs;    // pair ids (indices into gidx)
+};
+size_t pair_sort_workspace_bytes(int64_t n_pairs, int64_t n_rows);
+cudaError_t launch_sort_pairs_by_row(const int32_t* gidx, int64_t n_pairs, int64_t row_begin,
+                                     int64_t row_end, void* ws, PairSort* out,
+                                     cudaStream_t stream);
+// backward.cu: dense row gradients from the row-sorted pairs (pair_sort workspace)
+size_t row_gradient_workspace_bytes(int64_t M, int k, int64_t n_rows);
+cudaError_t launch_row_gradient(const float* w, const int32_t* idx, int64_t M, int k, const void* a,
+                                int a_bf16, int64_t lda, int64_t row_begin, int64_t row_end,
+                                void* grad, int grad_bf16, int64_t ldg, int d, void* ws,
+                                cudaStream_t stream);
 // lowrank_rows.cu: the same delta, row-stationary (rows read once), with a caller workspace
 size_t lowrank_rows_workspace_bytes(int64_t M, int k, int64_t n_rows, int d_B);
 int lowrank_rows_smem_bytes(int d_A, int d_B, int r);

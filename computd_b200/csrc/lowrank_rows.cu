@@ -8,9 +8,8 @@
 // every selected row once per token that selected it: at the reference's 1B
 // layout (8192 tokens x k = 16 over 16,384 rows of 43.5 KB) that is 5.7 GB of
 // row reads from a 713 MB pool.  Here:
-//   1. count the (token, entry) pairs per owned row, exclusive-scan the counts,
-//      scatter the pair ids into a row-sorted list (the order inside a row is
-//      irrelevant: every pair writes its own slot);
+//   1. sort the (token, entry) pairs by owned row (pair_sort.cu; the order
+//      inside a row is irrelevant: every pair writes its own slot);
 //   2. each CTA takes 32 consecutive pairs of that list, stages each row it
 //      meets (U | V | b, 43.5 KB) in shared memory once, and one warp per pair
 //      computes alpha (U_j (V_j h[m]) + b_j) into the pair's own fp32 slot
@@ -36,143 +35,16 @@ namespace {
 constexpr int kRowThreads = 256;
 constexpr int kRowWarps = kRowThreads / 32;
 constexpr int kPairsPerCta = 32;
-constexpr int kScanThreads = 1024;
-constexpr int kScanPerThread = 4;
-constexpr int kScanTile = kScanThreads * kScanPerThread;  // elements per scan block
 
 size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
 
-struct RowsWorkspace {
-  int32_t* offsets;  // [n_rows + 1]: exclusive scan of the per-row pair counts
-  int32_t* cursor;   // [n_rows]: counts, then scatter cursors
-  int32_t* pairs;    // [M k]: pair ids m k + e, sorted by row
-  int32_t* block_sums;  // [n_scan_blocks + 1]
-  float* part;       // [M k, d_B]: alpha (U_j (V_j h[m]) + b_j) per pair
-};
-
-RowsWorkspace carve(void* ws, int64_t M, int k, int64_t n_rows, int d_B) {
-  uint8_t* p = static_cast<uint8_t*>(ws);
-  RowsWorkspace w;
-  const int64_t n_pairs = M * k;
-  const int64_t n_blocks = (n_rows + kScanTile - 1) / kScanTile;
-  w.offsets = reinterpret_cast<int32_t*>(p);
-  p += up256(static_cast<size_t>(n_rows + 1) * 4);
-  w.cursor = reinterpret_cast<int32_t*>(p);
-  p += up256(static_cast<size_t>(n_rows) * 4);
-  w.pairs = reinterpret_cast<int32_t*>(p);
-  p += up256(static_cast<size_t>(n_pairs) * 4);
-  w.block_sums = reinterpret_cast<int32_t*>(p);
-  p += up256(static_cast<size_t>(n_blocks + 1) * 4);
-  w.part = reinterpret_cast<float*>(p);
-  (void)d_B;
-  return w;
+// Workspace: the row-sorted pair list (pair_sort.cu), then the per-pair slots.
+float* part_slots(void* ws, int64_t n_pairs, int64_t n_rows) {
+  return reinterpret_cast<float*>(static_cast<uint8_t*>(ws) +
+                                  up256(pair_sort_workspace_bytes(n_pairs, n_rows)));
 }
 
-// ---------------------------------------------------------------- 1. row-sorted pair list
-__global__ void count_rows_kernel(const int32_t* gidx, int64_t n_pairs, int64_t row_begin,
-                                  int64_t row_end, int32_t* counts) {
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n_pairs;
-       i += stride) {
-    const int32_t g = gidx[i];
-    if (g >= row_begin && g < row_end) atomicAdd(counts + (g - row_begin), 1);
-  }
-}
-
-// Exclusive scan of v over the block's 1024 threads; *total receives the sum.
-__device__ __forceinline__ int32_t block_exclusive_scan(int32_t v, int32_t* warp_sums,
-                                                        int32_t* total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int32_t x = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += y;
-  }
-  if (lane == 31) warp_sums[warp] = x;
-  __syncthreads();
-  if (warp == 0) {
-    int32_t w = warp_sums[lane];
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int32_t y = __shfl_up_sync(0xffffffffu, w, o);
-      if (lane >= o) w += y;
-    }
-    warp_sums[lane] = w;  // inclusive over warps
-  }
-  __syncthreads();
-  const int32_t before_warp = warp > 0 ? warp_sums[warp - 1] : 0;
-  *total = warp_sums[31];
-  __syncthreads();  // warp_sums is reused by the caller's next scan
-  return before_warp + x - v;
-}
-
-// Per tile of kScanTile counts: tile-local exclusive offsets and the tile total.
-__global__ void __launch_bounds__(kScanThreads) scan_tiles_kernel(const int32_t* counts,
-                                                                  int64_t n, int32_t* offsets,
-                                                                  int32_t* block_sums) {
-  __shared__ int32_t warp_sums[32];
-  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanTile + threadIdx.x * kScanPerThread;
-  int32_t c[kScanPerThread];
-  int32_t sum = 0;
-#pragma unroll
-  for (int u = 0; u < kScanPerThread; ++u) {
-    c[u] = base + u < n ? counts[base + u] : 0;
-    sum += c[u];
-  }
-  int32_t total;
-  int32_t run = block_exclusive_scan(sum, warp_sums, &total);
-#pragma unroll
-  for (int u = 0; u < kScanPerThread; ++u) {
-    if (base + u < n) offsets[base + u] = run;
-    run += c[u];
-  }
-  if (threadIdx.x == 0) block_sums[blockIdx.x] = total;
-}
-
-// One block: exclusive scan of the tile totals in place, the grand total after them.
-__global__ void __launch_bounds__(kScanThreads) scan_block_sums_kernel(int32_t* block_sums,
-                                                                       int64_t n_blocks) {
-  __shared__ int32_t warp_sums[32];
-  int32_t carry = 0;
-  for (int64_t b0 = 0; b0 < n_blocks; b0 += kScanThreads) {
-    const int64_t i = b0 + threadIdx.x;
-    const int32_t v = i < n_blocks ? block_sums[i] : 0;
-    int32_t total;
-    const int32_t ex = block_exclusive_scan(v, warp_sums, &total);
-    if (i < n_blocks) block_sums[i] = carry + ex;
-    carry += total;
-  }
-  if (threadIdx.x == 0) block_sums[n_blocks] = carry;
-}
-
-// offsets += tile base; offsets[n] = total; cursor = offsets.
-__global__ void scan_finish_kernel(int32_t* offsets, int32_t* cursor, const int32_t* block_sums,
-                                   int64_t n, int64_t n_blocks) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i < n) {
-    const int32_t o = offsets[i] + block_sums[i / kScanTile];
-    offsets[i] = o;
-    cursor[i] = o;
-  } else if (i == n) {
-    offsets[n] = block_sums[n_blocks];
-  }
-}
-
-__global__ void scatter_pairs_kernel(const int32_t* gidx, int64_t n_pairs, int64_t row_begin,
-                                     int64_t row_end, int32_t* cursor, int32_t* pairs) {
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n_pairs;
-       i += stride) {
-    const int32_t g = gidx[i];
-    if (g >= row_begin && g < row_end) {
-      const int32_t pos = atomicAdd(cursor + (g - row_begin), 1);
-      pairs[pos] = static_cast<int32_t>(i);
-    }
-  }
-}
-
-// ---------------------------------------------------------------- 2. rows x their tokens
+// ---------------------------------------------------------------- rows x their tokens
 struct RowsArgs {
   const void* h;
   int64_t ldh;
@@ -315,7 +187,7 @@ __global__ void __launch_bounds__(kRowThreads) lowrank_rows_kernel(const RowsArg
   }
 }
 
-// ---------------------------------------------------------------- 3. per-token sums
+// ---------------------------------------------------------------- per-token sums
 // delta[m, 4c..4c+3] = sum over the owned entries e of part[m k + e, 4c..], in entry order.
 __global__ void lowrank_rows_sum_kernel(const float* part, const int32_t* gidx, int64_t M, int k,
                                         int d_B, int64_t row_begin, int64_t row_end,
@@ -344,9 +216,7 @@ __global__ void lowrank_rows_sum_kernel(const float* part, const int32_t* gidx, 
 
 size_t lowrank_rows_workspace_bytes(int64_t M, int k, int64_t n_rows, int d_B) {
   const int64_t n_pairs = M * k;
-  const int64_t n_blocks = (n_rows + kScanTile - 1) / kScanTile;
-  return up256(static_cast<size_t>(n_rows + 1) * 4) + up256(static_cast<size_t>(n_rows) * 4) +
-         up256(static_cast<size_t>(n_pairs) * 4) + up256(static_cast<size_t>(n_blocks + 1) * 4) +
+  return up256(pair_sort_workspace_bytes(n_pairs, n_rows)) +
          up256(static_cast<size_t>(n_pairs) * static_cast<size_t>(d_B) * 4);
 }
 
@@ -376,29 +246,14 @@ cudaError_t launch_lowrank_rows(const void* h, int h_bf16, int64_t ldh, const fl
   if (n_rows == 0) {  // nothing owned: the partial sum is zero
     return cudaMemsetAsync(delta, 0, static_cast<size_t>(M) * d_B * 4, stream);
   }
-  RowsWorkspace w = carve(ws, M, k, n_rows, d_B);
-  int dev = 0, sms = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess)
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const unsigned pair_grid =
-      static_cast<unsigned>(std::min<int64_t>((n_pairs + 255) / 256, static_cast<int64_t>(sms) * 8));
-  cudaError_t e = cudaMemsetAsync(w.cursor, 0, static_cast<size_t>(n_rows) * 4, stream);
+  PairSort sorted;
+  cudaError_t e = launch_sort_pairs_by_row(gidx, n_pairs, row_begin, row_end, ws, &sorted, stream);
   if (e != cudaSuccess) return e;
-  count_rows_kernel<<<pair_grid, 256, 0, stream>>>(gidx, n_pairs, row_begin, row_end, w.cursor);
-  const int64_t n_blocks = (n_rows + kScanTile - 1) / kScanTile;
-  scan_tiles_kernel<<<static_cast<unsigned>(n_blocks), kScanThreads, 0, stream>>>(
-      w.cursor, n_rows, w.offsets, w.block_sums);
-  scan_block_sums_kernel<<<1, kScanThreads, 0, stream>>>(w.block_sums, n_blocks);
-  scan_finish_kernel<<<static_cast<unsigned>((n_rows + 1 + 255) / 256), 256, 0, stream>>>(
-      w.offsets, w.cursor, w.block_sums, n_rows, n_blocks);
-  scatter_pairs_kernel<<<pair_grid, 256, 0, stream>>>(gidx, n_pairs, row_begin, row_end, w.cursor,
-                                                      w.pairs);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  float* part = part_slots(ws, n_pairs, n_rows);
 
   RowsArgs a{h, ldh, alpha, gidx, k, static_cast<const __nv_bfloat16*>(vectors), row_begin, ldv,
-             d_A, d_B, r, lowrank_rows_smem_bytes(d_A, d_B, r) / 16, w.offsets, w.pairs, n_rows,
-             w.part};
+             d_A, d_B, r, lowrank_rows_smem_bytes(d_A, d_B, r) / 16, sorted.offsets, sorted.pairs,
+             n_rows, part};
   const unsigned row_grid = static_cast<unsigned>((n_pairs + kPairsPerCta - 1) / kPairsPerCta);
   const int smem = a.row_words * 16;
   const bool vec_u = r % 8 == 0;
@@ -419,7 +274,7 @@ cudaError_t launch_lowrank_rows(const void* h, int h_bf16, int64_t ldh, const fl
   }
   if (e != cudaSuccess) return e;
   lowrank_rows_sum_kernel<<<static_cast<unsigned>((sum_threads + 255) / 256), 256, 0, stream>>>(
-      w.part, gidx, M, k, d_B, row_begin, row_end, delta);
+      part, gidx, M, k, d_B, row_begin, row_end, delta);
   return cudaGetLastError();
 }
 

@@ -290,6 +290,27 @@ DWA_API dwa_status dwa_retrieval_backward(const void* q, int32_t q_is_bf16, int6
                           float T, const float* params, int32_t use_sigmoid, float* dscores,
                           float* dq, float* dparams, int32_t* status, dwa_stream_t stream);
 
+/*
+ * The dense gradient of the owned pool rows in one write, from the selections:
+ *   grad[r, :] = sum over (m, j) with gidx[m, j] == row_begin + r of w[m, j] a[m, :]
+ * for every owned row r (zero where no entry selected it), summed in f32 and
+ * stored as bf16 (grad_is_bf16 = 1) or f32.  The same values as zero-filling
+ * an f32 gradient, dwa_scatter_add_rows into it and converting, without the
+ * zero fill, the float atomics or the conversion pass: the (m, j) entries are
+ * sorted by row first (a counting sort in the workspace), then one warp per
+ * row sums its entries (in an order the sort leaves unspecified, as the
+ * atomics do).  w f32 [M, k]; a: [M, lda] bf16 or f32 rows; grad [row_end -
+ * row_begin, ldg]; d, lda, ldg multiples of 8; 16-byte aligned rows.
+ * workspace: >= dwa_row_gradient_workspace(M, k, row_end - row_begin) bytes,
+ * 256-byte aligned.  M k <= INT32_MAX.
+ */
+DWA_API size_t dwa_row_gradient_workspace(int64_t M, int32_t k, int64_t n_rows);
+DWA_API dwa_status dwa_row_gradient(const float* weights, const int32_t* gidx, int64_t M,
+                                    int32_t k, const void* a, int32_t a_is_bf16, int64_t lda,
+                                    int64_t row_begin, int64_t row_end, void* grad,
+                                    int32_t grad_is_bf16, int64_t ldg, int32_t d, void* workspace,
+                                    size_t workspace_bytes, dwa_stream_t stream);
+
 /* out[m, :] (= or +=) sum_j w[m, j] rows[gidx[m, j] - row_begin, :] over owned rows. */
 DWA_API dwa_status dwa_gather_rows(const float* weights, const int32_t* gidx, int64_t M, int32_t k,
                           const void* rows, int64_t row_begin, int64_t row_end, int64_t ldr,

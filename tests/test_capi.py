@@ -173,6 +173,15 @@ def test_nvlink_and_projection_entry_points_validate_before_launch():
                                  None) == 2
     assert lib.dwa_lowrank_delta(FAKE, 1, 64, FAKE, FAKE, 4, 2, FAKE, 0, 10, 100, 64, 16, 8, FAKE,
                                  None) == 1
+    # dense row gradient: workspace and limits checked before any launch
+    assert lib.dwa_row_gradient_workspace(8192, 64, 1 << 20) >= 8192 * 64 * 4 + (1 << 20) * 8
+    rg = lambda **kw: lib.dwa_row_gradient(FAKE, FAKE, kw.get("M", 4), 8, FAKE, 1, 64, 0, 100, FAKE,
+                                           1, 64, kw.get("d", 64), kw.get("ws", FAKE),
+                                           kw.get("ws_bytes", 1 << 30), None)
+    assert rg(ws=None) == _lib.DWA_ERR_WORKSPACE
+    assert rg(ws_bytes=16) == _lib.DWA_ERR_WORKSPACE
+    assert rg(d=12) == 2
+    assert rg(M=1 << 29) == 2                  # M k above INT32_MAX
     # fused backward: limits checked before any launch
     bwd = lambda **kw: lib.dwa_retrieval_backward(
         kw.get("q", FAKE), 1, 64, FAKE, 64, FAKE, 64, 64, FAKE, 64, 64, FAKE, FAKE, 4,

@@ -115,3 +115,50 @@ def test_fused_backward_equals_the_four_kernel_path(M, N, d, dv, k, sig, q_bf16,
     assert torch.equal(dq, dq_ref)
     torch.testing.assert_close(dp, dp_ref, rtol=1e-5, atol=1e-6)  # atomics: order varies
     assert int(status.item()) == 0
+
+
+@pytest.mark.parametrize("out_bf16", [False, True])
+def test_row_gradient_equals_zero_fill_and_scatter(out_bf16):
+    """dwa_row_gradient (one write of the owned rows) against zero-filled f32 +
+    dwa_scatter_add_rows: the same sums (their order may differ), untouched
+    rows exactly zero, an owned sub-range, bf16 output = the f32 result rounded."""
+    from computd_b200 import _lib
+    from computd_b200.tiled_topk import _stream_handle
+
+    lib = _lib.load()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(7)
+    M, k, N, d = 500, 16, 3000, 96
+    a = torch.randn(M, d, device=dev, generator=g).to(torch.bfloat16)
+    w = torch.randn(M, k, device=dev, generator=g)
+    idx = torch.randint(0, N, (M, k), device=dev, generator=g, dtype=torch.int32)
+    idx[:, 0] = 11                         # one row selected by every query
+    sh = _stream_handle(dev)
+    for rb, re in ((0, N), (1000, 2200)):
+        n = re - rb
+        ref = torch.zeros(n, d, device=dev)
+        assert lib.dwa_scatter_add_rows(w.data_ptr(), idx.data_ptr(), M, k, a.data_ptr(), 1, d, rb,
+                                        re, ref.data_ptr(), d, d, sh) == 0
+        out = torch.full((n, d), float("nan"), device=dev,
+                         dtype=torch.bfloat16 if out_bf16 else torch.float32)
+        ws = torch.empty(max(int(lib.dwa_row_gradient_workspace(M, k, n)), 256), dtype=torch.uint8,
+                         device=dev)
+        assert lib.dwa_row_gradient(w.data_ptr(), idx.data_ptr(), M, k, a.data_ptr(), 1, d, rb, re,
+                                    out.data_ptr(), int(out_bf16), d, d, ws.data_ptr(), ws.numel(),
+                                    sh) == 0
+        torch.cuda.synchronize()
+        sel = torch.zeros(n, dtype=torch.bool, device=dev)
+        own = (idx >= rb) & (idx < re)
+        sel[(idx[own] - rb).long()] = True
+        assert bool((out[~sel] == 0).all())       # untouched rows written as zeros
+        if out_bf16:
+            torch.testing.assert_close(out.float(), ref.to(torch.bfloat16).float(), rtol=1e-2,
+                                       atol=1e-2)
+        else:
+            torch.testing.assert_close(out, ref, rtol=1e-5, atol=1e-5)
+    # no queries: the whole owned gradient is zero
+    out = torch.full((N, d), 1.0, device=dev)
+    assert lib.dwa_row_gradient(w.data_ptr(), idx.data_ptr(), 0, k, a.data_ptr(), 1, d, 0, N,
+                                out.data_ptr(), 0, d, d, None, 0, sh) == 0
+    torch.cuda.synchronize()
+    assert bool((out == 0).all())
