@@ -76,6 +76,71 @@ __device__ __forceinline__ float dot8(const uint4 w, const float (&x)[8]) {
   return s;
 }
 
+// One warp applies the staged row (U | V | b in row_s) to pair pid:
+// hV = alpha V_j h[m] (lanes over d_A, butterfly sums), then
+// part[pid, i] = sum_t U_j[i, t] hV[t] + alpha b_j[i] (lanes over i).
+template <int RMAX, bool HBF16, bool VEC_U>
+__device__ __forceinline__ void apply_pair(const RowsArgs& a, const uint4* row_s, int32_t pid,
+                                           int lane, int v_word0, int a_words, int b_elem0) {
+  const int r = a.r;
+  const __nv_bfloat16* row_bf = reinterpret_cast<const __nv_bfloat16*>(row_s);
+  const int64_t m = pid / a.k;
+  const float al = a.alpha[pid];
+  float acc[RMAX];
+#pragma unroll
+  for (int t = 0; t < RMAX; ++t) acc[t] = 0.f;
+#pragma unroll 4
+  for (int c = lane; c < a_words; c += 32) {  // unrolled: the h loads (L2) go out together
+    float x[8];
+    if constexpr (HBF16) {
+      const uint4 hw =
+          __ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.h) +
+                                               m * a.ldh) + c);
+      x[0] = bf_lo(hw.x); x[1] = bf_hi(hw.x); x[2] = bf_lo(hw.y); x[3] = bf_hi(hw.y);
+      x[4] = bf_lo(hw.z); x[5] = bf_hi(hw.z); x[6] = bf_lo(hw.w); x[7] = bf_hi(hw.w);
+    } else {
+      const float4* hp = reinterpret_cast<const float4*>(static_cast<const float*>(a.h) +
+                                                         m * a.ldh) + 2 * c;
+      const float4 u0 = __ldg(hp), u1 = __ldg(hp + 1);
+      x[0] = u0.x; x[1] = u0.y; x[2] = u0.z; x[3] = u0.w;
+      x[4] = u1.x; x[5] = u1.y; x[6] = u1.z; x[7] = u1.w;
+    }
+#pragma unroll
+    for (int t = 0; t < RMAX; ++t)
+      if (t < r) acc[t] += dot8(row_s[v_word0 + t * a_words + c], x);
+  }
+#pragma unroll
+  for (int t = 0; t < RMAX; ++t) {
+    if (t < r) {
+#pragma unroll
+      for (int o = 16; o; o >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
+      acc[t] *= al;  // every lane holds alpha hV[t]
+    }
+  }
+  float* out = a.part + static_cast<int64_t>(pid) * a.d_B;
+#pragma unroll 4
+  for (int i = lane; i < a.d_B; i += 32) {
+    float u = 0.f;
+    if constexpr (VEC_U) {
+      const int uw = r >> 3;
+#pragma unroll
+      for (int c8 = 0; c8 < RMAX / 8; ++c8) {
+        if (c8 < uw) {
+          float hv8[8];
+#pragma unroll
+          for (int t = 0; t < 8; ++t) hv8[t] = acc[c8 * 8 + t];
+          u += dot8(row_s[i * uw + c8], hv8);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int t = 0; t < RMAX; ++t)
+        if (t < r) u = fmaf(__bfloat162float(row_bf[i * r + t]), acc[t], u);
+    }
+    out[i] = u + al * __bfloat162float(row_bf[b_elem0 + i]);
+  }
+}
+
 // CTA = 32 consecutive pairs of the row-sorted list.  Each run of pairs with
 // the same row is one segment: the CTA stages that row's U | V | b in shared
 // memory (read once from HBM), then warp w takes the segment's pairs w, w + 8,
@@ -117,7 +182,6 @@ __global__ void __launch_bounds__(kRowThreads) lowrank_rows_kernel(const RowsArg
   const int r = a.r;
   const int a_words = a.d_A >> 3;
   const int v_word0 = (a.d_B * r) >> 3;  // V follows U (d_B x r); both whole words
-  const __nv_bfloat16* row_bf = reinterpret_cast<const __nv_bfloat16*>(row_s);
   const int b_elem0 = a.d_B * r + r * a.d_A;
   for (int sgi = 0; sgi < n_seg; ++sgi) {
     const int q0 = seg_start[sgi], q1 = seg_start[sgi + 1];
@@ -125,64 +189,8 @@ __global__ void __launch_bounds__(kRowThreads) lowrank_rows_kernel(const RowsArg
         reinterpret_cast<const uint4*>(a.vectors + static_cast<int64_t>(seg_row[q0]) * a.ldv);
     for (int w = threadIdx.x; w < a.row_words; w += kRowThreads) row_s[w] = __ldg(src + w);
     __syncthreads();
-    for (int q = q0 + warp; q < q1; q += kRowWarps) {
-      const int32_t pid = seg_pair[q];
-      const int64_t m = pid / a.k;
-      const float al = a.alpha[pid];
-      float acc[RMAX];
-#pragma unroll
-      for (int t = 0; t < RMAX; ++t) acc[t] = 0.f;
-#pragma unroll 4
-      for (int c = lane; c < a_words; c += 32) {  // unrolled: the h loads (L2) go out together
-        float x[8];
-        if constexpr (HBF16) {
-          const uint4 hw =
-              __ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.h) +
-                                                   m * a.ldh) + c);
-          x[0] = bf_lo(hw.x); x[1] = bf_hi(hw.x); x[2] = bf_lo(hw.y); x[3] = bf_hi(hw.y);
-          x[4] = bf_lo(hw.z); x[5] = bf_hi(hw.z); x[6] = bf_lo(hw.w); x[7] = bf_hi(hw.w);
-        } else {
-          const float4* hp = reinterpret_cast<const float4*>(static_cast<const float*>(a.h) +
-                                                             m * a.ldh) + 2 * c;
-          const float4 u0 = __ldg(hp), u1 = __ldg(hp + 1);
-          x[0] = u0.x; x[1] = u0.y; x[2] = u0.z; x[3] = u0.w;
-          x[4] = u1.x; x[5] = u1.y; x[6] = u1.z; x[7] = u1.w;
-        }
-#pragma unroll
-        for (int t = 0; t < RMAX; ++t)
-          if (t < r) acc[t] += dot8(row_s[v_word0 + t * a_words + c], x);
-      }
-#pragma unroll
-      for (int t = 0; t < RMAX; ++t) {
-        if (t < r) {
-#pragma unroll
-          for (int o = 16; o; o >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
-          acc[t] *= al;  // every lane holds alpha hV[t]
-        }
-      }
-      float* out = a.part + static_cast<int64_t>(pid) * a.d_B;
-#pragma unroll 4
-      for (int i = lane; i < a.d_B; i += 32) {
-        float u = 0.f;
-        if constexpr (VEC_U) {
-          const int uw = r >> 3;
-#pragma unroll
-          for (int c8 = 0; c8 < RMAX / 8; ++c8) {
-            if (c8 < uw) {
-              float hv8[8];
-#pragma unroll
-              for (int t = 0; t < 8; ++t) hv8[t] = acc[c8 * 8 + t];
-              u += dot8(row_s[i * uw + c8], hv8);
-            }
-          }
-        } else {
-#pragma unroll
-          for (int t = 0; t < RMAX; ++t)
-            if (t < r) u = fmaf(__bfloat162float(row_bf[i * r + t]), acc[t], u);
-        }
-        out[i] = u + al * __bfloat162float(row_bf[b_elem0 + i]);
-      }
-    }
+    for (int q = q0 + warp; q < q1; q += kRowWarps)
+      apply_pair<RMAX, HBF16, VEC_U>(a, row_s, seg_pair[q], lane, v_word0, a_words, b_elem0);
     __syncthreads();  // the next segment overwrites the staged row
   }
 }
