@@ -502,3 +502,27 @@ def test_exact_ties_two_level_list(lib, k):
         assert torch.equal(i[r0:r0 + 512], ref), r0
         want_v = torch.exp(torch.gather(s, 1, ref.long()).double() / T).float()
         torch.testing.assert_close(v[r0:r0 + 512], want_v, rtol=1e-6, atol=0)
+
+
+@pytest.mark.parametrize("N,d,k", [(64, 64, 8), (300, 128, 16), (5000, 64, 32)])
+def test_identity_keys_one_hot_queries_known_answer(lib, N, d, k):
+    """Known answer: key n = c_n e_n for n < d (c_n = 1 + n / 64, exact in bf16),
+    zero rows beyond; query m = e_{m mod d}.  Query e_j scores c_j on key j and
+    exactly 0 on every other key, so its top-k is j followed by the zero-score
+    keys in ascending index order (lower index first among ties); the values
+    are the fused scores exp(s / T) of those raw scores."""
+    M = 2 * d + 3
+    keys = np.zeros((N, d), np.float32)
+    c = 1.0 + np.arange(d, dtype=np.float32) / 64.0
+    keys[np.arange(d), np.arange(d)] = c
+    q = np.zeros((M, d), np.float32)
+    q[np.arange(M), np.arange(M) % d] = 1.0
+    T = 0.5
+    v, i = lib.tiled_topk_fused(from_f32(q), from_f32(keys), k, 1.0, 0.0, T, False)
+    v, i = v.cpu().numpy(), i.cpu().numpy()
+    for m in range(M):
+        j = m % d
+        want = [j] + [n for n in range(k) if n != j][:k - 1]
+        assert list(i[m]) == want, (m, list(i[m]), want)
+        assert np.isclose(v[m, 0], np.exp(c[j] / T), rtol=1e-6)
+        assert np.allclose(v[m, 1:], 1.0)
