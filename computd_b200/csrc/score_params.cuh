@@ -39,6 +39,20 @@ __device__ __forceinline__ bool score_params_ok(const ScoreParams& p, int use_si
   return true;
 }
 
+// 2^x and 1/x as single special-function-unit instructions (PTX ex2.approx and
+// rcp.approx, subnormals flushed to zero).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float kLog2e = 1.4426950408889634f;  // log2(e): e^x = 2^(x log2 e)
+
 __device__ __forceinline__ void record_status(int* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
 }

@@ -569,34 +569,56 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
     };
     // AUX: the fused score of every (row, key) of the chunk, summed over the
     // rows of the row's group (sequence) and added into aux.  Runs after the
-    // chunk's scan and overwrites the chunk's registers.
+    // chunk's scan and overwrites the chunk's registers with v(s).
+    //   v(s) = 2^(s c_exp)                                   (exp(s / T))
+    //        * 1 / (1 + 2^(s c_g1 + c_g0))                   (the gate, when on)
+    // with c_exp = log2(e) / T, c_g1 = -lambda log2(e), c_g0 = lambda tau log2(e):
+    // per score one FMA-pipe and one special-function instruction without the
+    // gate, four and three with it; the 1 / group_rows scale goes on the column
+    // sums, and the TMEM loads overlap the work as in the plain scan.  (The
+    // reciprocal as Newton steps on the FMA pipe instead measured slower: the
+    // epilogue is issue-bound, not bound by the special-function unit.)
     const int64_t grow = static_cast<int64_t>(row0) + row;
     const int64_t my_group = AUX && grow < a.M ? grow / a.group_rows : -1;
     ScoreParams sp{a.lambda_sharp, a.tau, a.T};
     if constexpr (AUX) sp = load_score_params(a.params, a.lambda_sharp, a.tau, a.T);
-    const float inv_T = 1.0f / sp.T;
+    const float c_exp = kLog2e / sp.T;
+    const float c_g1 = -sp.lambda_sharp * kLog2e;
+    const float c_g0 = sp.lambda_sharp * sp.tau * kLog2e;
     const float aux_scale = AUX ? 1.0f / static_cast<float>(a.group_rows) : 0.0f;
     const int64_t g0 = __shfl_sync(0xffffffffu, my_group, 0);
     // rows increase with the lane: lane 0 invalid means the whole warp is padding
     const bool aux_uniform = __all_sync(0xffffffffu, my_group == g0 || my_group < 0);
-    auto aux_chunk = [&](const uint32_t (&r)[32], int rem, int32_t col0) {
+    const bool aux_all_rows = __all_sync(0xffffffffu, my_group >= 0);
+    auto aux_chunk = [&](uint32_t (&r)[32], int rem, int32_t col0) {
+      if (g0 < 0) return;
+      if (a.use_sigmoid) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float sc = __uint_as_float(r[j]);
+          const float gate = rcp_approx(1.0f + ex2_approx(fmaf(sc, c_g1, c_g0)));
+          r[j] = __float_as_uint(ex2_approx(sc * c_exp) * gate);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(ex2_approx(__uint_as_float(r[j]) * c_exp));
+      }
+      if (rem < 32 || !aux_all_rows) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (my_group < 0 || j >= rem) r[j] = 0u;
+      }
       float f[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float sc = __uint_as_float(r[j]);
-        float v = __expf(sc * inv_T);
-        if (a.use_sigmoid) v = __fdividef(v, 1.0f + __expf(-sp.lambda_sharp * (sc - sp.tau)));
-        f[j] = (my_group >= 0 && j < rem) ? v * aux_scale : 0.0f;
-      }
-      if (g0 < 0) return;
+      for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
       if (aux_uniform) {
         const float colsum = warp_column_sum32(f, lane);
-        if (lane < rem) atomicAdd(a.aux + g0 * a.ld_aux + col0 + lane, colsum);
+        if (lane < rem) atomicAdd(a.aux + g0 * a.ld_aux + col0 + lane, colsum * aux_scale);
       } else if (my_group >= 0) {
         // rows of two groups in this warp: every lane adds its own values
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-          if (j < rem) atomicAdd(a.aux + my_group * a.ld_aux + col0 + j, f[j]);
+          if (j < rem) atomicAdd(a.aux + my_group * a.ld_aux + col0 + j, f[j] * aux_scale);
       }
     };
     const uint32_t lead_tempty0 = map_to_cta(tempty_bar(0), 0);
@@ -626,19 +648,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
       const int ce = min(valid, cb + kColsPerWg);
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + static_cast<uint32_t>(acc * kTileN);
-      if constexpr (AUX) {
-        // One chunk of 32 columns at a time: the aux sums need the registers
-        // the overlapped load of the next chunk would hold.
+      // Chunks of 32 columns.  Two register sets in flight (the TMEM load of
+      // the next chunk overlaps the scan and aux sums of the current one)
+      // wherever the list leaves the registers for them.
+      constexpr bool kOverlap = !AUX || KCAP == 16 || KCAP == kCapHeap128 || NWG == 1 && KCAP <= 32;
+      if (!kOverlap) {
         for (int c = cb; c < ce; c += 32) {
           uint32_t r[32];
           tmem_ld_32x32b_x32_async(taddr + c, r);
           tmem_wait_ld_pin(r);
           scan_chunk(r, ce - c, static_cast<int32_t>(n0 + c));
-          aux_chunk(r, ce - c, static_cast<int32_t>(n0 + c));
+          if constexpr (AUX) aux_chunk(r, ce - c, static_cast<int32_t>(n0 + c));
         }
       } else if (cb < ce) {
-        // Chunks of 32 columns, two register sets in flight: the TMEM load of
-        // the next chunk overlaps the scan of the current one.
         uint32_t ra[32], rb[32];
         tmem_ld_32x32b_x32_async(taddr + cb, ra);
         tmem_wait_ld_pin(ra);
@@ -646,11 +668,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(NWG), 1)
           const bool has_b = c + 32 < ce;   // warp-uniform
           if (has_b) tmem_ld_32x32b_x32_async(taddr + c + 32, rb);
           scan_chunk(ra, ce - c, static_cast<int32_t>(n0 + c));
+          if constexpr (AUX) aux_chunk(ra, ce - c, static_cast<int32_t>(n0 + c));
           if (has_b) {
             tmem_wait_ld_pin(rb);
             const bool has_next = c + 64 < ce;
             if (has_next) tmem_ld_32x32b_x32_async(taddr + c + 64, ra);
             scan_chunk(rb, ce - c - 32, static_cast<int32_t>(n0 + c + 32));
+            if constexpr (AUX) aux_chunk(rb, ce - c - 32, static_cast<int32_t>(n0 + c + 32));
             if (has_next) tmem_wait_ld_pin(ra);
           }
         }
