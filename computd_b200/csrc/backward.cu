@@ -25,6 +25,7 @@
 
 #include "dwa_internal.h"
 #include "score_params.cuh"
+#include "sm100_ptx.cuh"
 
 namespace dwa {
 
@@ -217,6 +218,9 @@ __global__ void __launch_bounds__(kWarps * 32)
 // lambda / tau / T terms exactly as score_backward_kernel; (3) all threads:
 // dq = sum_j ds_j K_j over column slices, re-reading the K rows this CTA just
 // read (from L2).  Replaces gather_dot x 2 + score_backward + gather_rows.
+// The kernel is bound by how many row bytes are in flight: four CTAs per SM
+// (64 registers a thread) with eight 16-byte loads per lane keep ~128 KB per
+// SM outstanding.
 constexpr int kBwdMaxK = 128;
 
 struct FusedBwdArgs {
@@ -245,7 +249,7 @@ struct FusedBwdArgs {
   int* status;
 };
 
-__global__ void __launch_bounds__(kWarps * 32, 1) retrieval_backward_kernel(const FusedBwdArgs a) {
+__global__ void __launch_bounds__(kWarps * 32, 4) retrieval_backward_kernel(const FusedBwdArgs a) {
   __shared__ int32_t g_s[kBwdMaxK];
   __shared__ float s_s[kBwdMaxK], da_s[kBwdMaxK], ds_s[kBwdMaxK];
   __shared__ int ok_s;
@@ -254,28 +258,46 @@ __global__ void __launch_bounds__(kWarps * 32, 1) retrieval_backward_kernel(cons
   const int k = a.k;
   for (int j = tid; j < k; j += kWarps * 32) g_s[j] = a.idx[m * k + j];
   __syncthreads();
-  // (1) s_j and dalpha_j, entries j = w, w + 8, ...
+  // (1) s_j and dalpha_j, entries j = w, w + 8, ...  The K rows are read
+  // again by (3), so they are loaded with the L2 evict-last policy; the V rows
+  // are read once (evict-first).  Each pass of the column loop puts a row's
+  // next 1024 columns of K and of V in flight together (8 loads per lane).
+  const uint64_t pol_keep = l2_policy_evict_last();
+  const uint64_t pol_once = l2_policy_evict_first();
+  const int d_max = a.d_k > a.d_v ? a.d_k : a.d_v;
   for (int j = w; j < k; j += kWarps) {
     const int32_t g = g_s[j];
     float sj = 0.f, dj = 0.f;
     if (g >= a.row_begin && g < a.row_end) {  // warp-uniform
       const uint16_t* kr = a.keys + static_cast<int64_t>(g - a.row_begin) * a.ldk;
       const uint16_t* vr = a.values + static_cast<int64_t>(g - a.row_begin) * a.ldv;
-#pragma unroll 4
-      for (int c = lane * 8; c < a.d_k; c += 256) {  // unrolled: the row's loads go out together
-        float fa[8], fr[8];
-        load_a8(a.q, a.q_bf16, m * a.ldq + c, fa);
-        bf16x8(__ldg(reinterpret_cast<const uint4*>(kr + c)), fr);
+      for (int c0 = lane * 8; c0 < d_max; c0 += 1024) {
+        uint4 kx[4], vx[4];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) sj = fmaf(fa[e], fr[e], sj);
-      }
-#pragma unroll 4
-      for (int c = lane * 8; c < a.d_v; c += 256) {
-        float fa[8], fr[8];
-        load_a8(a.dout, 0, m * a.ld_dout + c, fa);
-        bf16x8(__ldg(reinterpret_cast<const uint4*>(vr + c)), fr);
+        for (int u = 0; u < 4; ++u) {
+          const int c = c0 + 256 * u;
+          kx[u] = c < a.d_k ? ld_nc_l2hint_v4(kr + c, pol_keep) : make_uint4(0u, 0u, 0u, 0u);
+          vx[u] = c < a.d_v ? ld_nc_l2hint_v4(vr + c, pol_once) : make_uint4(0u, 0u, 0u, 0u);
+        }
+        // per lane, columns in increasing order (the order of gather_dot_kernel)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) dj = fmaf(fa[e], fr[e], dj);
+        for (int u = 0; u < 4; ++u) {
+          const int c = c0 + 256 * u;
+          if (c < a.d_k) {
+            float fa[8], fr[8];
+            load_a8(a.q, a.q_bf16, m * a.ldq + c, fa);
+            bf16x8(kx[u], fr);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) sj = fmaf(fa[e], fr[e], sj);
+          }
+          if (c < a.d_v) {
+            float fa[8], fr[8];
+            load_a8(a.dout, 0, m * a.ld_dout + c, fa);
+            bf16x8(vx[u], fr);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) dj = fmaf(fa[e], fr[e], dj);
+          }
+        }
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
@@ -349,7 +371,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1) retrieval_backward_kernel(cons
   }
   __syncthreads();
   // (3) dq[m, c..c+3] = sum_j ds_j K_j[c..c+3]: 4 columns per thread per step,
-  // the k rows in blocks of 8 so eight loads are in flight
+  // the k rows in blocks of 8 so eight loads are in flight; the K rows' last
+  // read (evict-first)
   const bool ok = ok_s != 0;
   for (int c = tid * 4; c < a.d_k; c += kWarps * 32 * 4) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -360,8 +383,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1) retrieval_backward_kernel(cons
         const int j = j0 + u;
         const int32_t g = j < k ? g_s[j] : -1;
         raw[u] = (g >= a.row_begin && g < a.row_end)
-                     ? __ldg(reinterpret_cast<const uint2*>(
-                           a.keys + static_cast<int64_t>(g - a.row_begin) * a.ldk + c))
+                     ? ld_nc_l2hint_v2(a.keys + static_cast<int64_t>(g - a.row_begin) * a.ldk + c,
+                                       pol_once)
                      : make_uint2(0u, 0u);
       }
 #pragma unroll

@@ -112,7 +112,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t smem_dst, const CUtensorMap
       : "memory");
 }
 
-// L2 eviction-priority policies for the cache_hint operand.
 // Untiled bulk copy global -> this CTA's shared memory (no multicast), bytes
 // counted on `bar`.  Both addresses 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_load(uint32_t smem_dst, const void* src, uint32_t bytes,
@@ -123,6 +122,7 @@ __device__ __forceinline__ void bulk_load(uint32_t smem_dst, const void* src, ui
       : "memory");
 }
 
+// L2 eviction-priority policies for the cache_hint operand.
 __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
@@ -132,6 +132,27 @@ __device__ __forceinline__ uint64_t l2_policy_evict_normal() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
   return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// Read-only global loads (not allocated in L1) carrying an L2 eviction policy.
+__device__ __forceinline__ uint4 ld_nc_l2hint_v4(const void* p, uint64_t pol) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p), "l"(pol));
+  return v;
+}
+__device__ __forceinline__ uint2 ld_nc_l2hint_v2(const void* p, uint64_t pol) {
+  uint2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v2.u32 {%0, %1}, [%2], %3;"
+               : "=r"(v.x), "=r"(v.y)
+               : "l"(p), "l"(pol));
+  return v;
 }
 
 // ---------------------------------------------------------------- tcgen05

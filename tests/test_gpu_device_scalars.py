@@ -126,7 +126,9 @@ def test_score_backward_dev_matches_host_scalars(cb):
 @pytest.mark.parametrize("B,N,d,sig", [(1, 1000, 64, True), (3, 5000, 128, False),
                                        (4, 70000, 384, True), (5, 3001, 1024, True),
                                        (9, 20000, 4096, False), (16, 777, 136, True),
-                                       (2, 4099, 12800, True)])
+                                       (2, 4099, 12800, True), (8, 3000, 4096, True),
+                                       (4, 5000, 4096, True), (7, 1500, 1000, True),
+                                       (1, 999, 12800, False), (8, 600, 12800, True)])
 def test_seq_scores_vs_fp64(cb, B, N, d, sig):
     """sims = q . keys^T and v(sims) for the per-sequence mean queries
     (retrieval.py:332-341), every entry, against fp64."""
