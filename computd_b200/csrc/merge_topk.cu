@@ -12,11 +12,11 @@
 //    among ties equals ordering by (v desc, global index asc), because shard p's
 //    global indices all precede shard p+1's and each list is already sorted.
 //
-// One warp per query row.  Lane l holds the heads of lists l, l+32, l+64,
-// l+96 (up to kMaxSplits lists), each with the next few entries cached in
-// registers; every output step is a warp arg-max over the lane heads followed
-// by an advance of the winning list.  Lists must be sorted best first
-// (score descending, lower index first among equal scores).
+// One warp per query row, the row's lists staged in shared memory; lane l
+// holds the heads of lists l, l+32, l+64, l+96 (up to kMaxSplits lists);
+// every output step is a warp arg-max over the lane heads followed by an
+// advance of the winning list.  Lists must be sorted best first (score
+// descending, lower index first among equal scores).
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -30,9 +30,8 @@ namespace dwa {
 
 namespace {
 
-constexpr int kWarps = 8;           // rows per block
-constexpr int kSlots = kMaxSplits / 32;  // lists per lane
-constexpr int kCache = 4;           // entries cached per list
+constexpr int kWarps = 8;           // most rows per block
+constexpr int kMaxStagedEntries = 2048;  // n_lists x k_in staged per row (16 KB)
 
 constexpr int kMaxPeers = 16;       // peer lists of the NVLink exchange
 
@@ -64,6 +63,206 @@ __device__ __forceinline__ float fused_score(float s, int use_sigmoid, float lam
   return g * e;
 }
 
+__device__ __forceinline__ int32_t ld_acquire_sys(const int32_t* p) {
+  int32_t v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Keys whose unsigned order is the merge order: a float-order image of the
+// score (-0.0 tied with +0.0, as in the float comparison) and the reversed
+// index (lower index first among equal scores).
+__device__ __forceinline__ uint32_t score_key(float s) {
+  uint32_t su = __float_as_uint(s);
+  if (su == 0x80000000u) su = 0u;
+  return (su & 0x80000000u) ? ~su : (su | 0x80000000u);
+}
+__device__ __forceinline__ uint32_t index_key(int32_t i) {
+  return 0x7FFFFFFFu - static_cast<uint32_t>(i);  // i >= 0 or the sentinel
+}
+
+// One warp per query row.  The row's lists are first staged in this warp's
+// shared memory (entry p of list l as a (score bits, index) pair at l k_in +
+// p), so no global-memory latency sits on the merge's critical path.  Lane l
+// owns lists l, l + 32, ... (KSLOTS of them) and keeps their heads and its
+// best head in registers.  Each output step is a warp arg-best over the lane
+// bests (two hardware max-reductions and a ballot); only the winning lane
+// then advances its list and recomputes its best, so a step costs a few
+// warp-wide instructions whatever the number of lists.
+template <bool kPeer, int KSLOTS>
+__global__ void __launch_bounds__(kWarps * 32) merge_sorted_kernel(const MergeArgs a) {
+  __shared__ float st_s[kWarps][DWA_MERGE_MAX_K];
+  __shared__ int32_t st_i[kWarps][DWA_MERGE_MAX_K];
+  extern __shared__ uint4 stage_raw[];
+  const int w = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * wpb + w;
+  if (row >= a.M) return;  // warp-uniform; only warp-level synchronisation below
+  ScoreParams sp{a.lambda_sharp, a.tau, a.T};
+  if (a.transform) {
+    sp = load_score_params(a.params, a.lambda_sharp, a.tau, a.T);
+    if (!score_params_ok(sp, a.use_sigmoid)) {
+      // device-held scalars the selection cannot honour: no top-k is defined
+      if (lane == 0) record_status(a.status, kStatusDeviceCheck);
+      for (int j = lane; j < a.k; j += 32) {
+        a.out_v[row * a.k + j] = NAN;
+        a.out_i[row * a.k + j] = -1;
+      }
+      return;
+    }
+  }
+  const int n_lists = a.n_lists, k_in = a.k_in;
+  int2* stage = reinterpret_cast<int2*>(stage_raw) + static_cast<size_t>(w) * n_lists * k_in;
+  if constexpr (kPeer) {
+    // Wait (bounded) until every peer has published this step's lists.
+    bool ready = true;
+    if (lane < n_lists) {
+      const uint64_t t0 = globaltimer_ns();
+      while (ld_acquire_sys(a.flags + lane) < a.wait_step) {
+        if (globaltimer_ns() - t0 > a.wait_ns) {
+          ready = false;
+          break;
+        }
+      }
+    }
+    if (!__all_sync(0xffffffffu, ready)) {
+      if (lane == 0) atomicCAS(a.status, 0, kStatusTimeout);
+      for (int j = lane; j < a.k; j += 32) {
+        a.out_v[row * a.k + j] = -INFINITY;
+        a.out_i[row * a.k + j] = -1;
+      }
+      return;
+    }
+    // This row's P lists (k (score, index) pairs each, 8k bytes contiguous
+    // per list) with 16-byte loads all in flight together, so NVLink latency
+    // is paid once per row.  Plain (coherent) loads after the acquire.
+    const int words = k_in >> 1;  // 16-byte words per list row (k even)
+    uint4* dst = reinterpret_cast<uint4*>(stage);
+    for (int t = lane; t < n_lists * words; t += 32) {
+      const int l = t / words, c = t - l * words;
+      dst[t] = *reinterpret_cast<const uint4*>(a.peer[l] + row * a.stride_row + 4 * c);
+    }
+  } else {
+    // four entries per lane in flight per round
+    const int total = n_lists * k_in;
+    for (int t0 = 0; t0 < total; t0 += 128) {
+      float sv[4];
+      int32_t iv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int t = t0 + 32 * u + lane;
+        if (t < total) {
+          const int l = t / k_in, p = t - l * k_in;
+          const int64_t off = l * a.stride_list + row * a.stride_row + p * a.stride_pos;
+          sv[u] = __ldg(a.cv + off);
+          iv[u] = __ldg(a.ci + off);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int t = t0 + 32 * u + lane;
+        if (t < total) stage[t] = make_int2(__float_as_int(sv[u]), iv[u]);
+      }
+    }
+  }
+  __syncwarp();
+
+  int pos[KSLOTS] = {};
+  float hs[KSLOTS];
+  int32_t hi[KSLOTS];
+  auto load_head = [&](int u) {
+    const int l = lane + 32 * u;
+    if (l < n_lists && pos[u] < k_in) {
+      const int2 e = stage[l * k_in + pos[u]];
+      hs[u] = __int_as_float(e.x);
+      hi[u] = e.y;
+    } else {
+      hs[u] = -INFINITY;
+      hi[u] = kSentinelIdx;
+    }
+  };
+  float bs;
+  int32_t bi;
+  int bu;
+  uint32_t skey, ikey;
+  auto pick_best = [&]() {
+    bs = hs[0];
+    bi = hi[0];
+    bu = 0;
+#pragma unroll
+    for (int u = 1; u < KSLOTS; ++u)
+      if (topk_worse(bs, bi, hs[u], hi[u])) {
+        bs = hs[u];
+        bi = hi[u];
+        bu = u;
+      }
+    skey = score_key(bs);
+    ikey = index_key(bi);
+  };
+#pragma unroll
+  for (int u = 0; u < KSLOTS; ++u) {
+    pos[u] = 0;
+    load_head(u);
+  }
+  pick_best();
+
+  for (int j = 0; j < a.k; ++j) {
+    const uint32_t smax = __reduce_max_sync(0xffffffffu, skey);
+    const uint32_t imax = __reduce_max_sync(0xffffffffu, skey == smax ? ikey : 0u);
+    const uint32_t win = __ballot_sync(0xffffffffu, skey == smax && ikey == imax);
+    if (lane == __ffs(win) - 1) {
+      st_s[w][j] = bs;
+      st_i[w][j] = bi;
+#pragma unroll
+      for (int u = 0; u < KSLOTS; ++u)
+        if (u == bu) {
+          ++pos[u];
+          load_head(u);
+        }
+      pick_best();
+    }
+  }
+  __syncwarp();
+
+  if (a.transform) {
+    for (int j = lane; j < a.k; j += 32)
+      st_s[w][j] = fused_score(st_s[w][j], a.use_sigmoid, sp.lambda_sharp, sp.tau, sp.T);
+    __syncwarp();
+    // v is non-decreasing in s, so the list is ordered by v already; entries
+    // whose v became equal must still be ordered by lower index first.
+    if (lane == 0) {
+      for (int p = 1; p < a.k; ++p) {
+        const float vs = st_s[w][p];
+        const int32_t vi = st_i[w][p];
+        int q = p - 1;
+        while (q >= 0 && topk_worse(st_s[w][q], st_i[w][q], vs, vi)) {
+          st_s[w][q + 1] = st_s[w][q];
+          st_i[w][q + 1] = st_i[w][q];
+          --q;
+        }
+        st_s[w][q + 1] = vs;
+        st_i[w][q + 1] = vi;
+      }
+    }
+    __syncwarp();
+  }
+
+  float* ov = a.out_v + row * a.k;
+  int32_t* oi = a.out_i + row * a.k;
+  for (int j = lane; j < a.k; j += 32) {
+    const int32_t ix = st_i[w][j];
+    ov[j] = st_s[w][j];
+    oi[j] = ix == kSentinelIdx ? -1 : static_cast<int32_t>(ix + a.idx_offset);
+  }
+}
+
+// Lists too long to stage (n_lists k_in > kMaxStagedEntries): each lane keeps
+// a cursor with the next kCache entries of each of its lists in registers
+// and reloads them from global memory as the list advances.
+constexpr int kSlots = kMaxSplits / 32;  // lists per lane
+constexpr int kCache = 4;                // entries cached per list
+
 template <typename V>
 __device__ __forceinline__ V pick4(const V (&c)[kCache], int j) {
   const V lo = (j & 1) ? c[1] : c[0];
@@ -78,34 +277,18 @@ struct ListCursor {
   int off;   // current head = entry `off` of the cache
 };
 
-// kPeer: the lists live in other GPUs' memory and were written by their
-// kernels; plain (coherent) loads after the acquire on the flags, not the
-// read-only path.
-template <bool kPeer>
 __device__ __forceinline__ void load_block(ListCursor& L, const float* vp, const int32_t* ip,
                                            int64_t stride_pos, int k_in) {
 #pragma unroll
   for (int e = 0; e < kCache; ++e) {
     const int p = L.base + e;
     const bool in = p < k_in;
-    if constexpr (kPeer) {
-      L.s[e] = in ? vp[p * stride_pos] : -INFINITY;
-      L.i[e] = in ? ip[p * stride_pos] : kSentinelIdx;
-    } else {
-      L.s[e] = in ? __ldg(vp + p * stride_pos) : -INFINITY;
-      L.i[e] = in ? __ldg(ip + p * stride_pos) : kSentinelIdx;
-    }
+    L.s[e] = in ? __ldg(vp + p * stride_pos) : -INFINITY;
+    L.i[e] = in ? __ldg(ip + p * stride_pos) : kSentinelIdx;
   }
 }
 
-__device__ __forceinline__ int32_t ld_acquire_sys(const int32_t* p) {
-  int32_t v;
-  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-template <bool kPeer>
-__global__ void __launch_bounds__(kWarps * 32) merge_sorted_kernel(const MergeArgs a) {
+__global__ void __launch_bounds__(kWarps * 32) merge_cursor_kernel(const MergeArgs a) {
   __shared__ float st_s[kWarps][DWA_MERGE_MAX_K];
   __shared__ int32_t st_i[kWarps][DWA_MERGE_MAX_K];
   const int w = threadIdx.x >> 5;
@@ -125,44 +308,6 @@ __global__ void __launch_bounds__(kWarps * 32) merge_sorted_kernel(const MergeAr
       return;
     }
   }
-  if constexpr (kPeer) {
-    // Wait (bounded) until every peer has published this step's lists.
-    bool ready = true;
-    if (lane < a.n_lists) {
-      const uint64_t t0 = globaltimer_ns();
-      while (ld_acquire_sys(a.flags + lane) < a.wait_step) {
-        if (globaltimer_ns() - t0 > a.wait_ns) {
-          ready = false;
-          break;
-        }
-      }
-    }
-    if (!__all_sync(0xffffffffu, ready)) {
-      if (lane == 0) atomicCAS(a.status, 0, kStatusTimeout);
-      for (int j = lane; j < a.k; j += 32) {
-        a.out_v[row * a.k + j] = -INFINITY;
-        a.out_i[row * a.k + j] = -1;
-      }
-      return;
-    }
-  }
-  // Peer mode: pull this row's P lists (k (score, index) pairs each, 8k bytes
-  // contiguous per list) into this warp's shared memory with 16-byte loads
-  // all in flight together, so NVLink latency is paid once per row instead of
-  // once per cached block of every list.
-  extern __shared__ uint4 peer_stage[];
-  const int32_t* stage = nullptr;
-  if constexpr (kPeer) {
-    const int words = a.k >> 1;  // 16-byte words per list row (k even)
-    uint4* dst = peer_stage + static_cast<size_t>(w) * a.n_lists * words;
-    for (int t = lane; t < a.n_lists * words; t += 32) {
-      const int l = t / words, c = t - l * words;
-      dst[t] = *reinterpret_cast<const uint4*>(a.peer[l] + row * a.stride_row + 4 * c);
-    }
-    __syncwarp();
-    stage = reinterpret_cast<const int32_t*>(dst);
-  }
-
   ListCursor cur[kSlots];
   const float* vbase[kSlots];
   const int32_t* ibase[kSlots];
@@ -172,14 +317,9 @@ __global__ void __launch_bounds__(kWarps * 32) merge_sorted_kernel(const MergeAr
     cur[u].base = 0;
     cur[u].off = 0;
     if (l < a.n_lists) {
-      if constexpr (kPeer) {
-        ibase[u] = stage + static_cast<int64_t>(l) * 2 * a.k + 1;
-        vbase[u] = reinterpret_cast<const float*>(stage + static_cast<int64_t>(l) * 2 * a.k);
-      } else {
-        vbase[u] = a.cv + l * a.stride_list + row * a.stride_row;
-        ibase[u] = a.ci + l * a.stride_list + row * a.stride_row;
-      }
-      load_block<kPeer>(cur[u], vbase[u], ibase[u], a.stride_pos, a.k_in);
+      vbase[u] = a.cv + l * a.stride_list + row * a.stride_row;
+      ibase[u] = a.ci + l * a.stride_list + row * a.stride_row;
+      load_block(cur[u], vbase[u], ibase[u], a.stride_pos, a.k_in);
     } else {
       vbase[u] = nullptr;
       ibase[u] = nullptr;
@@ -231,7 +371,7 @@ __global__ void __launch_bounds__(kWarps * 32) merge_sorted_kernel(const MergeAr
             cur[u].off = 0;
             cur[u].base += kCache;
             if (vbase[u] != nullptr) {
-              load_block<kPeer>(cur[u], vbase[u], ibase[u], a.stride_pos, a.k_in);
+              load_block(cur[u], vbase[u], ibase[u], a.stride_pos, a.k_in);
             }
           }
         }
@@ -272,6 +412,32 @@ __global__ void __launch_bounds__(kWarps * 32) merge_sorted_kernel(const MergeAr
   }
 }
 
+// Rows per block for the staged kernel: up to kWarps, within kStageBudget
+// bytes of staged lists per block, so that three blocks fit on an SM.
+constexpr int64_t kStageBudget = 64 * 1024;
+
+int merge_warps_per_block(int n_lists, int k_in) {
+  const int64_t per_warp = static_cast<int64_t>(n_lists) * k_in * 8;
+  const int64_t w = kStageBudget / per_warp;
+  return static_cast<int>(w < 1 ? 1 : w > kWarps ? kWarps : w);
+}
+
+template <bool kPeer, int KSLOTS>
+cudaError_t launch_merge_kernel(const MergeArgs& a, cudaStream_t stream) {
+  const int wpb = merge_warps_per_block(a.n_lists, a.k_in);
+  const size_t smem = static_cast<size_t>(wpb) * a.n_lists * a.k_in * 8;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(merge_sorted_kernel<kPeer, KSLOTS>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
+  const int64_t blocks = (a.M + wpb - 1) / wpb;
+  merge_sorted_kernel<kPeer, KSLOTS>
+      <<<static_cast<unsigned>(blocks), wpb * 32, smem, stream>>>(a);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_merge_topk(const float* cand_vals, const int32_t* cand_idx, int n_lists,
@@ -303,9 +469,14 @@ cudaError_t launch_merge_topk(const float* cand_vals, const int32_t* cand_idx, i
   a.status = status;
   a.out_v = out_vals;
   a.out_i = out_idx;
-  const int64_t blocks = (M + kWarps - 1) / kWarps;
-  merge_sorted_kernel<false><<<static_cast<unsigned>(blocks), kWarps * 32, 0, stream>>>(a);
-  return cudaGetLastError();
+  if (static_cast<int64_t>(n_lists) * k_in > kMaxStagedEntries) {
+    const int64_t blocks = (M + kWarps - 1) / kWarps;
+    merge_cursor_kernel<<<static_cast<unsigned>(blocks), kWarps * 32, 0, stream>>>(a);
+    return cudaGetLastError();
+  }
+  if (n_lists <= 32) return launch_merge_kernel<false, 1>(a, stream);
+  if (n_lists <= 64) return launch_merge_kernel<false, 2>(a, stream);
+  return launch_merge_kernel<false, 4>(a, stream);
 }
 
 namespace {
@@ -364,16 +535,8 @@ cudaError_t launch_merge_topk_peers(const int32_t* const* packed, int n, int64_t
   a.out_v = out_vals;
   a.out_i = out_idx;
   if (k % 2 != 0) return cudaErrorInvalidValue;  // 16-byte staging words
-  const int64_t blocks = (M + kWarps - 1) / kWarps;
-  const size_t smem = static_cast<size_t>(kWarps) * n * k * 8;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(merge_sorted_kernel<true>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-  }
-  merge_sorted_kernel<true><<<static_cast<unsigned>(blocks), kWarps * 32, smem, stream>>>(a);
-  return cudaGetLastError();
+  static_assert(kMaxPeers <= 32, "one list per lane");
+  return launch_merge_kernel<true, 1>(a, stream);
 }
 
 }  // namespace dwa

@@ -138,9 +138,13 @@ def test_strided_inputs_and_offset(lib):
     assert errs == [], errs
 
 
-def test_merge_matches_oracle(lib):
-    rng = np.random.default_rng(11)
-    P, M, k = 8, 333, 64
+@pytest.mark.parametrize("P,M,k", [(8, 333, 64), (40, 100, 32), (100, 50, 16), (40, 70, 64),
+                                   (128, 20, 128), (1, 17, 5)])
+def test_merge_matches_oracle(lib, P, M, k):
+    """The k-way merge on every path: lists staged in shared memory with one,
+    two or four lists per lane (n_lists x k <= 2048), and the register-cursor
+    kernel for longer list sets."""
+    rng = np.random.default_rng(11 + P)
     vals = -np.sort(-rng.standard_normal((P, M, k)).astype(np.float32), axis=2)
     vals[:, :, 10:14] = vals[:, :, 10:11]   # ties inside and across lists
     vals = -np.sort(-vals, axis=2)
