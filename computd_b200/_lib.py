@@ -1,4 +1,5 @@
-"""ctypes binding of ``libdwa_b200.so`` (the C ABI declared in include/dwa_retrieval.h).
+"""ctypes binding of ``libdwa_b200.so`` (the C ABI declared in include/dwa_retrieval.h and
+include/dwa_lm.h).
 
 The library is the only implementation of the retrieval path: there is no
 CPU or PyTorch fallback.  If the shared library is missing, importing this
@@ -22,7 +23,7 @@ DWA_ERR_DEVICE_CHECK = 5
 DWA_ERR_WORKSPACE = 6
 DWA_MAX_K = 128
 
-# Every symbol include/dwa_retrieval.h declares, with its ctypes signature.
+# Every symbol include/dwa_retrieval.h and include/dwa_lm.h declare, with its ctypes signature.
 _c_void_p = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int32
@@ -101,6 +102,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dwa_usage_ema": (_i32, [_c_void_p, _c_void_p, _i64, _i64, _i64, _f32, _f32, _c_void_p,
                              _c_void_p]),
     "dwa_workspace_status": (_i32, [_c_void_p, _c_void_p, ctypes.POINTER(_i32)]),
+    # include/dwa_lm.h: the LM block's fused elementwise steps
+    "dwa_lm_rope_qk": (_i32, [_c_void_p, _i64, _i64, _i32, _i32, _i64, _c_void_p, _c_void_p,
+                              _i64, _c_void_p, _c_void_p, _c_void_p]),
+    "dwa_lm_aspect_queries": (_i32, [_c_void_p, _i64, _i32, _i32, _i64, _c_void_p, _c_void_p,
+                                     _f32, _f32, _i32, _c_void_p, _i64, _c_void_p, _c_void_p,
+                                     _c_void_p]),
 }
 
 _lock = threading.Lock()

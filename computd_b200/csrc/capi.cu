@@ -14,6 +14,7 @@
 #include <string>
 
 #include "dwa_retrieval.h"
+#include "dwa_lm.h"
 #include "dwa_internal.h"
 
 namespace {
@@ -823,6 +824,61 @@ dwa_status dwa_workspace_status(const void* ws, dwa_stream_t stream, int32_t* ou
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) return cuda_fail(e, "dwa_workspace_status");
   *out_status = v;
+  return ok();
+}
+
+dwa_status dwa_lm_rope_qk(const void* qkv, int64_t B, int64_t S, int32_t H, int32_t dh,
+                          int64_t ld_qkv, const void* cos_t, const void* sin_t, int64_t ld_cs,
+                          void* q_out, void* k_out, dwa_stream_t stream) {
+  if (B < 0 || S < 0 || H < 1 || dh < 8)
+    return fail(DWA_ERR_INVALID_ARG, "dwa_lm_rope_qk: bad sizes (B=%lld, S=%lld, H=%d, dh=%d)",
+                (long long)B, (long long)S, H, dh);
+  if (B == 0 || S == 0) return ok();
+  if (!qkv || !cos_t || !sin_t || !q_out || !k_out)
+    return fail(DWA_ERR_INVALID_ARG, "dwa_lm_rope_qk: null pointer");
+  if (dh % 8 != 0) return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_lm_rope_qk: dh=%d must be a multiple of 8", dh);
+  if (ld_qkv < 2ll * H * dh || ld_cs < dh / 2)
+    return fail(DWA_ERR_INVALID_ARG, "dwa_lm_rope_qk: a row stride is below its row length");
+  if (ld_qkv % 8 != 0 || ld_cs % 4 != 0 || !aligned(qkv, 16) || !aligned(q_out, 16) ||
+      !aligned(k_out, 16) || !aligned(cos_t, 8) || !aligned(sin_t, 8))
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_lm_rope_qk: alignment (ld_qkv %% 8, ld_cs %% 4, "
+                "16-byte qkv / outputs, 8-byte cos / sin)");
+  if (2 * B * S * H * (dh / 8) > INT32_MAX * 256ll)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_lm_rope_qk: too many elements");
+  cudaError_t e = dwa::launch_rope_qk(qkv, B, S, H, dh, ld_qkv, cos_t, sin_t, ld_cs, q_out, k_out,
+                                      static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_lm_rope_qk launch");
+  return ok();
+}
+
+dwa_status dwa_lm_aspect_queries(const void* q, int64_t M, int32_t S, int32_t d_k, int64_t ldq,
+                                 const float* aspect_logits, const float* tau_param,
+                                 float lambda_sharp, float T, int32_t use_sigmoid, void* out,
+                                 int64_t ldo, float* w_out, float* params_out,
+                                 dwa_stream_t stream) {
+  if (M < 0) return fail(DWA_ERR_INVALID_ARG, "dwa_lm_aspect_queries: negative M");
+  if (S < 1 || S > dwa::lm_max_aspects())
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_lm_aspect_queries: S=%d outside [1, %d]", S,
+                dwa::lm_max_aspects());
+  if (d_k < 8 || d_k % 8 != 0)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_lm_aspect_queries: d_k=%d must be a positive "
+                "multiple of 8", d_k);
+  if (!aspect_logits || (use_sigmoid && !tau_param))
+    return fail(DWA_ERR_INVALID_ARG, "dwa_lm_aspect_queries: null aspect_logits / tau_param");
+  if (M > 0 && (!q || !out)) return fail(DWA_ERR_INVALID_ARG, "dwa_lm_aspect_queries: null q / out");
+  if (ldq < static_cast<int64_t>(S) * d_k || ldo < static_cast<int64_t>(S) * d_k)
+    return fail(DWA_ERR_INVALID_ARG, "dwa_lm_aspect_queries: a row stride is below S d_k");
+  if (ldq % 8 != 0 || ldo % 8 != 0 || (M > 0 && (!aligned(q, 16) || !aligned(out, 16))))
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_lm_aspect_queries: 16-byte aligned rows required");
+  if (!aligned(aspect_logits, 4) || (tau_param && !aligned(tau_param, 4)) ||
+      (w_out && !aligned(w_out, 4)) || (params_out && !aligned(params_out, 4)))
+    return fail(DWA_ERR_INVALID_ARG, "dwa_lm_aspect_queries: f32 arrays must be 4-byte aligned");
+  if (M * S > INT32_MAX * 256ll)
+    return fail(DWA_ERR_UNSUPPORTED_SHAPE, "dwa_lm_aspect_queries: too many rows");
+  cudaError_t e = dwa::launch_aspect_queries(q, M, S, d_k, ldq, aspect_logits, tau_param,
+                                             lambda_sharp, T, use_sigmoid ? 1 : 0, out, ldo, w_out,
+                                             params_out, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwa_lm_aspect_queries launch");
   return ok();
 }
 

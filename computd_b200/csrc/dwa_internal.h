@@ -97,6 +97,16 @@ cudaError_t launch_seq_scores(const float* q, int64_t B, int64_t ldq, const void
                               float* sims, int64_t lds, float* fused, int64_t ldf, int* status,
                               cudaStream_t stream);
 int seq_scores_max_d();  // largest d launch_seq_scores accepts
+
+// lm_ops.cu: the LM block's fused elementwise steps (dwa_lm.h)
+cudaError_t launch_rope_qk(const void* qkv, int64_t B, int64_t S, int H, int dh, int64_t ld_qkv,
+                           const void* cosv, const void* sinv, int64_t ld_cs, void* q_out,
+                           void* k_out, cudaStream_t stream);
+cudaError_t launch_aspect_queries(const void* q, int64_t M, int S, int d_k, int64_t ldq,
+                                  const float* logits, const float* tau_param, float lambda_sharp,
+                                  float T, int use_sigmoid, void* out, int64_t ldo, float* w_out,
+                                  float* params_out, cudaStream_t stream);
+int lm_max_aspects();
 cudaError_t launch_gather_rows(const float* wts, const int32_t* idx, int64_t M, int k,
                                const void* rows, int64_t row_begin, int64_t row_end, int64_t ldr,
                                int d, float* out, int accumulate, cudaStream_t stream);

@@ -51,8 +51,8 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .assembler import WeightAssembler
+from .lm_ops import aspect_queries, rope_qk
 from .retrieval import MultiAspectRetrieval, Retriever, project_keys_packed
-from .tiled_topk import score_params
 
 
 @dataclass(frozen=True)
@@ -105,7 +105,9 @@ CONFIGS = {"small_char": SMALL_CHAR, "large_1b": LARGE_1B, "large_7b": LARGE_7B,
 
 
 def _rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    # rotate (even, odd) pairs, concatenated like the reference (parts.py:17-25)
+    """RoPE as bf16 tensor ops: rotate (even, odd) pairs, concatenated like the
+    reference (parts.py:17-25).  The forward runs ``lm_ops.rope_qk`` instead, which
+    equals this bit for bit."""
     x1, x2 = x[..., ::2], x[..., 1::2]
     return torch.cat([x1 * cos - x2 * sin, x1 * sin + x2 * cos], dim=-1)
 
@@ -127,12 +129,10 @@ class CausalSelfAttention(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         B, S, C = x.shape
-        q, k, v = self.qkv(self.norm(x)).split(C, dim=-1)
-        q = q.view(B, S, self.h, self.dh).transpose(1, 2)
-        k = k.view(B, S, self.h, self.dh).transpose(1, 2)
-        v = v.view(B, S, self.h, self.dh).transpose(1, 2)
-        q = _rope(q, self.cos[:S], self.sin[:S])
-        k = _rope(k, self.cos[:S], self.sin[:S])
+        qkv = self.qkv(self.norm(x))
+        # RoPE of q and k in one kernel, bit-identical to _rope on each
+        q, k = rope_qk(qkv, self.cos, self.sin, self.h, self.dh)
+        v = qkv[..., 2 * C:].view(B, S, self.h, self.dh).transpose(1, 2)
         o = F.scaled_dot_product_attention(q, k, v, is_causal=True)
         return x + self.proj(o.transpose(1, 2).reshape(B, S, C))
 
@@ -160,14 +160,17 @@ class DWABlock(nn.Module):
     def queries(self, z: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         """([sqrt(w_s) q_s / (|q_s| + 1e-8)]_s packed per position, bf16 [B * seq, S d_k];
         w = softmax(aspect_logits))
-        (retrieval.py:159-160 with the aspect weights folded in)."""
+        (retrieval.py:159-160 with the aspect weights folded in).  One GEMM for the S
+        aspect projections, then one kernel for the normalisation, the packing and
+        the retrieval's device scalars (written into ``self._params``)."""
         B, S_len, C = z.shape
-        w = torch.softmax(self.retrieval.aspect_logits.float(), dim=0)
-        q = torch.einsum("btd,skd->btsk", z, self.retrieval.W_Q)
-        qf = q.float()
-        qf = qf * (w.sqrt()[None, None, :, None] /
-                   (torch.linalg.vector_norm(qf, dim=-1, keepdim=True) + 1e-8))
-        return qf.reshape(B * S_len, -1).to(torch.bfloat16), w
+        cfg = self.cfg
+        W_Q = self.retrieval.W_Q
+        q_raw = torch.matmul(z.reshape(B * S_len, C), W_Q.reshape(cfg.S * cfg.d_k, C).t())
+        q, w, _ = aspect_queries(q_raw, cfg.S, cfg.d_k, self.retrieval.aspect_logits,
+                                 self.retrieval.tau, cfg.lambda_sharp, cfg.T, cfg.use_sigmoid,
+                                 params_out=self._params)
+        return q, w
 
     def forward(self, h: torch.Tensor, retriever: Retriever,
                 vectors: torch.Tensor | None = None) -> torch.Tensor:
@@ -175,10 +178,7 @@ class DWABlock(nn.Module):
         cfg = self.cfg
         h = self.attn(h)
         z = self.query_proj(h)
-        q, w = self.queries(z)
-        tau = (torch.dot(w, self.retrieval.tau.float()) if cfg.use_sigmoid
-               else torch.zeros((), dtype=torch.float32, device=w.device))
-        self._params.copy_(score_params(cfg.lambda_sharp, tau, cfg.T, h.device))
+        q, w = self.queries(z)  # also the retrieval's {lambda, w . tau, T} in self._params
         if cfg.r > 0:
             # this block's pool keys from the pool vectors (retrieval.py:155-156)
             project_keys_packed(vectors, self.retrieval.W_K, w, out=retriever.keys)

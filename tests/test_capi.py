@@ -1,6 +1,7 @@
 """CPU tests of the C ABI: the library loads, exports exactly what
-include/dwa_retrieval.h declares, and rejects invalid arguments on the host
-without launching anything (no GPU is touched by these calls)."""
+include/*.h (dwa_retrieval.h, dwa_lm.h) declare, and rejects invalid
+arguments on the host without launching anything (no GPU is touched by these
+calls)."""
 import ctypes
 import re
 from pathlib import Path
@@ -10,11 +11,11 @@ import pytest
 from computd_b200 import _lib
 
 ROOT = Path(__file__).resolve().parents[1]
-HEADER = ROOT / "include" / "dwa_retrieval.h"
+HEADERS = sorted((ROOT / "include").glob("*.h"))
 
 
 def declared_symbols():
-    text = HEADER.read_text()
+    text = "\n".join(h.read_text() for h in HEADERS)
     return sorted(set(re.findall(r"DWA_API\s+[\w\s\*]+?\b(dwa_\w+)\s*\(", text)))
 
 
@@ -239,3 +240,29 @@ def test_device_scalar_and_seq_entry_points_validate_before_launch():
     assert seq(keys=FAKE + 8) == 2
     assert seq(sims=None) == 1
     assert seq(B=0) == 0 and seq(N=0) == 0
+
+
+def test_lm_helpers_reject_bad_arguments_on_host():
+    lib = _lib.load()
+    rope = lambda **kw: lib.dwa_lm_rope_qk(*[kw.get(n, v) for n, v in [
+        ("qkv", FAKE), ("B", 2), ("S", 64), ("H", 4), ("dh", 64), ("ld", 768), ("cos", FAKE),
+        ("sin", FAKE), ("ldcs", 32), ("q", FAKE), ("k", FAKE), ("stream", None)]])
+    assert rope(dh=60, ld=720) == 2                    # dh % 8
+    assert rope(ld=511) == 1                           # row shorter than q and k
+    assert rope(ld=516) == 2                           # ld_qkv % 8
+    assert rope(ldcs=31) == 1
+    assert rope(ldcs=34) == 2                          # ld_cs % 4
+    assert rope(qkv=FAKE + 8) == 2 and rope(sin=FAKE + 4) == 2
+    assert rope(q=None) == 1 and rope(H=0) == 1
+    assert rope(B=0) == 0 and rope(S=0) == 0
+    asp = lambda **kw: lib.dwa_lm_aspect_queries(*[kw.get(n, v) for n, v in [
+        ("q", FAKE), ("M", 100), ("S", 8), ("dk", 64), ("ldq", 512), ("logits", FAKE),
+        ("tau", FAKE), ("lam", 1.0), ("T", 1.0), ("sig", 1), ("out", FAKE), ("ldo", 512),
+        ("w", None), ("params", None), ("stream", None)]])
+    assert asp(S=0) == 2 and asp(S=65, ldq=65 * 64, ldo=65 * 64) == 2
+    assert asp(dk=60) == 2
+    assert asp(ldq=504) == 1 and asp(ldo=504) == 1
+    assert asp(ldq=520, ldo=516) == 2
+    assert asp(tau=None) == 1 and asp(logits=None) == 1
+    assert asp(out=None) == 1 and asp(q=FAKE + 8) == 2
+    assert asp(params=FAKE + 2) == 1
