@@ -222,9 +222,10 @@ class WeightAssembler:
         for h [M, d_A] and the summed delta f32 [M, d_B] of the retrieved rows
         (h_delta + b_delta; b_delta alone when the pool rows hold only b)."""
         if h.dtype == torch.bfloat16 and self.W_base.dtype == torch.bfloat16:
-            # bf16 operands, fp32 result: the tensor-core GEMM (exact products, fp32 sums)
-            base = torch.mm(h, self.W_base.t(), out_dtype=torch.float32)
-            base += self.b_base.to(torch.float32)
+            # bf16 operands, fp32 result: the tensor-core GEMM (exact products, fp32
+            # sums), the f32 bias added in its epilogue
+            base = torch.addmm(self.b_base.to(torch.float32), h, self.W_base.t(),
+                               out_dtype=torch.float32)
         else:
             base = torch.addmm(self.b_base.to(torch.float32), h.to(torch.float32),
                                self.W_base.to(torch.float32).t())

@@ -434,6 +434,73 @@ __device__ __forceinline__ float finish_x(const FinishArgs& a, int64_t m, int i)
 
 // One warp per row: x = residual + gamma * (base + delta); two-pass mean and
 // variance; out = (x - mean) / sqrt(var + eps) * scale + bias.
+// Rows of NV x 128 elements (d_B = 128 NV, 16-byte aligned rows): lane l holds
+// elements 128 j + 4 l .. + 3 in registers, read once with 16-byte loads.
+template <int NV>
+__global__ void __launch_bounds__(256) assemble_finish_reg_kernel(const FinishArgs a) {
+  const int64_t m = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (m >= a.M) return;
+  float4 x[NV];
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = 128 * j + 4 * lane;
+    float4 v = *reinterpret_cast<const float4*>(a.delta + m * a.d_B + i);
+    if (a.base) {
+      const float4 bv = *reinterpret_cast<const float4*>(a.base + m * a.d_B + i);
+      v.x += bv.x; v.y += bv.y; v.z += bv.z; v.w += bv.w;
+    }
+    v.x *= a.gamma; v.y *= a.gamma; v.z *= a.gamma; v.w *= a.gamma;
+    if (a.residual) {
+      if (a.res_bf16) {
+        const uint2 r = *reinterpret_cast<const uint2*>(
+            static_cast<const __nv_bfloat16*>(a.residual) + m * a.ldr + i);
+        v.x += __uint_as_float(r.x << 16);
+        v.y += __uint_as_float(r.x & 0xFFFF0000u);
+        v.z += __uint_as_float(r.y << 16);
+        v.w += __uint_as_float(r.y & 0xFFFF0000u);
+      } else {
+        const float4 r = *reinterpret_cast<const float4*>(
+            static_cast<const float*>(a.residual) + m * a.ldr + i);
+        v.x += r.x; v.y += r.y; v.z += r.z; v.w += r.w;
+      }
+    }
+    x[j] = v;
+    s += (v.x + v.y) + (v.z + v.w);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / static_cast<float>(a.d_B);
+  float var = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const float dx = x[j].x - mean, dy = x[j].y - mean, dz = x[j].z - mean, dw = x[j].w - mean;
+    var = fmaf(dx, dx, var);
+    var = fmaf(dy, dy, var);
+    var = fmaf(dz, dz, var);
+    var = fmaf(dw, dw, var);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+  const float inv = rsqrtf(var / static_cast<float>(a.d_B) + a.eps);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = 128 * j + 4 * lane;
+    float4 y = make_float4((x[j].x - mean) * inv, (x[j].y - mean) * inv, (x[j].z - mean) * inv,
+                           (x[j].w - mean) * inv);
+    if (a.ln_scale) {
+      const float4 sc = *reinterpret_cast<const float4*>(a.ln_scale + i);
+      y.x *= sc.x; y.y *= sc.y; y.z *= sc.z; y.w *= sc.w;
+    }
+    if (a.ln_bias) {
+      const float4 bi = *reinterpret_cast<const float4*>(a.ln_bias + i);
+      y.x += bi.x; y.y += bi.y; y.z += bi.z; y.w += bi.w;
+    }
+    *reinterpret_cast<float4*>(a.out + m * a.d_B + i) = y;
+  }
+}
+
 __global__ void __launch_bounds__(256) assemble_finish_kernel(const FinishArgs a) {
   const int64_t m = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -549,6 +616,25 @@ cudaError_t launch_assemble_finish(const void* residual, int res_bf16, int64_t l
                                    float eps, float* out, cudaStream_t stream) {
   FinishArgs a{residual, res_bf16, ldr, base, delta, M, d_B, gamma, ln_scale, ln_bias, eps, out};
   const int64_t blocks = (M * 32 + 255) / 256;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const bool vec = d_B % 128 == 0 && d_B <= 2048 && al16(delta) && al16(out) &&
+                   (base == nullptr || al16(base)) &&
+                   (residual == nullptr ||
+                    ((reinterpret_cast<uintptr_t>(residual) & (res_bf16 ? 7u : 15u)) == 0 &&
+                     ldr % 4 == 0)) &&
+                   (ln_scale == nullptr || al16(ln_scale)) && (ln_bias == nullptr || al16(ln_bias));
+  if (vec) {
+    switch (d_B / 128) {
+#define DWA_FINISH_CASE(n) \
+  case n: assemble_finish_reg_kernel<n><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a); break;
+      DWA_FINISH_CASE(1) DWA_FINISH_CASE(2) DWA_FINISH_CASE(3) DWA_FINISH_CASE(4)
+      DWA_FINISH_CASE(5) DWA_FINISH_CASE(6) DWA_FINISH_CASE(7) DWA_FINISH_CASE(8)
+      DWA_FINISH_CASE(9) DWA_FINISH_CASE(10) DWA_FINISH_CASE(11) DWA_FINISH_CASE(12)
+      DWA_FINISH_CASE(13) DWA_FINISH_CASE(14) DWA_FINISH_CASE(15) DWA_FINISH_CASE(16)
+#undef DWA_FINISH_CASE
+    }
+    return cudaGetLastError();
+  }
   assemble_finish_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
   return cudaGetLastError();
 }

@@ -154,9 +154,11 @@ def test_lowrank_rows_reference_1b_layout(lib):
     _close(got[sel].cpu().numpy(), want)
 
 
-def test_assemble_finish_vs_oracle(lib):
-    rng = np.random.default_rng(11)
-    M, d = 77, 200
+@pytest.mark.parametrize("M,d", [(77, 200), (300, 1280), (33, 128), (9, 2048)])
+def test_assemble_finish_vs_oracle(lib, M, d):
+    """The generic kernel (d = 200) and the register-resident one (d a multiple
+    of 128 up to 2048, 16-byte aligned rows)."""
+    rng = np.random.default_rng(11 + d)
     delta = rng.standard_normal((M, d)).astype(np.float32)
     base = rng.standard_normal((M, d)).astype(np.float32)
     res = O.bf16_round(rng.standard_normal((M, d)).astype(np.float32))
