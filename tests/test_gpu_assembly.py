@@ -81,10 +81,11 @@ def test_lowrank_delta_vs_oracle(lib, M, N, d_A, d_B, r, k, extra, rows):
     torch.testing.assert_close(got32, got, rtol=1e-5, atol=1e-5)
 
 
+@pytest.mark.parametrize("d_A,d_B", [(128, 96), (256, 128)])
 @pytest.mark.parametrize("rows", [False, True])
-def test_lowrank_delta_owner_computes_partials_add_up(lib, rows):
+def test_lowrank_delta_owner_computes_partials_add_up(lib, rows, d_A, d_B):
     rng = np.random.default_rng(7)
-    M, N, d_A, d_B, r, k, P = 120, 900, 128, 96, 8, 12, 3
+    M, N, r, k, P = 120, 900, 8, 12, 3
     D = d_B * r + r * d_A + d_B
     vectors = _bf16((rng.standard_normal((N, D)) * 0.2).astype(np.float32))
     h = _bf16(rng.standard_normal((M, d_A)).astype(np.float32))
@@ -101,12 +102,13 @@ def test_lowrank_delta_owner_computes_partials_add_up(lib, rows):
     assert torch.count_nonzero(none) == 0
 
 
-def test_lowrank_rows_skewed_rows_and_determinism(lib):
+@pytest.mark.parametrize("d_B", [192, 256])
+def test_lowrank_rows_skewed_rows_and_determinism(lib, d_B):
     """Row-stationary path: a few rows selected by every token (their pairs span
     many 32-pair chunks), repeated rows inside a token, the per-token kernel as
     the reference, and two runs bit-identical (no float atomics)."""
     rng = np.random.default_rng(21)
-    M, N, d_A, d_B, r, k = 700, 3000, 256, 192, 8, 16
+    M, N, d_A, r, k = 700, 3000, 256, 8, 16
     D = d_B * r + r * d_A + d_B
     vectors = _bf16((rng.standard_normal((N, D)) * 0.2).astype(np.float32))
     h = _bf16(rng.standard_normal((M, d_A)).astype(np.float32))
