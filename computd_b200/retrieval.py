@@ -725,6 +725,32 @@ class MultiAspectRetrieval:
     def _normalize(x: torch.Tensor) -> torch.Tensor:
         return x / (torch.linalg.norm(x, dim=-1, keepdim=True) + 1e-8)
 
+    def _project_queries(self, z: torch.Tensor) -> torch.Tensor:
+        """sum_d W_Q[s, k, d] z[b, t, d] in fp32 (retrieval.py:159, 247), f32 [B, seq, S, d_k].
+
+        For bf16 z every product with a bf16 weight is exact in fp32, so the fp32
+        einsum equals bf16 tensor-core GEMMs with fp32 accumulation: one GEMM for
+        bf16 W_Q; for fp32 W_Q, W_Q = hi + mid + lo (three bf16 parts, together
+        within 2^-24 of W_Q) and three GEMMs accumulating into one fp32 result.
+        fp32 z keeps the fp32 einsum."""
+        B, seq, d_A = z.shape
+        if z.dtype != torch.bfloat16 or not z.is_cuda:
+            return torch.einsum("skd,btd->btsk", self.W_Q.float(), z.float())
+        z2 = z.reshape(B * seq, d_A)
+        W = self.W_Q.reshape(self.S * self.d_k, d_A)
+        if W.dtype == torch.bfloat16:
+            q = torch.mm(z2, W.t(), out_dtype=torch.float32)
+        else:
+            Wf = W.float()
+            hi = Wf.to(torch.bfloat16)
+            r = Wf - hi.float()
+            mid = r.to(torch.bfloat16)
+            lo = (r - mid.float()).to(torch.bfloat16)
+            q = torch.mm(z2, hi.t(), out_dtype=torch.float32)
+            q = torch.addmm(q, z2, mid.t(), out_dtype=torch.float32)
+            q = torch.addmm(q, z2, lo.t(), out_dtype=torch.float32)
+        return q.view(B, seq, self.S, self.d_k)
+
     def project_keys(self, vectors: torch.Tensor, w: torch.Tensor, chunk_rows: int = 1 << 18
                      ) -> torch.Tensor:
         """keys_w = sum_s w_s W_K[s] v / (|W_K[s] v| + 1e-8) for every pool row
@@ -776,8 +802,7 @@ class MultiAspectRetrieval:
         tau = (torch.dot(w, self.tau.float()) if use_sigmoid                    # 168
                else torch.zeros((), dtype=torch.float32, device=w.device))
         keys_p = self.project_keys_packed(vectors, w)                           # 155-156
-        zf = z.float()
-        queries_s = self._normalize(torch.einsum("skd,btd->btsk", self.W_Q.float(), zf))  # 159-160
+        queries_s = self._normalize(self._project_queries(z))                  # 159-160
         q_packed = (queries_s * w.sqrt()[None, None, :, None]).reshape(B, seq, -1)
         queries_flat = q_packed.reshape(B * seq, -1).to(torch.bfloat16)
         # 163-175: the aspect-weighted score of every (position, key), its gate/exp,
@@ -817,8 +842,8 @@ class MultiAspectRetrieval:
                else torch.zeros((), dtype=torch.float32, device=w.device))
         keys_w = self.project_keys(vectors, w)                                  # 241-242, 261
         zf = z.float()
-        queries_s = self._normalize(torch.einsum("skd,btd->sbtk", self.W_Q.float(), zf))  # 247-248
-        queries_w = torch.einsum("s,sbtk->btk", w, queries_s)                   # 262
+        queries_s = self._normalize(self._project_queries(z))                  # 247-248
+        queries_w = torch.einsum("s,btsk->btk", w, queries_s)                   # 262
         queries_flat = queries_w.reshape(B * seq, self.d_k).to(torch.bfloat16)  # 263
         group = mesh if (tp_axis is not None and mesh is not None) else None
         final_v, final_i = chip_topk(queries_flat, keys_w, k_max, lambda_sharp, tau, T,
