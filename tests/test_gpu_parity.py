@@ -479,6 +479,29 @@ def test_score_topk_seqmean_vs_fp64(lib, B, seq, N, d, k, sig):
     torch.testing.assert_close(mean.double(), want, rtol=1e-4, atol=0)
 
 
+@pytest.mark.parametrize("M,N,d,k,seq", [(600, 30000, 512, 128, 200),       # whole-heap list
+                                          (18944, 524288, 512, 128, 256)])  # two-level list
+def test_score_topk_seqmean_k128(lib, M, N, d, k, seq):
+    """The seq-mean epilogue on the k > 64 lists (the whole shared-memory heap for
+    short units, the register + heap two-level list for long ones): the top-k equal
+    to the plain kernel's and the fused means of sampled sequences against fp64."""
+    dev = _dev()
+    q = lib.new_normal(M, d, seed=M + k, stddev=d ** -0.5, device=dev)
+    keys = lib.new_normal(N, d, seed=N + d, stddev=d ** -0.5, device=dev)
+    lam, tau, T = 2.0, 0.02, 0.5
+    tv, ti, mean = lib.score_topk_seqmean(q, keys, k, lam, tau, T, True, seq)
+    params = lib.score_params(lam, tau, T, dev)
+    tv2, ti2 = lib.tiled_topk_fused(q, keys, k, params[0], params[1], params[2], True)
+    torch.cuda.synchronize()
+    assert torch.equal(ti, ti2) and torch.equal(tv, tv2)
+    kd = keys.double()
+    B = M // seq
+    for b in sorted({0, B // 2, B - 1}):
+        s = q[b * seq:(b + 1) * seq].double() @ kd.T
+        v = torch.exp(s / T) * torch.sigmoid(lam * (s - tau))
+        torch.testing.assert_close(mean[b].double(), v.mean(0), rtol=1e-4, atol=0)
+
+
 @pytest.mark.parametrize("k", [100, 128])
 def test_exact_ties_two_level_list(lib, k):
     """k > 64 over units whose key tiles x d reach 2^20 takes the two-level list
