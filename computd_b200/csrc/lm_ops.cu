@@ -5,11 +5,12 @@
 //  * rope_qk_kernel: the rotary embedding of the attention's queries and keys
 //    (parts.py:17-25: x1 = x[..., 0::2], x2 = x[..., 1::2],
 //    [x1 cos - x2 sin, x1 sin + x2 cos]) read straight from the QKV
-//    projection's rows and written in the [B, H, S, dh] layout attention
-//    takes.  Each product, sum and difference is rounded to bf16 as the
-//    elementwise bf16 tensor ops do, so the result is bit-identical to them;
-//    one pass instead of six elementwise kernels and a concatenation per
-//    tensor.
+//    projection's rows and written token-major, [B, S, H, dh], the layout
+//    attention reads through a (1, 2)-transposed view and writes its output
+//    in, so the output projection needs no transposing copy.  Each product,
+//    sum and difference is rounded to bf16 as the elementwise bf16 tensor ops
+//    do, so the result is bit-identical to them; one pass instead of six
+//    elementwise kernels and a concatenation per tensor.
 //  * aspect_queries_kernel: the packed aspect queries of the hybrid score
 //    (retrieval.py:159-168): w = softmax(aspect_logits), and per row m and
 //    aspect s, q[m, s, :] sqrt(w_s) / (|q[m, s, :]| + 1e-8) in bf16; block 0
@@ -71,7 +72,7 @@ __global__ void rope_qk_kernel(const uint16_t* __restrict__ qkv, int64_t B, int6
     lo[p] = to_bf(rbf(x1 * c) - rbf(x2 * sn));
     hi[p] = to_bf(rbf(x1 * sn) + rbf(x2 * c));
   }
-  uint16_t* o = (which ? k_out : q_out) + ((b * H + h) * S + s) * dh;
+  uint16_t* o = (which ? k_out : q_out) + ((b * S + s) * H + h) * dh;
   uint2 lw, hw;
   lw.x = static_cast<uint32_t>(lo[0]) | (static_cast<uint32_t>(lo[1]) << 16);
   lw.y = static_cast<uint32_t>(lo[2]) | (static_cast<uint32_t>(lo[3]) << 16);

@@ -16,9 +16,11 @@ def rope_qk(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, n_heads: in
 
     ``qkv`` bf16 [B, S, W] with rows of uniform stride (q in columns
     [0, H dh), k in [H dh, 2 H dh)); ``cos`` / ``sin`` bf16 [>= S, dh / 2].
-    Returns q, k bf16 [B, H, S, dh] (contiguous) with
+    Returns q, k bf16 [B, H, S, dh] with
     [x1 cos - x2 sin, x1 sin + x2 cos] for x1 = x[..., 0::2], x2 = x[..., 1::2],
-    every step rounded to bf16 as the elementwise bf16 tensor ops round it."""
+    every step rounded to bf16 as the elementwise bf16 tensor ops round it; both
+    are (1, 2)-transposed views of token-major [B, S, H, dh] buffers, the layout
+    attention then also writes its output in."""
     if qkv.dtype != torch.bfloat16 or qkv.dim() != 3:
         raise ValueError("qkv must be a bf16 [B, S, W] tensor")
     B, S, W = qkv.shape
@@ -33,7 +35,7 @@ def rope_qk(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, n_heads: in
             raise ValueError("cos / sin must be bf16 [>= S, dh / 2] on the qkv device")
     if cos.stride(0) != sin.stride(0):
         raise ValueError("cos and sin must share a row stride")
-    q = torch.empty((B, H, S, dh), dtype=torch.bfloat16, device=qkv.device)
+    q = torch.empty((B, S, H, dh), dtype=torch.bfloat16, device=qkv.device)
     k = torch.empty_like(q)
     lib = _lib.load()
     with torch.cuda.device(qkv.device):
@@ -41,7 +43,7 @@ def rope_qk(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, n_heads: in
                                 sin.data_ptr(), cos.stride(0), q.data_ptr(), k.data_ptr(),
                                 _stream_handle(qkv.device))
     _lib.check(st, "dwa_lm_rope_qk")
-    return q, k
+    return q.transpose(1, 2), k.transpose(1, 2)
 
 
 def aspect_queries(q_raw: torch.Tensor, S: int, d_k: int, aspect_logits: torch.Tensor,

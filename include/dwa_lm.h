@@ -20,12 +20,12 @@ extern "C" {
  * for x = the q (columns [0, H dh)) or k (columns [H dh, 2 H dh)) part of
  * row (b, s) of the QKV projection qkv (bf16 [B S, ld_qkv]) and each head,
  * x1 = x[0::2], x2 = x[1::2] (dh / 2 each),
- *   out[b, h, s, 0:dh/2]  = x1 cos[s] - x2 sin[s]
- *   out[b, h, s, dh/2:dh] = x1 sin[s] + x2 cos[s]
+ *   out[b, s, h, 0:dh/2]  = x1 cos[s] - x2 sin[s]
+ *   out[b, s, h, dh/2:dh] = x1 sin[s] + x2 cos[s]
  * with every product, sum and difference rounded to bf16 (bit-identical to
  * the same steps as elementwise bf16 tensor operations).  cos / sin: bf16
- * [S, ld_cs] (first dh / 2 columns used); q_out / k_out: bf16 [B, H, S, dh]
- * contiguous.  dh % 8 == 0; ld_qkv % 8 == 0, ld_cs % 4 == 0; qkv, q_out,
+ * [S, ld_cs] (first dh / 2 columns used); q_out / k_out: bf16 [B, S, H, dh]
+ * contiguous (token-major, as the rows of qkv).  dh % 8 == 0; ld_qkv % 8 == 0, ld_cs % 4 == 0; qkv, q_out,
  * k_out 16-byte aligned, cos / sin 8-byte aligned.
  */
 DWA_API dwa_status dwa_lm_rope_qk(const void* qkv, int64_t B, int64_t S, int32_t H, int32_t dh,

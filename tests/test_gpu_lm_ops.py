@@ -29,7 +29,7 @@ def test_rope_qk_matches_tensor_ops(B, S, H, dh):
     torch.cuda.synchronize()
     q_ref = _rope(qkv[..., :C].view(B, S, H, dh).transpose(1, 2), cos[:S], sin[:S])
     k_ref = _rope(qkv[..., C:2 * C].view(B, S, H, dh).transpose(1, 2), cos[:S], sin[:S])
-    assert q.is_contiguous() and q.shape == (B, H, S, dh)
+    assert q.shape == (B, H, S, dh) and q.transpose(1, 2).is_contiguous()
     assert torch.equal(q, q_ref) and torch.equal(k, k_ref)
 
 
