@@ -14,6 +14,8 @@
 // fp32 (the reference computes this product in fp32), and the KR x QB dot
 // products of a warp are summed across its lanes with one transpose-reduction.
 // B > QB takes several passes over the keys.
+#include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -21,6 +23,7 @@
 
 #include "dwa_internal.h"
 #include "score_params.cuh"
+#include "sm100_ptx.cuh"
 
 namespace dwa {
 
@@ -187,6 +190,237 @@ cudaError_t launch_qb(const SeqArgs& a, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------- tensor-core path
+// For up to kSqMaxQ queries whose split operand fits in shared memory: the
+// product runs on the tensor cores as D[128 keys x npad] = K_tile . Qs^T, the
+// key tiles streamed by TMA through a kSqStages-deep ring and the accumulators
+// double-buffered in TMEM, so the kernel is bound by reading the keys once
+// from HBM, not by CUDA-core issue.  The fp32 queries enter the bf16 MMA as
+// three bf16 parts q = hi + mid + lo (hi = bf16(q), mid = bf16(q - hi),
+// lo = bf16(q - hi - mid), which represent q exactly), rows 3 b + p of the
+// staged operand: every product with a bf16 key is exact in fp32 and the MMA
+// accumulates in fp32, so sims = (D[3b] + D[3b+1]) + D[3b+2] keeps the fp32
+// product of the reference.  Persistent CTAs take key tiles t = blockIdx.x +
+// i gridDim.x; warp 0 issues the TMA loads, warp 1 the MMAs, warps 2-5 read
+// the accumulators (one key per thread) and write sims / fused.
+constexpr int kSqKeys = 128;     // keys per tile = TMEM lanes
+constexpr int kSqK = 64;         // d per k-block: 128-byte rows
+constexpr int kSqStages = 4;
+constexpr int kSqThreads = 192;
+constexpr int kSqMaxQ = 10;      // 3 parts each: <= 30 of the 32 accumulator columns
+constexpr int kSqStageBytes = kSqKeys * kSqK * 2;  // 16 KB
+constexpr int kSqBarBytes = 256;
+
+struct SeqMmaArgs {
+  const float* q;
+  int64_t ldq;
+  int nq;        // queries of this launch (<= kSqMaxQ)
+  int npad;      // operand rows: 3 nq rounded up to 16
+  int64_t N;
+  int d, num_kb;
+  int64_t n_tiles;
+  const float* params;
+  int use_sigmoid;
+  float* sims;
+  int64_t lds;
+  float* fused;
+  int64_t ldf;
+  int* status;
+};
+
+size_t seq_mma_smem_bytes(int npad, int num_kb) {
+  return 1024 + static_cast<size_t>(num_kb) * npad * 128 +
+         static_cast<size_t>(kSqStages) * kSqStageBytes + kSqBarBytes;
+}
+
+__global__ void __launch_bounds__(kSqThreads, 1)
+    seq_scores_mma_kernel(const __grid_constant__ CUtensorMap tmap_k, const SeqMmaArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw_addr);
+  const uint32_t q_tile_bytes = static_cast<uint32_t>(a.npad) * 128u;  // one k-block of the operand
+  const uint32_t qop = base;
+  const uint32_t ring = base + static_cast<uint32_t>(a.num_kb) * q_tile_bytes;
+  uint8_t* bar_area = smem + static_cast<size_t>(a.num_kb) * q_tile_bytes +
+                      static_cast<size_t>(kSqStages) * kSqStageBytes;
+  const uint32_t bar0 = smem_u32(bar_area);
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (kSqStages + s); };
+  auto tfull_bar = [&](int acc) { return bar0 + 8u * (2 * kSqStages + acc); };
+  auto tempty_bar = [&](int acc) { return bar0 + 8u * (2 * kSqStages + 2 + acc); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * kSqStages + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_area + 8 * (2 * kSqStages + 5));
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* n_issued = reinterpret_cast<int*>(tmem_slot + 2);
+  int* n_consumed = reinterpret_cast<int*>(tmem_slot + 3);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t my_tiles =
+      blockIdx.x < a.n_tiles ? (a.n_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+
+  // The split-query operand, all k-blocks, in the TMA 128-byte-swizzle layout
+  // (row r, 16-byte chunk c of a k-block at (r / 8) 1024 + (r % 8) 128 +
+  // ((c ^ (r % 8)) 16)); zeros beyond d and beyond 3 nq rows.
+  const int chunks = a.num_kb * a.npad * 8;
+  for (int idx = threadIdx.x; idx < chunks; idx += blockDim.x) {
+    const int kb = idx / (a.npad * 8);
+    const int rem = idx - kb * a.npad * 8;
+    const int r = rem >> 3, c = rem & 7;
+    const int b = r / 3, part = r - 3 * b;
+    uint32_t w[4];
+#pragma unroll
+    for (int e2 = 0; e2 < 4; ++e2) {
+      uint32_t h2 = 0;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int col = kb * kSqK + c * 8 + 2 * e2 + h;
+        const float x = (b < a.nq && col < a.d) ? __ldg(a.q + b * a.ldq + col) : 0.f;
+        const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+        const float r1 = x - __bfloat162float(hi);
+        const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+        const __nv_bfloat16 lo = __float2bfloat16_rn(r1 - __bfloat162float(mid));
+        const __nv_bfloat16 v = part == 0 ? hi : part == 1 ? mid : lo;
+        h2 |= static_cast<uint32_t>(__bfloat16_as_ushort(v)) << (16 * h);
+      }
+      w[e2] = h2;
+    }
+    const uint32_t off = static_cast<uint32_t>(kb) * q_tile_bytes + (r >> 3) * 1024u +
+                         (r & 7) * 128u + static_cast<uint32_t>((c ^ (r & 7)) * 16);
+    *reinterpret_cast<uint4*>(smem + off) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  fence_proxy_async_smem();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kSqStages; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int acc = 0; acc < 2; ++acc) {
+      mbar_init(tfull_bar(acc), 1);
+      mbar_init(tempty_bar(acc), 4);  // the four epilogue warps
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    *n_issued = 0;
+    *n_consumed = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmap_k);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 64);  // two accumulators of 32 columns
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();  // the keys are read once
+      int it = 0;
+      bool ok = true;
+      for (int64_t i = 0; i < my_tiles && ok; ++i) {
+        const int32_t krow = static_cast<int32_t>((blockIdx.x + i * gridDim.x) * kSqKeys);
+        for (int kb = 0; kb < a.num_kb; ++kb, ++it) {
+          const int s = it % kSqStages;
+          const uint32_t ph = static_cast<uint32_t>(it / kSqStages);
+          if (!mbar_wait(empty_bar(s), (ph & 1u) ^ 1u, a.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full_bar(s), kSqStageBytes);
+          tma_load_2d(ring + s * kSqStageBytes, &tmap_k, full_bar(s), kb * kSqK, krow, pol);
+        }
+      }
+      *n_issued = it;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_bf16_f32(kSqKeys, a.npad);
+      int it = 0;
+      bool ok = true;
+      for (int64_t i = 0; i < my_tiles && ok; ++i) {
+        const int acc = static_cast<int>(i & 1);
+        const uint32_t use = static_cast<uint32_t>(i >> 1);
+        if (!mbar_wait(tempty_bar(acc), (use & 1u) ^ 1u, a.status, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t tmem_d = tmem_base + static_cast<uint32_t>(acc * 32);
+        for (int kb = 0; kb < a.num_kb; ++kb, ++it) {
+          const int s = it % kSqStages;
+          const uint32_t ph = static_cast<uint32_t>(it / kSqStages);
+          if (!mbar_wait(full_bar(s), ph & 1u, a.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = sw128_kmajor_desc(ring + s * kSqStageBytes);
+          const uint64_t bd = sw128_kmajor_desc(qop + static_cast<uint32_t>(kb) * q_tile_bytes);
+#pragma unroll
+          for (int kk = 0; kk < kSqK / 16; ++kk)
+            umma_bf16_ss(tmem_d, ad + 2u * kk, bd + 2u * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+          umma_commit(empty_bar(s));
+        }
+        if (ok) umma_commit(tfull_bar(acc));
+      }
+      *n_consumed = it;
+      // every MMA must finish (it writes TMEM, reads shared memory) before release
+      umma_commit(drain_bar);
+      mbar_wait(drain_bar, 0u, a.status, nullptr);
+    }
+  } else {
+    const int quarter = warp & 3;  // TMEM lanes this warp may read
+    const int row = quarter * 32 + lane;
+    const ScoreParams sp = load_score_params(a.params, 1.0f, 0.0f, 1.0f);
+    const bool params_ok = score_params_ok(sp, a.use_sigmoid);
+    if (!params_ok && blockIdx.x == 0 && threadIdx.x == 64) record_status(a.status, kStatusDeviceCheck);
+    for (int64_t i = 0; i < my_tiles; ++i) {
+      const int acc = static_cast<int>(i & 1);
+      const uint32_t use = static_cast<uint32_t>(i >> 1);
+      const bool got = mbar_wait(tfull_bar(acc), use & 1u, a.status, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) break;
+      tc_fence_after();
+      float v[32];
+      tmem_ld_32x32b_x32_sync(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                  static_cast<uint32_t>(acc * 32),
+                              v);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(acc));
+      const int64_t n = (blockIdx.x + i * gridDim.x) * kSqKeys + row;
+      if (n < a.N) {
+#pragma unroll
+        for (int b = 0; b < kSqMaxQ; ++b) {
+          if (b < a.nq) {
+            const float sv = (v[3 * b] + v[3 * b + 1]) + v[3 * b + 2];
+            a.sims[b * a.lds + n] = sv;
+            if (a.fused != nullptr) {
+              float f = NAN;
+              if (params_ok) {
+                f = expf(sv / sp.T);
+                if (a.use_sigmoid) f *= 1.0f / (1.0f + expf(-(sp.lambda_sharp * (sv - sp.tau))));
+              }
+              a.fused[b * a.ldf + n] = f;
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // Loads issued but never consumed (only after an abort) must land before exit.
+    for (int i = *n_consumed; i < *n_issued; ++i)
+      mbar_wait(full_bar(i % kSqStages), static_cast<uint32_t>(i / kSqStages) & 1u, a.status, nullptr);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 64);
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_seq_scores(const float* q, int64_t B, int64_t ldq, const void* keys, int64_t N,
@@ -194,6 +428,29 @@ cudaError_t launch_seq_scores(const float* q, int64_t B, int64_t ldq, const void
                               float* sims, int64_t lds, float* fused, int64_t ldf, int* status,
                               cudaStream_t stream) {
   if (B <= 0 || N <= 0) return cudaSuccess;
+  // Tensor cores when all queries fit one launch and their split operand
+  // leaves the ring its stages; CUDA cores otherwise.
+  if (B <= kSqMaxQ) {
+    const int npad = static_cast<int>((3 * B + 15) / 16 * 16);
+    const int num_kb = (d + kSqK - 1) / kSqK;
+    const size_t smem = seq_mma_smem_bytes(npad, num_kb);
+    CUtensorMap mk;
+    if (smem <= 232448 && (reinterpret_cast<uintptr_t>(keys) & 15u) == 0 && ldk % 8 == 0 &&
+        N <= INT32_MAX - kSqKeys &&
+        make_bf16_tile_map(&mk, keys, static_cast<uint64_t>(d), static_cast<uint64_t>(N),
+                           static_cast<uint64_t>(ldk), kSqK, kSqKeys)) {
+      SeqMmaArgs m{q, ldq, static_cast<int>(B), npad, N, d, num_kb,
+                   (N + kSqKeys - 1) / kSqKeys, params, use_sigmoid, sims, lds, fused, ldf,
+                   status};
+      cudaError_t e = cudaFuncSetAttribute(seq_scores_mma_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem));
+      if (e != cudaSuccess) return e;
+      const int64_t grid = std::min<int64_t>(m.n_tiles, device_sm_count());
+      seq_scores_mma_kernel<<<static_cast<unsigned>(grid), kSqThreads, smem, stream>>>(mk, m);
+      return cudaGetLastError();
+    }
+  }
   SeqArgs a{q, B, ldq, static_cast<const uint16_t*>(keys), N, ldk, d, params, use_sigmoid,
             sims, lds, fused, ldf, status};
   if (B <= 4 && 4ll * 4 * d <= kSmemLimit) return launch_qb<4>(a, stream);
