@@ -120,8 +120,10 @@ def test_fused_backward_equals_the_four_kernel_path(M, N, d, dv, k, sig, q_bf16,
 @pytest.mark.parametrize("out_bf16", [False, True])
 def test_row_gradient_equals_zero_fill_and_scatter(out_bf16):
     """dwa_row_gradient (one write of the owned rows) against zero-filled f32 +
-    dwa_scatter_add_rows: the same sums (their order may differ), untouched
-    rows exactly zero, an owned sub-range, bf16 output = the f32 result rounded."""
+    dwa_scatter_add_rows and an fp64 sum: the same sums (their order may differ:
+    the atomics' order is not fixed, so both are held to the fp32 summation
+    bound (n - 1) 2^-24 sum |w a| of the fp64 value), untouched rows exactly
+    zero, an owned sub-range, bf16 output = the f32 result rounded."""
     from computd_b200 import _lib
     from computd_b200.tiled_topk import _stream_handle
 
@@ -151,11 +153,16 @@ def test_row_gradient_equals_zero_fill_and_scatter(out_bf16):
         own = (idx >= rb) & (idx < re)
         sel[(idx[own] - rb).long()] = True
         assert bool((out[~sel] == 0).all())       # untouched rows written as zeros
+        rows = (idx[own] - rb).long()
+        terms = (w[own][:, None].double() * a[own.nonzero()[:, 0]].double())
+        ref64 = torch.zeros(n, d, device=dev, dtype=torch.float64).index_add_(0, rows, terms)
+        bound = torch.zeros(n, d, device=dev, dtype=torch.float64).index_add_(0, rows, terms.abs())
+        tol = (M - 1) * 2.0 ** -24 * bound + 1e-7
+        assert bool(((ref.double() - ref64).abs() <= tol).all())   # the scatter reference itself
         if out_bf16:
-            torch.testing.assert_close(out.float(), ref.to(torch.bfloat16).float(), rtol=1e-2,
-                                       atol=1e-2)
+            assert bool(((out.double() - ref64).abs() <= 2.0 ** -8 * ref64.abs() + tol).all())
         else:
-            torch.testing.assert_close(out, ref, rtol=1e-5, atol=1e-5)
+            assert bool(((out.double() - ref64).abs() <= tol).all())
     # no queries: the whole owned gradient is zero
     out = torch.full((N, d), 1.0, device=dev)
     assert lib.dwa_row_gradient(w.data_ptr(), idx.data_ptr(), 0, k, a.data_ptr(), 1, d, 0, N,
