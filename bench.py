@@ -580,7 +580,19 @@ def measure_hybrid(local_rank, warmup=3, steps=10):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / n
 
-    ms_fwd = timed(lambda: m.hybrid_forward(z, vectors, k, 1.0, 1.0, True), steps)
+    ms_eager = timed(lambda: m.hybrid_forward(z, vectors, k, 1.0, 1.0, True), steps)
+    # The same call captured once in a CUDA graph and replayed: the device time
+    # without the host's per-op launch overhead (what a jitted caller sees).
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        m.hybrid_forward(z, vectors, k, 1.0, 1.0, True)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        m.hybrid_forward(z, vectors, k, 1.0, 1.0, True)
+    ms_fwd = timed(graph.replay, steps)
+    del graph
     p = m.hybrid_parts(z, vectors, k, 1.0, 1.0, True)
     q, keys = p.queries_flat, p.keys_w
     params = cb.score_params(1.0, p.tau, 1.0, dev)
@@ -604,7 +616,8 @@ def measure_hybrid(local_rank, warmup=3, steps=10):
     torch.cuda.empty_cache()
     return {"config": "reference 1B hybrid layout: batch 8 x seq 1024, d_A 1280, S 8 x d_k 64, "
                       "pool 16384 x 21760, k 16, gate on",
-            "hybrid_forward_ms": ms_fwd, "tokens_per_s": B * seq / (ms_fwd * 1e-3),
+            "hybrid_forward_ms": ms_fwd, "timing": "CUDA-graph replay of the whole call",
+            "hybrid_forward_eager_ms": ms_eager, "tokens_per_s": B * seq / (ms_fwd * 1e-3),
             "score_topk_seqmean_ms": ms_aux, "score_topk_plain_ms": ms_plain,
             "seqmean_overhead": ms_aux / ms_plain - 1.0,
             "roofline_score": {"bound": "tensor", "flops_per_launch": flops,
