@@ -7,13 +7,17 @@
 //                           or exp(sims / T)                    (338-341)
 // for the B sequence-mean queries (B = batch, a handful of rows) against every
 // key of the shard.  With B this small the product is a skinny
-// [B, d] x [d, N] whose cost is reading the key shard once from HBM, so it
-// runs on the CUDA cores, not the tensor pipe: each warp streams KR key rows
-// at a time with 16-byte loads (the next chunk's loads are in flight while the
-// current chunk's FMAs run), the QB queries of a pass sit in shared memory in
-// fp32 (the reference computes this product in fp32), and the KR x QB dot
-// products of a warp are summed across its lanes with one transpose-reduction.
-// B > QB takes several passes over the keys.
+// [B, d] x [d, N] whose cost is reading the key shard once from HBM.  Two
+// kernels:
+//  * seq_scores_mma_kernel (B <= 10 and the split query operand fits in
+//    shared memory): tcgen05 with TMA-streamed key tiles, the fp32 queries as
+//    three exact bf16 parts, fp32 accumulation; it runs at HBM speed;
+//  * seq_scores_kernel otherwise, on the CUDA cores: each warp streams KR key
+//    rows at a time with 16-byte loads (the next chunk's loads are in flight
+//    while the current chunk's FMAs run), the QB queries of a pass sit in
+//    shared memory in fp32 (the reference computes this product in fp32), and
+//    the KR x QB dot products of a warp are summed across its lanes with one
+//    transpose-reduction; B > QB takes several passes over the keys.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
