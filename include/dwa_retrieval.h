@@ -167,7 +167,9 @@ DWA_API dwa_status dwa_score_topk_seqmean(const void* q, int64_t M, int64_t ldq,
  *               = exp(sims / T)                                        otherwise
  * sims f32 [B, lds], fused f32 [B, ldf] (may be NULL; then params may be
  * NULL too); params: device {lambda_sharp, tau, T}.  HBM-bound: the keys are
- * read once per 8 query rows.  d % 8 == 0 and d <= 12800, keys 16-byte
+ * read once (tensor cores) for B <= 10 when the split query operand fits in
+ * shared memory (3 B rounded up to 16 rows x d bf16, about d <= 5100 at
+ * B <= 5), otherwise once per 8 query rows.  d % 8 == 0 and d <= 12800, keys 16-byte
  * aligned, ldk % 8 == 0.  status (device int32, may be NULL) receives
  * DWA_ERR_DEVICE_CHECK when the params fail the checks of dwa_score_topk_dev
  * (fused is then NaN).
