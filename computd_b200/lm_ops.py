@@ -21,8 +21,8 @@ def rope_qk(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, n_heads: in
     every step rounded to bf16 as the elementwise bf16 tensor ops round it; both
     are (1, 2)-transposed views of token-major [B, S, H, dh] buffers, the layout
     attention then also writes its output in."""
-    if qkv.dtype != torch.bfloat16 or qkv.dim() != 3:
-        raise ValueError("qkv must be a bf16 [B, S, W] tensor")
+    if qkv.dtype != torch.bfloat16 or qkv.dim() != 3 or not qkv.is_cuda:
+        raise ValueError("qkv must be a bf16 [B, S, W] CUDA tensor")
     B, S, W = qkv.shape
     H, dh = int(n_heads), int(head_dim)
     if qkv.stride(2) != 1 or (B > 1 and qkv.stride(0) != S * qkv.stride(1)):
@@ -56,8 +56,8 @@ def aspect_queries(q_raw: torch.Tensor, S: int, d_k: int, aspect_logits: torch.T
     Returns (queries, w f32 [S], params f32 [3] = {lambda_sharp, w . tau_param or 0, T},
     the device scalars of the fused score); ``params_out`` receives the params when
     given.  One kernel, nothing read back to the host."""
-    if q_raw.dtype != torch.bfloat16 or q_raw.dim() != 2 or q_raw.stride(1) != 1:
-        raise ValueError("q_raw must be a bf16 [M, S d_k] tensor with contiguous rows")
+    if q_raw.dtype != torch.bfloat16 or q_raw.dim() != 2 or q_raw.stride(1) != 1 or not q_raw.is_cuda:
+        raise ValueError("q_raw must be a bf16 [M, S d_k] CUDA tensor with contiguous rows")
     S, d_k = int(S), int(d_k)
     M = q_raw.shape[0]
     if q_raw.shape[1] < S * d_k:
