@@ -234,6 +234,8 @@ def merge_topk(cand_vals: torch.Tensor, cand_idx: torch.Tensor, k_max: int | Non
         raise ValueError("candidate lists must both be [P, M, k]")
     if cand_vals.dtype != torch.float32 or cand_idx.dtype != torch.int32:
         raise ValueError("candidate lists must be float32 scores and int32 indices")
+    if cand_vals.device.type != "cuda" or cand_idx.device != cand_vals.device:
+        raise ValueError("candidate lists must live on one CUDA device")
     P, M, k = cand_vals.shape
     if k_max is not None and int(k_max) != k:
         raise ValueError("k_max must equal the candidate list length")

@@ -26,3 +26,10 @@ def test_aspect_queries_rejects_bad_inputs():
     with pytest.raises(ValueError):       # strided columns
         aspect_queries(torch.zeros((256, 8), dtype=torch.bfloat16).t(), 4, 64, logits, None,
                        1.0, 1.0, False)
+
+
+def test_merge_topk_rejects_host_lists():
+    from computd_b200.tiled_topk import merge_topk
+
+    with pytest.raises(ValueError):
+        merge_topk(torch.zeros((2, 4, 8)), torch.zeros((2, 4, 8), dtype=torch.int32))
