@@ -1,5 +1,6 @@
-"""CPU: the LM block kernels' Python wrappers reject what their kernels cannot
-take before anything reaches the library (no GPU is touched)."""
+"""CPU: Python wrappers (the LM block kernels, the shard merge) reject what
+their kernels cannot take before anything reaches the library (no GPU is
+touched)."""
 import pytest
 import torch
 
