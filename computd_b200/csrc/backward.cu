@@ -424,7 +424,9 @@ struct RowGradArgs {
 };
 
 template <bool OUT_BF16>
-__global__ void __launch_bounds__(kWarps * 32) row_gradient_kernel(const RowGradArgs g) {
+// Six blocks per SM (40 registers, no spills): most rows have no or one entry,
+// so a row is a short chain of dependent loads and more rows in flight pay.
+__global__ void __launch_bounds__(kWarps * 32, 6) row_gradient_kernel(const RowGradArgs g) {
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r = static_cast<int64_t>(blockIdx.x) * kWarps + w;
   if (r >= g.n_rows) return;
